@@ -1,0 +1,11 @@
+"""q4k -- host side of the B200 Q4_K matmul path (libq4k.so).
+
+Operators mirror the reference's matmul-path pipelines (src/engine.ts,
+shaders/matmul_quant*.wgsl, logit_softcap, argmax, topk256, gelu_mul); the
+compute runs in libq4k.so's sm_100a kernels, loaded through ctypes.
+"""
+from ._lib import Q4KError, lib  # noqa: F401
+from .ops import Context, Selection, context, sample_topk256  # noqa: F401
+from . import synth  # noqa: F401
+
+__all__ = ["Context", "Selection", "context", "sample_topk256", "synth", "Q4KError", "lib"]

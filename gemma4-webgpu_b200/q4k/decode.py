@@ -1,0 +1,203 @@
+"""The matmul call sites of one synthetic Gemma-4-E2B-shaped decode step.
+
+Mirrors the per-token matmul dispatch list of encodeTransformerPass
+(src/engine.ts:1539-1619) and the LM head of sampleNextTokenSubmit
+(src/engine.ts:1686-1741), at the shapes of the benchmark's config 3:
+35 layers x {q 2048x1536, k 256x1536, v 256x1536, o 1536x2048,
+gate 6144x1536, up 6144x1536, down 1536x6144} + the 262144x1536 LM head,
+all Q4_K from the seeded synthetic generator.
+
+Only the matmul path is in scope, so the non-matmul passes between the
+GEMVs (norms, RoPE, attention, residual adds) are not run.  Each layer
+therefore reads fixed seeded activations: q/k/v/gate/up and the LM head
+read x_h [batch, 1536], o reads x_attn [batch, 2048]; down reads
+gelu_mul(gate, up) of the same layer, as in the reference
+(src/engine.ts:1589-1605).  Layers do not feed one another.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import synth
+from .ops import Context, Selection
+
+CONFIG = 3  # seeds: synth.seed_for(3, matrix_id)
+
+
+@dataclass
+class E2BShape:
+    layers: int = 35
+    hidden: int = 1536
+    q: int = 2048  # 8 heads x 256
+    kv: int = 256  # 1 KV head x 256
+    ffn: int = 6144
+    vocab: int = 262144
+    softcap: float = 30.0
+
+
+LAYER_MATS = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+def layer_shapes(s: E2BShape) -> dict[str, tuple[int, int]]:
+    """(rows M, cols N) of each per-layer matrix."""
+    return {
+        "q": (s.q, s.hidden),
+        "k": (s.kv, s.hidden),
+        "v": (s.kv, s.hidden),
+        "o": (s.hidden, s.q),
+        "gate": (s.ffn, s.hidden),
+        "up": (s.ffn, s.hidden),
+        "down": (s.hidden, s.ffn),
+    }
+
+
+def matrix_seed(layer: int, name: str) -> int:
+    return synth.seed_for(CONFIG, 8 * layer + LAYER_MATS.index(name))
+
+
+LMHEAD_SEED = synth.seed_for(CONFIG, 999)
+
+
+@dataclass
+class DecodeStep:
+    """Device-resident weights, activations and outputs of the synthetic step."""
+
+    ctx: Context
+    shape: E2BShape = field(default_factory=E2BShape)
+    batch: int = 1
+    weights: dict = field(default_factory=dict)  # (layer, name) -> uint8 tensor
+    lm_head: torch.Tensor | None = None
+
+    def __post_init__(self):
+        dev = self.ctx.device
+        s, B = self.shape, self.batch
+        shapes = layer_shapes(s)
+        for layer in range(s.layers):
+            for name in LAYER_MATS:
+                M, N = shapes[name]
+                w = synth.q4k_matrix(M, N, matrix_seed(layer, name))
+                self.weights[(layer, name)] = torch.from_numpy(w).to(dev)
+        self.lm_head = torch.from_numpy(synth.q4k_matrix(s.vocab, s.hidden, LMHEAD_SEED)).to(dev)
+        self.x_h = torch.from_numpy(synth.activations(B, s.hidden, synth.seed_for(CONFIG, 100))).to(dev)
+        self.x_attn = torch.from_numpy(synth.activations(B, s.q, synth.seed_for(CONFIG, 101))).to(dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.out = {name: torch.empty((B, shapes[name][0]), **f32) for name in LAYER_MATS}
+        self.act = torch.empty((B, s.ffn), **f32)
+        if B == 1:
+            self.sel = Selection(
+                cand_val=torch.empty(256, **f32),
+                cand_idx=torch.empty(256, dtype=torch.int32, device=dev),
+                argmax=torch.empty(1, dtype=torch.int32, device=dev),
+                logits=None,
+            )
+        else:
+            self.logits = torch.empty((B, s.vocab), **f32)
+            self.topk = torch.empty((B, 512), **f32)
+            self.argmax = torch.empty((B,), dtype=torch.int32, device=dev)
+
+    # ---- accounting ---------------------------------------------------------
+
+    def weight_bytes(self) -> int:
+        s = self.shape
+        per_layer = sum(synth.q4k_bytes(M, N) for M, N in layer_shapes(s).values())
+        return s.layers * per_layer + synth.q4k_bytes(s.vocab, s.hidden)
+
+    def algorithmic_bytes(self) -> int:
+        """Bytes one step must move at minimum: Q4_K weights, each GEMV's f32
+        input and output, the gelu_mul operands, and the LM head's input plus
+        its 2 KB of candidates (per activation row)."""
+        s, B = self.shape, self.batch
+        total = self.weight_bytes()
+        for M, N in layer_shapes(s).values():
+            total += s.layers * 4 * B * (M + N)
+        total += s.layers * 3 * 4 * B * s.ffn           # gelu_mul: gate, up in; act out
+        total += 4 * B * s.hidden + B * (256 * 8 + 4)   # LM head: x in, candidates + argmax out
+        return total
+
+    def launches_per_step(self) -> int:
+        per_layer = len(LAYER_MATS) + 1  # 7 GEMVs + gelu_mul
+        lm = 1 if self.batch == 1 else 1 + 3 * self.batch
+        return self.shape.layers * per_layer + lm
+
+    # ---- the step -------------------------------------------------------------
+
+    def run(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Record one decode step's matmul path on `stream` (reference order)."""
+        c, s, B = self.ctx, self.shape, self.batch
+        shapes = layer_shapes(s)
+        for layer in range(s.layers):
+            W = self.weights
+            for name in ("q", "k", "v"):
+                M, N = shapes[name]
+                c.gemv(W[(layer, name)], self.x_h, M, N, out=self.out[name], stream=stream)
+            M, N = shapes["o"]
+            c.gemv(W[(layer, "o")], self.x_attn, M, N, out=self.out["o"], stream=stream)
+            for name in ("gate", "up"):
+                M, N = shapes[name]
+                c.gemv(W[(layer, name)], self.x_h, M, N, out=self.out[name], stream=stream)
+            c.gelu_mul(self.out["gate"], self.out["up"], out=self.act, stream=stream)
+            M, N = shapes["down"]
+            c.gemv(W[(layer, "down")], self.act, M, N, out=self.out["down"], stream=stream)
+        if B == 1:
+            c.lmhead_select(self.lm_head, self.x_h, s.vocab, s.hidden, s.softcap, out=self.sel, stream=stream)
+        else:
+            c.gemv(self.lm_head, self.x_h, s.vocab, s.hidden, out=self.logits, stream=stream)
+            for b in range(B):
+                c.logit_softcap(self.logits[b], s.softcap, stream=stream)
+                c.topk256(self.logits[b], out=self.topk[b], stream=stream)
+                c.argmax(self.logits[b], out=self.argmax[b:b + 1], stream=stream)
+
+    def run_layer_gemvs(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Only the 7 GEMV launches of every layer (no gelu_mul, no LM head):
+        used to time the GEMV kernel on its own."""
+        c, s = self.ctx, self.shape
+        shapes = layer_shapes(s)
+        for layer in range(s.layers):
+            for name in LAYER_MATS:
+                M, N = shapes[name]
+                x = self.x_attn if name == "o" else (self.act if name == "down" else self.x_h)
+                c.gemv(self.weights[(layer, name)], x, M, N, out=self.out[name], stream=stream)
+
+    def layer_gemv_bytes(self) -> int:
+        s, B = self.shape, self.batch
+        return sum(s.layers * (synth.q4k_bytes(M, N) + 4 * B * (M + N)) for M, N in layer_shapes(s).values())
+
+    def result_tensors(self) -> list[torch.Tensor]:
+        """What a decode step hands back to the host: the sampled token and the
+        2 KB topk256 candidates (src/engine.ts:1731-1741)."""
+        if self.batch == 1:
+            return [self.sel.argmax, self.sel.cand_val, self.sel.cand_idx]
+        return [self.argmax, self.topk]
+
+    def sample_matrices(self, layers: int = 1) -> list[tuple[np.ndarray, int, int]]:
+        """Host copies (regenerated from the same seeds) of the first `layers`
+        layers' matrices, for CPU timing samples."""
+        out = []
+        for layer in range(layers):
+            for name, (M, N) in layer_shapes(self.shape).items():
+                out.append((synth.q4k_matrix(M, N, matrix_seed(layer, name)), M, N))
+        return out
+
+
+class StepGraph:
+    """A decode step captured once as a CUDA graph and replayed per token (the
+    way the engine pre-builds its bind groups and only re-dispatches).  The
+    capture records the same libq4k launches as DecodeStep.run."""
+
+    def __init__(self, step: DecodeStep, stream: torch.cuda.Stream | None = None, body=None):
+        self.step = step
+        self.stream = stream or torch.cuda.Stream(device=step.ctx.device)
+        body = body or step.run
+        with torch.cuda.stream(self.stream):
+            body(self.stream)  # warm-up outside capture
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            body(self.stream)
+
+    def replay(self) -> None:
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()

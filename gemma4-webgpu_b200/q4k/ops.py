@@ -1,0 +1,271 @@
+"""Host-side mirror of the reference's matmul-path operators on torch tensors.
+
+Each method wraps one libq4k.so entry point and keeps the name, argument
+meaning and error behaviour of the WebGPU pipeline it replaces in
+src/engine.ts (matmulQuant, matmulQuantMR4, logitSoftcap, argmax, topk256,
+geluMul and the lmHead sequence of sampleNextTokenSubmit).  PyTorch is only
+the plumbing here: device memory, streams and tensors.  Every call launches
+CUDA kernels of libq4k.so; there is no CPU or PyTorch fallback, and a failed
+call raises Q4KError.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import random
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import Q4KError
+
+QK_K = 256
+BLOCK_BYTES = 144
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream: torch.cuda.Stream | None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str, device: torch.device) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} has dtype {t.dtype}, expected {dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+@dataclass
+class Selection:
+    """Outputs of the fused LM head (one shard or the whole vocabulary)."""
+
+    cand_val: torch.Tensor  # f32 [256]: per-residue max (topk256 values)
+    cand_idx: torch.Tensor  # u32-as-int32 [256]: their global indices
+    argmax: torch.Tensor  # int32 [1]
+    logits: torch.Tensor | None  # f32 [V] softcapped logits, when requested
+
+    def topk256_buffer(self) -> torch.Tensor:
+        """The reference's topk256Result layout: f32[512] of (val, bitcast idx)
+        pairs (shaders/topk256.wgsl:19-20)."""
+        out = torch.empty(512, dtype=torch.float32, device=self.cand_val.device)
+        out[0::2] = self.cand_val
+        out[1::2] = self.cand_idx.view(torch.float32)
+        return out
+
+
+class Context:
+    """A libq4k context on one CUDA device (q4k_create / q4k_destroy)."""
+
+    def __init__(self, device: int | torch.device = 0):
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("libq4k runs on CUDA devices only")
+        self.device = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+        self._L = _lib.lib()
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            rc = self._L.q4k_create(self.device.index, ctypes.byref(handle))
+        if rc != _lib.Q4K_OK:
+            raise Q4KError(rc, f"q4k_create(device={self.device.index}) failed")
+        self._h = handle.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.q4k_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int) -> None:
+        _lib.check(rc, self._h)
+
+    # ---- matmulQuant / matmulQuantMR4 -----------------------------------
+
+    def matmul_quant(self, input: torch.Tensor, weight: torch.Tensor, output: torch.Tensor, M: int, N: int,
+                     stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """output[m] = sum_k f32(w16[m, k]) * input[k] -- the matmulQuant
+        pipeline with bind group {input, weight, output, {M, N}}
+        (shaders/matmul_quant.wgsl:12-16, src/engine.ts:332-341).  `weight`
+        holds Q4_K bytes (uint8, M*N/256*144)."""
+        _need(input, torch.float32, "input", self.device)
+        _need(weight, torch.uint8, "weight", self.device)
+        _need(output, torch.float32, "output", self.device)
+        if input.numel() < N or output.numel() < M or weight.numel() < M * (N // QK_K) * BLOCK_BYTES:
+            raise ValueError("buffer smaller than {M, N} requires")
+        self._check(self._L.q4k_matmul_quant(self._h, _ptr(input), _ptr(weight), _ptr(output), M, N,
+                                             _stream(stream)))
+        return output
+
+    def gemv(self, weight: torch.Tensor, x: torch.Tensor, M: int, N: int, out: torch.Tensor | None = None,
+             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """y[b, m] for x [batch, N] (or [N]); one weight stream per call."""
+        _need(weight, torch.uint8, "weight", self.device)
+        _need(x, torch.float32, "x", self.device)
+        if x.numel() % N:
+            raise ValueError(f"x has {x.numel()} elements, not a multiple of N={N}")
+        batch = x.numel() // N
+        if weight.numel() < M * (N // QK_K) * BLOCK_BYTES:
+            raise ValueError("weight buffer smaller than M*N/256*144 bytes")
+        if out is None:
+            out = torch.empty((batch, M), dtype=torch.float32, device=self.device)
+        _need(out, torch.float32, "out", self.device)
+        if out.numel() < batch * M:
+            raise ValueError("out smaller than batch*M")
+        self._check(self._L.q4k_gemv(self._h, _ptr(weight), _ptr(x), _ptr(out), M, N, batch, _stream(stream)))
+        return out
+
+    def dequant_f16(self, weight: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """The f16 weights the reference uploads (as int16 bit patterns)."""
+        _need(weight, torch.uint8, "weight", self.device)
+        if weight.numel() % BLOCK_BYTES:
+            raise ValueError("weight size is not a whole number of 144-byte super-blocks")
+        nb = weight.numel() // BLOCK_BYTES
+        out = torch.empty(nb * QK_K, dtype=torch.int16, device=self.device)
+        self._check(self._L.q4k_dequant_f16(self._h, _ptr(weight), _ptr(out), nb, _stream(stream)))
+        return out
+
+    # ---- LM-head consumers ------------------------------------------------
+
+    def logit_softcap(self, logits: torch.Tensor, cap: float = 30.0,
+                      stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """In place, shaders/logit_softcap.wgsl:9-16."""
+        _need(logits, torch.float32, "logits", self.device)
+        self._check(self._L.q4k_logit_softcap(self._h, _ptr(logits), logits.numel(), cap, _stream(stream)))
+        return logits
+
+    def argmax(self, logits: torch.Tensor, out: torch.Tensor | None = None,
+               stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """int32 [1], shaders/argmax.wgsl:7-34 tie rule."""
+        _need(logits, torch.float32, "logits", self.device)
+        out = torch.empty(1, dtype=torch.int32, device=self.device) if out is None else out
+        self._check(self._L.q4k_argmax(self._h, _ptr(logits), logits.numel(), _ptr(out), _stream(stream)))
+        return out
+
+    def topk256(self, logits: torch.Tensor, out: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """f32 [512] (val, bitcast idx) pairs, shaders/topk256.wgsl:5-21."""
+        _need(logits, torch.float32, "logits", self.device)
+        out = torch.empty(512, dtype=torch.float32, device=self.device) if out is None else out
+        self._check(self._L.q4k_topk256(self._h, _ptr(logits), logits.numel(), _ptr(out), _stream(stream)))
+        return out
+
+    def gelu_mul(self, gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None,
+                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """GELU_tanh(gate) * up, shaders/gelu_mul.wgsl."""
+        _need(gate, torch.float32, "gate", self.device)
+        _need(up, torch.float32, "up", self.device)
+        if gate.numel() != up.numel():
+            raise ValueError("gate and up differ in size")
+        out = torch.empty_like(gate) if out is None else out
+        self._check(self._L.q4k_gelu_mul(self._h, _ptr(gate), _ptr(up), _ptr(out), gate.numel(), _stream(stream)))
+        return out
+
+    def lmhead_select(self, weight: torch.Tensor, x: torch.Tensor, V: int, N: int, cap: float = 30.0,
+                      row_offset: int = 0, return_logits: bool = False,
+                      out: Selection | None = None, stream: torch.cuda.Stream | None = None) -> Selection:
+        """lmHead matmul + logitSoftcap + argmax/topk256 in one launch
+        (src/engine.ts:1686-1741) over vocabulary rows [row_offset, row_offset+V)."""
+        _need(weight, torch.uint8, "weight", self.device)
+        _need(x, torch.float32, "x", self.device)
+        if x.numel() != N:
+            raise ValueError(f"x has {x.numel()} elements, expected N={N}")
+        if weight.numel() < V * (N // QK_K) * BLOCK_BYTES:
+            raise ValueError("weight buffer smaller than V*N/256*144 bytes")
+        if out is None:
+            out = Selection(
+                cand_val=torch.empty(256, dtype=torch.float32, device=self.device),
+                cand_idx=torch.empty(256, dtype=torch.int32, device=self.device),
+                argmax=torch.empty(1, dtype=torch.int32, device=self.device),
+                logits=torch.empty(V, dtype=torch.float32, device=self.device) if return_logits else None,
+            )
+        self._check(self._L.q4k_lmhead_select(
+            self._h, _ptr(weight), _ptr(x), V, N, cap, row_offset, _ptr(out.logits), _ptr(out.cand_val),
+            _ptr(out.cand_idx), _ptr(out.argmax), _stream(stream)))
+        return out
+
+    def merge_candidates(self, vals: torch.Tensor, idx: torch.Tensor, out: Selection | None = None,
+                         stream: torch.cuda.Stream | None = None) -> Selection:
+        """[G, 256] gathered shard candidates -> one Selection (no logits)."""
+        _need(vals, torch.float32, "vals", self.device)
+        _need(idx, torch.int32, "idx", self.device)
+        G = vals.numel() // 256
+        if vals.numel() != G * 256 or idx.numel() != G * 256:
+            raise ValueError("vals/idx must hold G*256 entries")
+        if out is None:
+            out = Selection(
+                cand_val=torch.empty(256, dtype=torch.float32, device=self.device),
+                cand_idx=torch.empty(256, dtype=torch.int32, device=self.device),
+                argmax=torch.empty(1, dtype=torch.int32, device=self.device),
+                logits=None,
+            )
+        self._check(self._L.q4k_merge_candidates(self._h, _ptr(vals), _ptr(idx), G, _ptr(out.cand_val),
+                                                 _ptr(out.cand_idx), _ptr(out.argmax), _stream(stream)))
+        return out
+
+
+_contexts: dict[int, Context] = {}
+
+
+def context(device: int | None = None) -> Context:
+    """The cached per-device Context (created on first use)."""
+    if device is None:
+        device = torch.cuda.current_device()
+    if device not in _contexts:
+        _contexts[device] = Context(device)
+    return _contexts[device]
+
+
+# ---- host-side consumer of topk256 (CPU, as in the reference) ---------------
+
+def sample_topk256(result512, temperature: float = 0.0, top_p: float = 1.0, rep_penalty: float = 1.0,
+                   all_tokens=(), rng: random.Random | None = None) -> int:
+    """Pick the next token from the topk256 buffer the way
+    sampleNextTokenSubmit's readback does (src/engine.ts:1792-1837):
+    repetition penalty on seen ids, a stable descending sort by value, then
+    greedy (temperature 0) or temperature + top-p sampling over the 256."""
+    import numpy as np
+
+    buf = np.asarray(result512, dtype=np.float32).reshape(-1)
+    vals = buf[0::2].astype(np.float64)
+    ids = buf[1::2].view(np.uint32).astype(np.int64)
+    cands = [[float(vals[i]), int(ids[i])] for i in range(256)]
+    if rep_penalty > 1.0 and len(all_tokens) > 0:
+        seen = set(all_tokens)
+        for c in cands:
+            if c[1] in seen:
+                c[0] = c[0] / rep_penalty if c[0] > 0 else c[0] * rep_penalty
+    cands.sort(key=lambda c: -c[0])  # Array.prototype.sort is stable, as is list.sort
+    if temperature == 0:
+        return cands[0][1]
+    rng = rng or random.Random()
+    max_logit = cands[0][0]
+    probs = [math.exp((c[0] - max_logit) / temperature) for c in cands]
+    s = sum(probs)
+    cum, cutoff = 0.0, 256
+    for i, p in enumerate(probs):
+        cum += p / s
+        if cum >= top_p:
+            cutoff = i + 1
+            break
+    subset = sum(probs[:cutoff])
+    r = rng.random() * subset
+    picked = cands[cutoff - 1][1]
+    for i in range(cutoff):
+        r -= probs[i]
+        if r <= 0:
+            picked = cands[i][1]
+            break
+    return picked

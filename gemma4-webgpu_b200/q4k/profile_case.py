@@ -1,0 +1,51 @@
+"""Small, self-contained launches of one libq4k kernel, for profiler captures.
+
+    python gemma4-webgpu_b200/q4k/profile_case.py gemv [--batch B] [--reps R]
+    python gemma4-webgpu_b200/q4k/profile_case.py lmhead [--reps R]
+
+`gemv` rotates over 35 distinct 6144x1536 Q4_K matrices (186 MB, more than
+the 126 MB L2, so each launch reads its weights from HBM); `lmhead` runs the
+fused 262144-row LM head (226 MB).  A few hundred MB of device memory at
+most; the process exits after `reps` launches.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+import torch  # noqa: E402
+
+from q4k import Context, synth  # noqa: E402
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["gemv", "lmhead"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--reps", type=int, default=40)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    ctx = Context(0)
+    if a.kernel == "gemv":
+        M, N = 6144, 1536
+        ws = [torch.from_numpy(synth.q4k_matrix(M, N, synth.seed_for(3, 8 * i + 4))).to(dev) for i in range(35)]
+        x = torch.from_numpy(synth.activations(a.batch, N, 1)).to(dev)
+        y = torch.empty((a.batch, M), dtype=torch.float32, device=dev)
+        for r in range(a.reps):
+            ctx.gemv(ws[r % len(ws)], x, M, N, out=y)
+    else:
+        V, N = 262144, 1536
+        w = torch.from_numpy(synth.q4k_matrix(V, N, synth.seed_for(3, 999))).to(dev)
+        x = torch.from_numpy(synth.activations(1, N, 1)).to(dev)
+        for _ in range(a.reps):
+            ctx.lmhead_select(w, x[0], V, N, 30.0)
+    torch.cuda.synchronize()
+    ctx.close()
+    print("done")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+/*
+ * q4k.h -- C ABI of libq4k.so, the B200 (sm_100a) Q4_K matmul path of
+ * gemma4-webgpu (tylerstraub/gemma4-webgpu).
+ *
+ * Every entry point is a drop-in for one WebGPU pipeline dispatch that
+ * src/engine.ts records on the decode hot path; the comment of each names the
+ * reference interface it replaces.  Conventions shared by all calls:
+ *
+ *   - All array arguments are DEVICE pointers owned by the caller.  The
+ *     library never allocates per call (the context allocates its small
+ *     scratch once, in q4k_create).  Outputs are overwritten.
+ *   - Weights are GGUF Q4_K bytes exactly as the file stores them: rows of
+ *     N/256 super-blocks of 144 bytes (f16 d, f16 dmin, 12 bytes of packed
+ *     6-bit scales/mins, 128 bytes of nibbles; src/gguf.ts:157-210), row-major
+ *     (ne0 = N fastest, src/gguf.ts:89-97).  N must be a multiple of 256.
+ *   - The weight each output sees is the reference's: the Q4_K value rounded
+ *     once to f32 and then to f16 (round to nearest even), multiplied in f32
+ *     (src/gguf.ts:168-210 + 425-473, shaders/matmul_quant.wgsl:35).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *     asynchronous on that stream; none synchronizes the host, none allocates,
+ *     so they can be captured in a CUDA graph.
+ *   - Pointers must be 16-byte aligned (weights, activations, outputs).
+ *   - Return value: Q4K_OK (0) or a negative Q4K_ERR_* code; the reason is in
+ *     q4k_last_error(ctx).  Launch errors are reported at the call; faults
+ *     inside a kernel surface at the caller's next synchronization, as CUDA
+ *     errors do.  Nothing throws across the ABI.
+ *   - A context belongs to one device and one host thread; calls on one
+ *     context must be ordered on one stream (the fused LM head shares the
+ *     context's selection scratch between calls).
+ */
+#ifndef Q4K_H_
+#define Q4K_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define Q4K_API __attribute__((visibility("default")))
+#else
+#define Q4K_API
+#endif
+
+#define Q4K_OK 0
+#define Q4K_ERR_INVALID_ARG (-1) /* shape, alignment or null pointer rejected */
+#define Q4K_ERR_CUDA (-2)        /* CUDA runtime error (launch, device) */
+#define Q4K_ERR_UNSUPPORTED (-3) /* valid request this build cannot serve */
+
+#define Q4K_QK 256          /* weights per Q4_K super-block */
+#define Q4K_BLOCK_BYTES 144 /* bytes per Q4_K super-block */
+
+typedef struct q4k_ctx q4k_ctx;
+
+/* ABI version (major * 100 + minor). */
+Q4K_API int q4k_version(void);
+
+/* Create a context on `device` (makes it current on the calling thread) and
+ * allocate its scratch.  Replaces the engine's device/pipeline set-up for this
+ * path: initWebGPU + createPipelines (src/engine.ts:354-430). */
+Q4K_API int q4k_create(int device, q4k_ctx** out);
+
+/* Free the context and its scratch.  NULL is ignored. */
+Q4K_API void q4k_destroy(q4k_ctx* ctx);
+
+/* Message of the last failed call on `ctx` ("" if none); never NULL. */
+Q4K_API const char* q4k_last_error(const q4k_ctx* ctx);
+
+/* matmul_quant: output[m] = sum_k f32(w[m,k]) * input[k], m < M.
+ * Argument order and meaning follow the pipeline's bind group 0
+ * {0: input f32[N], 1: weight, 2: output f32[M], 3: {M, N}}
+ * (shaders/matmul_quant.wgsl:12-16, shaders/matmul_quant_mr4.wgsl:73-76,
+ * dispatched by dispatchMatmul, src/engine.ts:332-341); the weight binding
+ * holds Q4_K bytes instead of the pre-dequantized f16 buffer. */
+Q4K_API int q4k_matmul_quant(q4k_ctx* ctx, const float* input, const void* weight, float* output, uint32_t M, uint32_t N,
+                     void* stream);
+
+/* Batched form: y[b*M + m] = sum_k f32(w[m,k]) * x[b*N + k] for b < batch.
+ * One weight stream serves all `batch` activation rows (the MR4 pipeline's
+ * shared input read, shaders/matmul_quant_mr4.wgsl:107-115, turned around:
+ * several inputs share one weight read).  batch >= 1. */
+Q4K_API int q4k_gemv(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t batch,
+             void* stream);
+
+/* The f16 weights the reference uploads for a Q4_K tensor (its
+ * dequantizeQ4_K + f32ToF16Array + createF16Buffer, src/gguf.ts:168-210,
+ * 425-473, src/engine.ts:553-578, 828-841): n_blocks super-blocks ->
+ * n_blocks*256 f16 bit patterns.  The weight-probe comparison
+ * (src/diagnostics/weight-probe.ts:60-162) reads these. */
+Q4K_API int q4k_dequant_f16(q4k_ctx* ctx, const void* w, uint16_t* out, uint64_t n_blocks, void* stream);
+
+/* logit_softcap in place: logits[i] = tanh(clamp(logits[i]/cap, -15, 15))*cap
+ * (shaders/logit_softcap.wgsl:9-16; cap from src/engine.ts:447). */
+Q4K_API int q4k_logit_softcap(q4k_ctx* ctx, float* logits, uint32_t n, float cap, void* stream);
+
+/* argmax: *result = index of the maximum with the reference's tie rule
+ * (shaders/argmax.wgsl:7-34; result buffer src/engine.ts:1037). */
+Q4K_API int q4k_argmax(q4k_ctx* ctx, const float* logits, uint32_t n, uint32_t* result, void* stream);
+
+/* topk256: result f32[512] = 256 (max, bitcast<f32>(index)) pairs, pair t
+ * being the first strict maximum over indices = t (mod 256)
+ * (shaders/topk256.wgsl:5-21; buffer src/engine.ts:1042). */
+Q4K_API int q4k_topk256(q4k_ctx* ctx, const float* logits, uint32_t n, float* result, void* stream);
+
+/* gelu_mul: out[i] = GELU_tanh(gate[i]) * up[i] (shaders/gelu_mul.wgsl:1-17). */
+Q4K_API int q4k_gelu_mul(q4k_ctx* ctx, const float* gate, const float* up, float* out, uint32_t n, void* stream);
+
+/* Fused LM head on a vocabulary shard: the lmHead matmul + logitSoftcap +
+ * argmax/topk256 passes of sampleNextTokenSubmit (src/engine.ts:1686-1741)
+ * in one launch.  Rows [0, V) of `w` are global vocabulary indices
+ * row_offset + i (row_offset = 0 for an unsharded head).  cap <= 0 skips
+ * the softcap (src/engine.ts:1695).  Outputs: cand_val/cand_idx [256] =
+ * the topk256 pairs of this shard in global indices, *argmax = the argmax of
+ * this shard, logits [V] = the softcapped logits (may be NULL: not stored).
+ * row_offset + V must be < 2^31. */
+Q4K_API int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint32_t V, uint32_t N, float cap,
+                      uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx, uint32_t* argmax,
+                      void* stream);
+
+/* Merge G shards' candidate sets (vals/idx [G][256], e.g. after an
+ * all-gather) into the candidates and argmax the unsharded head would give.
+ * No reference counterpart: the reference is single-device. */
+Q4K_API int q4k_merge_candidates(q4k_ctx* ctx, const float* vals, const uint32_t* idx, uint32_t G, float* out_val,
+                         uint32_t* out_idx, uint32_t* argmax, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q4K_H_ */
