@@ -20,14 +20,10 @@ the host cores, on a bounded sample of the same workload per step.
 from __future__ import annotations
 
 import argparse
-import csv
-import io
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -51,52 +47,66 @@ def peaks() -> dict:
 # ---- clocks ---------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    polled from a thread every 5 ms (nvidia-smi as a fallback)."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {  # nvmlClocksEventReason bits
+        0x8: "hw_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x20: "sw_thermal_slowdown",
+        0x4: "sw_power_cap",
+    }
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.proc = None
-        self.file = None
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._error = None
 
     def start(self):
+        import threading
+
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception as e:  # no NVML: report it
+            self._error = f"nvml unavailable: {e}"
+            return
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                    self.samples.append((mhz, reasons))
+                except Exception as e:
+                    self._error = str(e)
+                    return
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.file.flush()
-        text = Path(self.file.name).read_text()
-        os.unlink(self.file.name)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for row in csv.reader(io.StringIO(text)):
-            if len(row) < 9:
-                continue
-            try:
-                sm.append(float(row[1]))
-                mx = float(row[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, row[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [self._error or "no samples"],
+                    "samples": 0}
+        seen = set()
+        for _, r in self.samples:
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    seen.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(seen), "samples": len(self.samples)}
 
 
 # ---- distributed plumbing ----------------------------------------------------------
@@ -190,7 +200,6 @@ def run_ours(args) -> None:
     barrier(world)
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     barrier(world)
@@ -207,36 +216,34 @@ def run_ours(args) -> None:
     value = world * bytes_step * args.steps / (ms / 1e3) / 1e9
     tokens_per_s = world * args.batch * args.steps / (ms / 1e3)
 
-    # dominant kernel: the GEMV, timed alone over all layers' launches (graph
-    # replays of only the 245 layer GEMVs; includes the graph's launch gaps)
-    gemv_graph = StepGraph(step, body=step.run_layer_gemvs)
-    for _ in range(3):
-        gemv_graph.replay()
-    torch.cuda.synchronize()
-    reps = max(3, args.steps)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(gemv_graph.stream)
-    for _ in range(reps):
-        gemv_graph.replay()
-    b.record(gemv_graph.stream)
-    torch.cuda.synchronize()
-    gemv_ms = a.elapsed_time(b) / reps
-    gemv_launches = step.shape.layers * 7
-    gemv_bytes = step.layer_gemv_bytes()
-    gemv_gbs = gemv_bytes / (gemv_ms / 1e3) / 1e9
+    def time_body(body, reps):
+        g = StepGraph(step, body=body)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(g.stream)
+        for _ in range(reps):
+            g.replay()
+        b.record(g.stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps, g
 
-    # LM head kernel alone (one launch, 226 MB)
+    reps = min(max(5, args.steps), 200)
+    # dominant kernel: the engine launch of stage 0 (every GEMV but down, and
+    # the LM head), timed alone with its activation-prep launch in front
+    stage0 = step.plan(stages=(0,))
+    s0_ms, s0_graph = time_body(lambda st: stage0.run(st), reps)
+    s0_bytes = step.stage0_bytes()
+    s0_gbs = s0_bytes / (s0_ms / 1e3) / 1e9
+    # the same step as one libq4k call per reference dispatch (246 launches)
+    serial_ms, serial_graph = time_body(step.run_serial, reps)
+    # the LM head alone
     lm_ms = None
     if args.batch == 1:
-        for _ in range(3):
-            ctx.lmhead_select(step.lm_head, step.x_h, 262144, 1536, 30.0, out=step.sel, stream=s)
-        torch.cuda.synchronize()
-        a.record(s)
-        for _ in range(reps):
-            ctx.lmhead_select(step.lm_head, step.x_h, 262144, 1536, 30.0, out=step.sel, stream=s)
-        b.record(s)
-        torch.cuda.synchronize()
-        lm_ms = a.elapsed_time(b) / reps
+        lm_ms, lm_graph = time_body(
+            lambda st: ctx.lmhead_select(step.lm_head, step.x_h, 262144, 1536, 30.0, out=step.sel, stream=st), reps)
+        del lm_graph
     lm_bytes = 226_492_416 + 4 * 1536 + 2052
 
     # end to end through the public API: pinned host inputs in, results out
@@ -270,21 +277,24 @@ def run_ours(args) -> None:
     pk = peaks()
     traffic = None
     if PROFILE_TRAFFIC.exists():
-        traffic = json.loads(PROFILE_TRAFFIC.read_text()).get("gemv_rowwarp", {}).get("bytes_per_launch")
+        traffic = json.loads(PROFILE_TRAFFIC.read_text()).get("stage0_engine", {}).get("bytes_per_launch")
     roofline = {
-        "kernel": "q4k gemv (layer GEMVs, 245 launches/step)",
+        "kernel": "engine_kernel, plan stage 0 (210 GEMVs + fused LM head in one launch; timed with its prep launch)",
         "bound": "hbm",
-        "achieved": round(gemv_gbs, 1),
+        "achieved": round(s0_gbs, 1),
         "peak": pk["hbm_gbs"],
         "peak_source": pk["source"],
         "unit": "GB/s",
-        "frac": round(gemv_gbs / pk["hbm_gbs"], 4),
+        "frac": round(s0_gbs / pk["hbm_gbs"], 4),
         "traffic": traffic,
-        "algorithmic_bytes_per_launch": round(gemv_bytes / gemv_launches),
-        "avg_launch_us": round(gemv_ms * 1e3 / gemv_launches, 3),
+        "algorithmic_bytes_per_launch": s0_bytes,
+        "avg_launch_us": round(s0_ms * 1e3, 2),
     }
-    kernels = {"gemv_layers": {"ms": round(gemv_ms, 4), "GB/s": round(gemv_gbs, 1),
-                               "frac_of_peak": round(gemv_gbs / pk["hbm_gbs"], 4)}}
+    kernels = {"stage0_engine": {"ms": round(s0_ms, 4), "GB/s": round(s0_gbs, 1),
+                                 "frac_of_peak": round(s0_gbs / pk["hbm_gbs"], 4)},
+               "serial_step": {"ms": round(serial_ms, 4), "launches": step.serial_calls_per_step(),
+                               "GB/s": round(bytes_step / (serial_ms / 1e3) / 1e9, 1),
+                               "tokens_per_s": round(args.batch / (serial_ms / 1e3), 1)}}
     if lm_ms:
         kernels["lmhead_select"] = {"ms": round(lm_ms, 4), "GB/s": round(lm_bytes / (lm_ms / 1e3) / 1e9, 1),
                                     "frac_of_peak": round(lm_bytes / (lm_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
@@ -319,6 +329,8 @@ def run_ours(args) -> None:
             "algorithmic_bytes_per_step": bytes_step,
             "l2": "inputs larger than L2 (923 MB of weights per step vs 126 MB L2)",
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "step": "plan: stage 0 = 210 GEMVs + fused LM head (1 prep + 1 engine launch), "
+                    "stage 1 = 35 x gelu_mul->down (1 prep + 1 engine launch); CUDA graph replay",
         },
         "tokens_per_s": round(tokens_per_s, 1),
         "roofline": roofline,
@@ -331,7 +343,7 @@ def run_ours(args) -> None:
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph, gemv_graph
+    del graph, s0_graph, serial_graph
     ctx.close()
     if world > 1:
         import torch.distributed as dist
@@ -396,8 +408,8 @@ def run_reference(args) -> None:
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--batch", type=int, default=1, help="activation rows per step (config 3: 1 or 4)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -1,57 +1,73 @@
-// extern "C" entry points of libq4k.so (declared in include/q4k.h):
-// argument validation, context and scratch ownership, error reporting.
+// extern "C" entry points of libq4k.so (declared in include/q4k.h): argument
+// validation, context and scratch ownership, error reporting.
 #include <cuda_runtime.h>
-#include <stdarg.h>
 #include <stdint.h>
-#include <stdio.h>
 #include <string.h>
 
-#include "../../include/q4k.h"
-#include "q4k_kernels.cuh"
+#include "q4k_ctx.cuh"
 
-struct q4k_ctx {
-  int device = 0;
-  int sm_count = 0;
-  q4k::SelectScratch select;
-  void* scratch = nullptr;
-  char err[512] = {0};
-};
+using namespace q4k;
 
 namespace {
-
-int fail(q4k_ctx* ctx, int code, const char* fmt, ...) {
-  if (ctx) {
-    va_list ap;
-    va_start(ap, fmt);
-    vsnprintf(ctx->err, sizeof(ctx->err), fmt, ap);
-    va_end(ap);
-  }
-  return code;
-}
-
-int cuda_status(q4k_ctx* ctx, cudaError_t e, const char* what) {
-  if (e == cudaSuccess) {
-    ctx->err[0] = 0;
-    return Q4K_OK;
-  }
-  return fail(ctx, Q4K_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
-}
-
-bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 // Shape and pointer checks shared by the matmul entry points.
 int check_matmul(q4k_ctx* ctx, const void* w, const float* x, const float* y, uint32_t M, uint32_t N,
                  uint32_t batch) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
-  if (!w || !x || !y) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer (w=%p x=%p y=%p)", w, x, (const void*)y);
+  if (!w || !x || !y)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer (w=%p x=%p y=%p)", w, (const void*)x, (const void*)y);
   if (N == 0 || N % Q4K_QK != 0)
-    return fail(ctx, Q4K_ERR_INVALID_ARG, "N=%u is not a positive multiple of %d (Q4_K super-block)", N, Q4K_QK);
-  if (batch == 0) return fail(ctx, Q4K_ERR_INVALID_ARG, "batch must be >= 1");
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "N=%u is not a positive multiple of %d (Q4_K super-block)", N,
+                    Q4K_QK);
+  if (batch == 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "batch must be >= 1");
   if (!aligned16(w) || !aligned16(x) || !aligned16(y))
-    return fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned (w=%p x=%p y=%p)", w, x,
-                (const void*)y);
-  if ((uint64_t)M * batch > 0xffffffffull)
-    return fail(ctx, Q4K_ERR_INVALID_ARG, "M*batch=%llu exceeds 2^32-1", (unsigned long long)M * batch);
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned (w=%p x=%p y=%p)", w,
+                    (const void*)x, (const void*)y);
+  if ((uint64_t)M * batch > 0xffffffffull || (uint64_t)N * batch > 0xffffffffull)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "M*batch or N*batch exceeds 2^32-1");
+  return Q4K_OK;
+}
+
+// The engine path for batch <= 16 when the prepared activation fits the
+// context scratch; otherwise the scratch-free warp-per-row kernel.
+int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t batch,
+             cudaStream_t s) {
+  uint32_t done = 0;
+  while (done < batch) {
+    const uint32_t b = (batch - done) > (uint32_t)kMaxTokens ? (uint32_t)kMaxTokens : (batch - done);
+    const float* xc = x + (uint64_t)done * N;
+    float* yc = y + (uint64_t)done * M;
+    if (xfrag_bytes(N, b) <= ctx->xfrag_cap) {
+      JobList jl{};
+      jl.n = 1;
+      jl.inl.x = xc;
+      jl.inl.xfrag = ctx->xfrag;
+      jl.inl.inv_scale = ctx->inv_scale;
+      jl.inl.N = N;
+      jl.inl.mode = 0;
+      cudaError_t e = launch_xprep(jl, b, s);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv activation prep launch");
+      TaskList tl{};
+      tl.n = 1;
+      tl.inl.w = w;
+      tl.inl.xfrag = ctx->xfrag;
+      tl.inl.inv_scale = ctx->inv_scale;
+      tl.inl.y = yc;
+      tl.inl.M = M;
+      tl.inl.N = N;
+      tl.inl.item_begin = 0;
+      tl.inl.item_end = tiles_of(M);
+      tl.inl.kind = kTaskPlain;
+      tl.total_items = tiles_of(M);
+      e = launch_engine(tl, b, false, ctx->select, ctx->sm_count, s);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv engine launch");
+    } else {
+      cudaError_t e = launch_gemv(w, xc, yc, M, N, b, N, M, 0, s);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv launch");
+    }
+    done += b;
+  }
+  ctx->err[0] = 0;
   return Q4K_OK;
 }
 
@@ -74,13 +90,20 @@ int q4k_create(int device, q4k_ctx** out) {
   q4k_ctx* ctx = new q4k_ctx();
   ctx->device = device;
   ctx->sm_count = prop.multiProcessorCount;
-  if (cudaMalloc(&ctx->scratch, q4k::kSelectScratchBytes) != cudaSuccess) {
+  const size_t sel_bytes = 256 * sizeof(unsigned long long) + 256;
+  const size_t scale_bytes = 256;
+  const size_t total = sel_bytes + scale_bytes + kCtxXfragBytes;
+  if (cudaMalloc(&ctx->scratch, total) != cudaSuccess) {
     delete ctx;
     return Q4K_ERR_CUDA;
   }
-  ctx->select.slots = static_cast<unsigned long long*>(ctx->scratch);
-  ctx->select.counter = reinterpret_cast<uint32_t*>(static_cast<char*>(ctx->scratch) + 256 * 8);
-  if (q4k::init_select_scratch(ctx->select, nullptr) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+  char* base = static_cast<char*>(ctx->scratch);
+  ctx->select.slots = reinterpret_cast<unsigned long long*>(base);
+  ctx->select.counter = reinterpret_cast<uint32_t*>(base + 256 * 8);
+  ctx->inv_scale = reinterpret_cast<float*>(base + sel_bytes);
+  ctx->xfrag = reinterpret_cast<uint2*>(base + sel_bytes + scale_bytes);
+  ctx->xfrag_cap = kCtxXfragBytes;
+  if (init_select_scratch(ctx->select, nullptr) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(ctx->scratch);
     delete ctx;
     return Q4K_ERR_CUDA;
@@ -102,10 +125,7 @@ int q4k_gemv(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, 
   int rc = check_matmul(ctx, w, x, y, M, N, batch);
   if (rc != Q4K_OK) return rc;
   if (M == 0) return Q4K_OK;
-  return cuda_status(ctx,
-                     q4k::launch_gemv(static_cast<const uint8_t*>(w), x, y, M, N, batch, N, M, 0,
-                                      static_cast<cudaStream_t>(stream)),
-                     "q4k_gemv launch");
+  return run_gemv(ctx, static_cast<const uint8_t*>(w), x, y, M, N, batch, static_cast<cudaStream_t>(stream));
 }
 
 int q4k_matmul_quant(q4k_ctx* ctx, const float* input, const void* weight, float* output, uint32_t M, uint32_t N,
@@ -116,74 +136,95 @@ int q4k_matmul_quant(q4k_ctx* ctx, const float* input, const void* weight, float
 int q4k_dequant_f16(q4k_ctx* ctx, const void* w, uint16_t* out, uint64_t n_blocks, void* stream) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
   if (n_blocks == 0) return Q4K_OK;
-  if (!w || !out) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
-  if (!aligned16(w) || !aligned16(out)) return fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
-  if (n_blocks > (1ull << 36)) return fail(ctx, Q4K_ERR_INVALID_ARG, "n_blocks too large");
-  return cuda_status(ctx,
-                     q4k::launch_dequant_f16(static_cast<const uint8_t*>(w), out, n_blocks,
-                                             static_cast<cudaStream_t>(stream)),
-                     "q4k_dequant_f16 launch");
+  if (!w || !out) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(w) || !aligned16(out)) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  if (n_blocks > (1ull << 36)) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "n_blocks too large");
+  return ctx_cuda(ctx,
+                  launch_dequant_f16(static_cast<const uint8_t*>(w), out, n_blocks,
+                                     static_cast<cudaStream_t>(stream)),
+                  "q4k_dequant_f16 launch");
 }
 
 int q4k_logit_softcap(q4k_ctx* ctx, float* logits, uint32_t n, float cap, void* stream) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
   if (n == 0) return Q4K_OK;
-  if (!logits) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
-  if (!(cap > 0.0f)) return fail(ctx, Q4K_ERR_INVALID_ARG, "cap must be > 0 (the engine skips the pass otherwise)");
-  return cuda_status(ctx, q4k::launch_softcap(logits, n, cap, static_cast<cudaStream_t>(stream)),
-                     "q4k_logit_softcap launch");
+  if (!logits) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (!(cap > 0.0f))
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "cap must be > 0 (the engine skips the pass otherwise)");
+  return ctx_cuda(ctx, launch_softcap(logits, n, cap, static_cast<cudaStream_t>(stream)),
+                  "q4k_logit_softcap launch");
 }
 
 int q4k_argmax(q4k_ctx* ctx, const float* logits, uint32_t n, uint32_t* result, void* stream) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
-  if (!logits || !result) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
-  return cuda_status(ctx, q4k::launch_argmax(logits, n, result, static_cast<cudaStream_t>(stream)),
-                     "q4k_argmax launch");
+  if (!logits || !result) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  return ctx_cuda(ctx, launch_argmax(logits, n, result, static_cast<cudaStream_t>(stream)), "q4k_argmax launch");
 }
 
 int q4k_topk256(q4k_ctx* ctx, const float* logits, uint32_t n, float* result, void* stream) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
-  if (!logits || !result) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
-  return cuda_status(ctx, q4k::launch_topk256(logits, n, result, static_cast<cudaStream_t>(stream)),
-                     "q4k_topk256 launch");
+  if (!logits || !result) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  return ctx_cuda(ctx, launch_topk256(logits, n, result, static_cast<cudaStream_t>(stream)), "q4k_topk256 launch");
 }
 
 int q4k_gelu_mul(q4k_ctx* ctx, const float* gate, const float* up, float* out, uint32_t n, void* stream) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
   if (n == 0) return Q4K_OK;
-  if (!gate || !up || !out) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
-  return cuda_status(ctx, q4k::launch_gelu_mul(gate, up, out, n, static_cast<cudaStream_t>(stream)),
-                     "q4k_gelu_mul launch");
+  if (!gate || !up || !out) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  return ctx_cuda(ctx, launch_gelu_mul(gate, up, out, n, static_cast<cudaStream_t>(stream)), "q4k_gelu_mul launch");
 }
 
 int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint32_t V, uint32_t N, float cap,
                       uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx, uint32_t* argmax,
                       void* stream) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
-  if (!w || !x || !cand_val || !cand_idx || !argmax) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (!w || !x || !cand_val || !cand_idx || !argmax) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
   if (N == 0 || N % Q4K_QK != 0)
-    return fail(ctx, Q4K_ERR_INVALID_ARG, "N=%u is not a positive multiple of %d", N, Q4K_QK);
-  if (V == 0) return fail(ctx, Q4K_ERR_INVALID_ARG, "V must be >= 1");
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "N=%u is not a positive multiple of %d", N, Q4K_QK);
+  if (V == 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "V must be >= 1");
   if ((uint64_t)row_offset + V >= (1ull << 31))
-    return fail(ctx, Q4K_ERR_INVALID_ARG, "row_offset + V must be < 2^31");
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "row_offset + V must be < 2^31");
   if (!aligned16(w) || !aligned16(x) || (logits && !aligned16(logits)))
-    return fail(ctx, Q4K_ERR_INVALID_ARG, "w, x and logits must be 16-byte aligned");
-  return cuda_status(ctx,
-                     q4k::launch_lmhead_select(static_cast<const uint8_t*>(w), x, V, N, cap, row_offset, logits,
-                                               cand_val, cand_idx, argmax, ctx->select,
-                                               static_cast<cudaStream_t>(stream)),
-                     "q4k_lmhead_select launch");
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "w, x and logits must be 16-byte aligned");
+  if (xfrag_bytes(N, 1) > ctx->xfrag_cap)
+    return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "N=%u exceeds the context's activation scratch", N);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  JobList jl{};
+  jl.n = 1;
+  jl.inl.x = x;
+  jl.inl.xfrag = ctx->xfrag;
+  jl.inl.inv_scale = ctx->inv_scale;
+  jl.inl.N = N;
+  cudaError_t e = launch_xprep(jl, 1, s);
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_lmhead_select activation prep launch");
+  TaskList tl{};
+  tl.n = 1;
+  tl.inl.w = static_cast<const uint8_t*>(w);
+  tl.inl.xfrag = ctx->xfrag;
+  tl.inl.inv_scale = ctx->inv_scale;
+  tl.inl.logits = logits;
+  tl.inl.cand_val = cand_val;
+  tl.inl.cand_idx = cand_idx;
+  tl.inl.argmax = argmax;
+  tl.inl.M = V;
+  tl.inl.N = N;
+  tl.inl.item_begin = 0;
+  tl.inl.item_end = tiles_of(V);
+  tl.inl.kind = kTaskSelect;
+  tl.inl.row_offset = row_offset;
+  tl.inl.cap = cap;
+  tl.total_items = tiles_of(V);
+  return ctx_cuda(ctx, launch_engine(tl, 1, true, ctx->select, ctx->sm_count, s), "q4k_lmhead_select launch");
 }
 
 int q4k_merge_candidates(q4k_ctx* ctx, const float* vals, const uint32_t* idx, uint32_t G, float* out_val,
                          uint32_t* out_idx, uint32_t* argmax, void* stream) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
-  if (!vals || !idx || !out_val || !out_idx || !argmax) return fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
-  if (G == 0 || G > 4096) return fail(ctx, Q4K_ERR_INVALID_ARG, "G=%u out of range [1, 4096]", G);
-  return cuda_status(ctx,
-                     q4k::launch_merge_candidates(vals, idx, G, out_val, out_idx, argmax,
-                                                  static_cast<cudaStream_t>(stream)),
-                     "q4k_merge_candidates launch");
+  if (!vals || !idx || !out_val || !out_idx || !argmax) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (G == 0 || G > 4096) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "G=%u out of range [1, 4096]", G);
+  return ctx_cuda(ctx,
+                  launch_merge_candidates(vals, idx, G, out_val, out_idx, argmax, static_cast<cudaStream_t>(stream)),
+                  "q4k_merge_candidates launch");
 }
 
 }  // extern "C"

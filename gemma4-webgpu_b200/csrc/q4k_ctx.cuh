@@ -1,0 +1,52 @@
+// The library context (opaque q4k_ctx of include/q4k.h) and shared helpers of
+// the C-ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/q4k.h"
+#include "q4k_engine.cuh"
+#include "q4k_kernels.cuh"
+
+struct q4k_ctx {
+  int device = 0;
+  int sm_count = 0;
+  q4k::SelectScratch select;
+  // Single-call scratch: prepared activations of one GEMV and their scales.
+  uint2* xfrag = nullptr;
+  size_t xfrag_cap = 0;  // bytes
+  float* inv_scale = nullptr;  // [kMaxTokens]
+  void* scratch = nullptr;     // the one allocation holding all of the above
+  char err[512] = {0};
+};
+
+namespace q4k {
+
+// Prepared-activation scratch a context allocates once (q4k_create).
+constexpr size_t kCtxXfragBytes = 16u << 20;
+
+inline int ctx_fail(q4k_ctx* ctx, int code, const char* fmt, ...) {
+  if (ctx) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(ctx->err, sizeof(ctx->err), fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+inline int ctx_cuda(q4k_ctx* ctx, cudaError_t e, const char* what) {
+  if (e == cudaSuccess) {
+    ctx->err[0] = 0;
+    return Q4K_OK;
+  }
+  return ctx_fail(ctx, Q4K_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+inline uint32_t tiles_of(uint32_t M) { return (M + kTileRows - 1) / kTileRows; }
+
+}  // namespace q4k

@@ -86,6 +86,16 @@ __device__ __forceinline__ float softcap(float v, float cap) {
   return tanhf(t) * cap;
 }
 
+// shaders/gelu_mul.wgsl:14-16: GELU(tanh)(g) * u.  One definition shared by
+// the gelu_mul op and the activation preparation that evaluates it on the
+// fly, so both produce the same bits.
+__device__ __forceinline__ float gelu_mul_value(float g, float u) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  float a = k0 * g * (1.0f + k1 * g * g);
+  a = a < -15.0f ? -15.0f : (a > 15.0f ? 15.0f : a);
+  return (0.5f * g * (1.0f + tanhf(a))) * u;
+}
+
 // Selection order of the reference's argmax / topk256 scans
 // (shaders/argmax.wgsl:12-20, topk256.wgsl:10-17): a first strict maximum over
 // ascending indices, started at (-1e30, 0), equals the maximum under float

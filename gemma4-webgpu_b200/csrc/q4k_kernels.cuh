@@ -21,6 +21,8 @@ constexpr size_t kSelectScratchBytes = 256 * sizeof(unsigned long long) + 256;
 cudaError_t init_select_scratch(const SelectScratch& sc, cudaStream_t s);
 
 // y[b*ldy + m] = sum_k w16(m,k) * x[b*ldx + k] for b < batch, m < M.
+// The scratch-free CUDA-core kernel (one warp per row); the engine
+// (q4k_engine.cuh) is the fast path.
 cudaError_t launch_gemv(const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t batch,
                         uint32_t ldx, uint32_t ldy, int variant, cudaStream_t s);
 
@@ -31,13 +33,6 @@ cudaError_t launch_softcap(float* logits, uint32_t n, float cap, cudaStream_t s)
 cudaError_t launch_argmax(const float* logits, uint32_t n, uint32_t* result, cudaStream_t s);
 cudaError_t launch_topk256(const float* logits, uint32_t n, float* result512, cudaStream_t s);
 cudaError_t launch_gelu_mul(const float* gate, const float* up, float* out, uint32_t n, cudaStream_t s);
-
-// Fused LM head on rows [0, V) of a (shard of a) Q4_K vocabulary matrix:
-// logits = softcap(W x) (cap <= 0 skips the softcap), optional logits store,
-// per-residue candidates over global indices row_offset + i, and argmax.
-cudaError_t launch_lmhead_select(const uint8_t* w, const float* x, uint32_t V, uint32_t N, float cap,
-                                 uint32_t row_offset, float* logits_opt, float* cand_val, uint32_t* cand_idx,
-                                 uint32_t* argmax, const SelectScratch& scratch, cudaStream_t s);
 
 // Merge G ranks' candidate sets ([G][256] each, rank-major) into one.
 cudaError_t launch_merge_candidates(const float* vals, const uint32_t* idx, uint32_t G, float* out_val,

@@ -1,0 +1,321 @@
+// Plans: a recorded sequence of matmul-path operations replayed with a fixed
+// number of launches (2 per stage), the way src/engine.ts records a token's
+// passes into one command encoder with pre-built bind groups
+// (encodeTransformerPass, :1466-1626) and submits it once (:1748).
+//
+// A plan has stages.  Inside a stage every operation is independent: one
+// activation-preparation launch prepares every distinct GEMV input (and
+// evaluates gelu_mul ops whose output feeds a GEMV of the same stage), then
+// one engine launch runs every GEMV and the LM-head selection of the stage
+// over one shared work list.  Stage s+1 starts after stage s has finished.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "q4k_ctx.cuh"
+
+using namespace q4k;
+
+namespace {
+
+struct PlanGemv {
+  const uint8_t* w;
+  const float* x;
+  float* y;
+  uint32_t M, N;
+};
+
+struct PlanGelu {
+  const float* gate;
+  const float* up;
+  float* act;
+  uint32_t n;
+};
+
+struct PlanSelect {
+  const uint8_t* w;
+  const float* x;
+  uint32_t V, N;
+  float cap;
+  uint32_t row_offset;
+  float* logits;
+  float* cand_val;
+  uint32_t* cand_idx;
+  uint32_t* argmax;
+};
+
+struct Stage {
+  std::vector<PlanGemv> gemvs;
+  std::vector<PlanGelu> gelus;
+  std::vector<PlanSelect> selects;
+  // filled by commit
+  EngineTask* tasks_dev = nullptr;
+  XJob* jobs_dev = nullptr;
+  uint32_t n_tasks = 0, n_jobs = 0, total_items = 0;
+};
+
+}  // namespace
+
+struct q4k_plan {
+  q4k_ctx* ctx = nullptr;
+  uint32_t batch = 1;
+  std::vector<Stage> stages;
+  bool committed = false;
+  void* mem = nullptr;  // one allocation: descriptors + prepared activations
+  size_t bytes = 0;
+};
+
+namespace {
+
+Stage* stage_of(q4k_plan* p, uint32_t s) {
+  if (s >= 64) return nullptr;
+  if (p->stages.size() <= s) p->stages.resize(s + 1);
+  return &p->stages[s];
+}
+
+int check_plan(q4k_plan* p) {
+  if (!p) return Q4K_ERR_INVALID_ARG;
+  if (p->committed) return ctx_fail(p->ctx, Q4K_ERR_INVALID_ARG, "plan already committed");
+  return Q4K_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" {
+
+int q4k_plan_create(q4k_ctx* ctx, uint32_t batch, q4k_plan** out) {
+  if (!ctx || !out) return Q4K_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (batch == 0 || batch > (uint32_t)kMaxTokens)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan batch=%u outside [1, %d]", batch, kMaxTokens);
+  q4k_plan* p = new q4k_plan();
+  p->ctx = ctx;
+  p->batch = batch;
+  *out = p;
+  return Q4K_OK;
+}
+
+void q4k_plan_destroy(q4k_plan* p) {
+  if (!p) return;
+  if (p->mem) cudaFree(p->mem);
+  delete p;
+}
+
+int q4k_plan_gemv(q4k_plan* p, uint32_t stage, const void* w, const float* x, float* y, uint32_t M, uint32_t N) {
+  int rc = check_plan(p);
+  if (rc != Q4K_OK) return rc;
+  q4k_ctx* ctx = p->ctx;
+  if (!w || !x || !y) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (M == 0 || N == 0 || N % Q4K_QK != 0)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "bad shape M=%u N=%u (N must be a multiple of 256)", M, N);
+  if (!aligned16(w) || !aligned16(x) || !aligned16(y))
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  Stage* st = stage_of(p, stage);
+  if (!st) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "stage %u out of range", stage);
+  st->gemvs.push_back({static_cast<const uint8_t*>(w), x, y, M, N});
+  return Q4K_OK;
+}
+
+int q4k_plan_gelu_mul(q4k_plan* p, uint32_t stage, const float* gate, const float* up, float* act, uint32_t n) {
+  int rc = check_plan(p);
+  if (rc != Q4K_OK) return rc;
+  q4k_ctx* ctx = p->ctx;
+  if (!gate || !up || !act) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (n == 0 || n % Q4K_QK != 0)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan gelu_mul size %u must be a multiple of 256", n);
+  Stage* st = stage_of(p, stage);
+  if (!st) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "stage %u out of range", stage);
+  st->gelus.push_back({gate, up, act, n});
+  return Q4K_OK;
+}
+
+int q4k_plan_lmhead(q4k_plan* p, uint32_t stage, const void* w, const float* x, uint32_t V, uint32_t N, float cap,
+                    uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx, uint32_t* argmax) {
+  int rc = check_plan(p);
+  if (rc != Q4K_OK) return rc;
+  q4k_ctx* ctx = p->ctx;
+  if (p->batch != 1) return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "the fused LM head takes batch 1");
+  if (!w || !x || !cand_val || !cand_idx || !argmax) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (V == 0 || N == 0 || N % Q4K_QK != 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "bad shape V=%u N=%u", V, N);
+  if ((uint64_t)row_offset + V >= (1ull << 31))
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "row_offset + V must be < 2^31");
+  if (!aligned16(w) || !aligned16(x) || (logits && !aligned16(logits)))
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  Stage* st = stage_of(p, stage);
+  if (!st) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "stage %u out of range", stage);
+  if (!st->selects.empty()) return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "one LM head per plan stage");
+  st->selects.push_back({static_cast<const uint8_t*>(w), x, V, N, cap, row_offset, logits, cand_val, cand_idx,
+                         argmax});
+  return Q4K_OK;
+}
+
+int q4k_plan_commit(q4k_plan* p) {
+  int rc = check_plan(p);
+  if (rc != Q4K_OK) return rc;
+  q4k_ctx* ctx = p->ctx;
+  const uint32_t B = p->batch;
+  // Per stage: one preparation job per distinct (input, N); a gelu_mul's
+  // output is a GEMV input of its stage.
+  struct JobKey {
+    const float* x;
+    uint32_t N;
+    int gelu;  // index into gelus, or -1
+  };
+  std::vector<std::vector<JobKey>> keys(p->stages.size());
+  std::vector<std::vector<EngineTask>> tasks(p->stages.size());
+  size_t xbytes = 0, desc_bytes = 0;
+  for (size_t s = 0; s < p->stages.size(); ++s) {
+    Stage& st = p->stages[s];
+    auto job_for = [&](const float* x, uint32_t N) -> int {
+      for (size_t j = 0; j < keys[s].size(); ++j)
+        if (keys[s][j].x == x && keys[s][j].N == N) return (int)j;
+      int gelu = -1;
+      for (size_t g = 0; g < st.gelus.size(); ++g)
+        if (st.gelus[g].act == x) {
+          if (st.gelus[g].n != N) return -2;
+          gelu = (int)g;
+        }
+      keys[s].push_back({x, N, gelu});
+      return (int)keys[s].size() - 1;
+    };
+    uint32_t items = 0;
+    for (const PlanGemv& g : st.gemvs) {
+      const int j = job_for(g.x, g.N);
+      if (j < 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "gelu_mul output size differs from a GEMV's N");
+      EngineTask t{};
+      t.w = g.w;
+      t.y = g.y;
+      t.M = g.M;
+      t.N = g.N;
+      t.kind = kTaskPlain;
+      t.item_begin = items;
+      items += tiles_of(g.M);
+      t.item_end = items;
+      t.pad_ = (uint32_t)j;  // job index until the buffers are laid out
+      tasks[s].push_back(t);
+    }
+    for (const PlanSelect& q : st.selects) {
+      const int j = job_for(q.x, q.N);
+      if (j < 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "gelu_mul output size differs from the LM head's N");
+      EngineTask t{};
+      t.w = q.w;
+      t.logits = q.logits;
+      t.cand_val = q.cand_val;
+      t.cand_idx = q.cand_idx;
+      t.argmax = q.argmax;
+      t.M = q.V;
+      t.N = q.N;
+      t.kind = kTaskSelect;
+      t.row_offset = q.row_offset;
+      t.cap = q.cap;
+      t.item_begin = items;
+      items += tiles_of(q.V);
+      t.item_end = items;
+      t.pad_ = (uint32_t)j;
+      tasks[s].push_back(t);
+    }
+    // gelu_mul ops nobody consumes still run (their act output is written)
+    for (size_t g = 0; g < st.gelus.size(); ++g) {
+      bool used = false;
+      for (const JobKey& k : keys[s]) used |= (k.gelu == (int)g);
+      if (!used) keys[s].push_back({st.gelus[g].act, st.gelus[g].n, (int)g});
+    }
+    st.total_items = items;
+    st.n_tasks = (uint32_t)tasks[s].size();
+    st.n_jobs = (uint32_t)keys[s].size();
+    for (const JobKey& k : keys[s]) xbytes += align_up(xfrag_bytes(k.N, B), 256) + 256;
+    desc_bytes += align_up(sizeof(EngineTask) * st.n_tasks, 256) + align_up(sizeof(XJob) * st.n_jobs, 256);
+  }
+  p->bytes = desc_bytes + xbytes;
+  if (p->bytes == 0) {
+    p->committed = true;
+    return Q4K_OK;
+  }
+  cudaError_t e = cudaMalloc(&p->mem, p->bytes);
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit allocation");
+  char* cur = static_cast<char*>(p->mem);
+  char* xcur = cur + desc_bytes;
+  for (size_t s = 0; s < p->stages.size(); ++s) {
+    Stage& st = p->stages[s];
+    std::vector<XJob> jobs(st.n_jobs);
+    for (uint32_t j = 0; j < st.n_jobs; ++j) {
+      const JobKey& k = keys[s][j];
+      XJob& J = jobs[j];
+      J = XJob{};
+      J.N = k.N;
+      if (k.gelu >= 0) {
+        const PlanGelu& g = st.gelus[k.gelu];
+        J.mode = 1;
+        J.gate = g.gate;
+        J.up = g.up;
+        J.act = g.act;
+      } else {
+        J.mode = 0;
+        J.x = k.x;
+      }
+      J.xfrag = reinterpret_cast<uint2*>(xcur);
+      xcur += align_up(xfrag_bytes(k.N, B), 256);
+      J.inv_scale = reinterpret_cast<float*>(xcur);
+      xcur += 256;
+    }
+    for (EngineTask& t : tasks[s]) {
+      const XJob& J = jobs[t.pad_];
+      t.xfrag = J.xfrag;
+      t.inv_scale = J.inv_scale;
+      t.pad_ = 0;
+    }
+    st.tasks_dev = reinterpret_cast<EngineTask*>(cur);
+    cur += align_up(sizeof(EngineTask) * st.n_tasks, 256);
+    st.jobs_dev = reinterpret_cast<XJob*>(cur);
+    cur += align_up(sizeof(XJob) * st.n_jobs, 256);
+    if (st.n_tasks) {
+      e = cudaMemcpy(st.tasks_dev, tasks[s].data(), sizeof(EngineTask) * st.n_tasks, cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
+    }
+    if (st.n_jobs) {
+      e = cudaMemcpy(st.jobs_dev, jobs.data(), sizeof(XJob) * st.n_jobs, cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
+    }
+  }
+  p->committed = true;
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
+int q4k_plan_run(q4k_plan* p, void* stream) {
+  if (!p) return Q4K_ERR_INVALID_ARG;
+  q4k_ctx* ctx = p->ctx;
+  if (!p->committed) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan not committed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (const Stage& st : p->stages) {
+    if (st.n_jobs) {
+      JobList jl{};
+      jl.dev = st.jobs_dev;
+      jl.n = st.n_jobs;
+      cudaError_t e = launch_xprep(jl, p->batch, s);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run activation prep launch");
+    }
+    if (st.total_items) {
+      TaskList tl{};
+      tl.dev = st.tasks_dev;
+      tl.n = st.n_tasks;
+      tl.total_items = st.total_items;
+      cudaError_t e = launch_engine(tl, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
+    }
+  }
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
+int q4k_plan_launches(const q4k_plan* p) {
+  if (!p || !p->committed) return -1;
+  int n = 0;
+  for (const Stage& st : p->stages) n += (st.n_jobs ? 1 : 0) + (st.total_items ? 1 : 0);
+  return n;
+}
+
+}  // extern "C"

@@ -33,6 +33,14 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_gelu_mul": ([_P, _P, _P, _P, _U32, _P], _I),
     "q4k_lmhead_select": ([_P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_merge_candidates": ([_P, _P, _P, _U32, _P, _P, _P, _P], _I),
+    "q4k_plan_create": ([_P, _U32, ctypes.POINTER(_P)], _I),
+    "q4k_plan_destroy": ([_P], None),
+    "q4k_plan_gemv": ([_P, _U32, _P, _P, _P, _U32, _U32], _I),
+    "q4k_plan_gelu_mul": ([_P, _U32, _P, _P, _P, _U32], _I),
+    "q4k_plan_lmhead": ([_P, _U32, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P], _I),
+    "q4k_plan_commit": ([_P], _I),
+    "q4k_plan_run": ([_P, _P], _I),
+    "q4k_plan_launches": ([_P], _I),
 }
 
 

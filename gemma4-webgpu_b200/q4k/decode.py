@@ -12,7 +12,15 @@ GEMVs (norms, RoPE, attention, residual adds) are not run.  Each layer
 therefore reads fixed seeded activations: q/k/v/gate/up and the LM head
 read x_h [batch, 1536], o reads x_attn [batch, 2048]; down reads
 gelu_mul(gate, up) of the same layer, as in the reference
-(src/engine.ts:1589-1605).  Layers do not feed one another.
+(src/engine.ts:1589-1605).  Layers do not feed one another, so the step's
+only data dependency is gate/up -> gelu_mul -> down.
+
+Two ways to run it:
+  * run()        -- a Plan with two stages (every GEMV that reads x_h/x_attn
+                    plus the fused LM head; then gelu_mul + down for all
+                    layers): 4 kernel launches per step;
+  * run_serial() -- one libq4k call per reference dispatch, in the
+                    reference's order (246 calls per step at batch 1).
 """
 from __future__ import annotations
 
@@ -22,7 +30,7 @@ import numpy as np
 import torch
 
 from . import synth
-from .ops import Context, Selection
+from .ops import Context, Plan, Selection
 
 CONFIG = 3  # seeds: synth.seed_for(3, matrix_id)
 
@@ -84,8 +92,10 @@ class DecodeStep:
         self.x_h = torch.from_numpy(synth.activations(B, s.hidden, synth.seed_for(CONFIG, 100))).to(dev)
         self.x_attn = torch.from_numpy(synth.activations(B, s.q, synth.seed_for(CONFIG, 101))).to(dev)
         f32 = dict(dtype=torch.float32, device=dev)
-        self.out = {name: torch.empty((B, shapes[name][0]), **f32) for name in LAYER_MATS}
-        self.act = torch.empty((B, s.ffn), **f32)
+        # distinct outputs per layer: a plan runs the layers concurrently
+        self.out = {(layer, name): torch.empty((B, shapes[name][0]), **f32)
+                    for layer in range(s.layers) for name in LAYER_MATS}
+        self.act = [torch.empty((B, s.ffn), **f32) for _ in range(s.layers)]
         if B == 1:
             self.sel = Selection(
                 cand_val=torch.empty(256, **f32),
@@ -97,6 +107,7 @@ class DecodeStep:
             self.logits = torch.empty((B, s.vocab), **f32)
             self.topk = torch.empty((B, 512), **f32)
             self.argmax = torch.empty((B,), dtype=torch.int32, device=dev)
+        self._plan: Plan | None = None
 
     # ---- accounting ---------------------------------------------------------
 
@@ -117,53 +128,91 @@ class DecodeStep:
         total += 4 * B * s.hidden + B * (256 * 8 + 4)   # LM head: x in, candidates + argmax out
         return total
 
+    def stage0_bytes(self) -> int:
+        """Algorithmic bytes of the plan's first engine launch: every GEMV but
+        down, and the LM head."""
+        s, B = self.shape, self.batch
+        total = 0
+        for name, (M, N) in layer_shapes(s).items():
+            if name != "down":
+                total += s.layers * (synth.q4k_bytes(M, N) + 4 * B * (M + N))
+        return total + synth.q4k_bytes(s.vocab, s.hidden) + 4 * B * s.hidden + B * (256 * 8 + 4)
+
     def launches_per_step(self) -> int:
+        return self.plan().launches() + (0 if self.batch == 1 else 3 * self.batch)
+
+    def serial_calls_per_step(self) -> int:
         per_layer = len(LAYER_MATS) + 1  # 7 GEMVs + gelu_mul
         lm = 1 if self.batch == 1 else 1 + 3 * self.batch
         return self.shape.layers * per_layer + lm
 
-    # ---- the step -------------------------------------------------------------
+    # ---- the plan ---------------------------------------------------------------
 
-    def run(self, stream: torch.cuda.Stream | None = None) -> None:
-        """Record one decode step's matmul path on `stream` (reference order)."""
+    def plan(self, stages: tuple[int, ...] = (0, 1)) -> Plan:
+        """Record the step (or some of its stages) as a Plan.  Stage 0: every
+        GEMV reading x_h / x_attn and the LM head; stage 1: gelu_mul and down."""
+        if stages == (0, 1) and self._plan is not None:
+            return self._plan
         c, s, B = self.ctx, self.shape, self.batch
         shapes = layer_shapes(s)
+        p = Plan(c, batch=B)
+        if 0 in stages:
+            for layer in range(s.layers):
+                for name in ("q", "k", "v", "o", "gate", "up"):
+                    M, N = shapes[name]
+                    x = self.x_attn if name == "o" else self.x_h
+                    p.gemv(0, self.weights[(layer, name)], x, self.out[(layer, name)], M, N)
+            if B == 1:
+                p.lmhead(0, self.lm_head, self.x_h, s.vocab, s.hidden, s.softcap, self.sel)
+            else:
+                p.gemv(0, self.lm_head, self.x_h, self.logits, s.vocab, s.hidden)
+        if 1 in stages:
+            st = 1 if 0 in stages else 0
+            for layer in range(s.layers):
+                p.gelu_mul(st, self.out[(layer, "gate")], self.out[(layer, "up")], self.act[layer])
+                M, N = shapes["down"]
+                p.gemv(st, self.weights[(layer, "down")], self.act[layer], self.out[(layer, "down")], M, N)
+        p.commit()
+        if stages == (0, 1):
+            self._plan = p
+        return p
+
+    def _select_rows(self, stream) -> None:
+        c, s = self.ctx, self.shape
+        for b in range(self.batch):
+            c.logit_softcap(self.logits[b], s.softcap, stream=stream)
+            c.topk256(self.logits[b], out=self.topk[b], stream=stream)
+            c.argmax(self.logits[b], out=self.argmax[b:b + 1], stream=stream)
+
+    def run(self, stream: torch.cuda.Stream | None = None) -> None:
+        """One decode step through the plan (4 launches at batch 1)."""
+        self.plan().run(stream)
+        if self.batch > 1:
+            self._select_rows(stream)
+
+    def run_serial(self, stream: torch.cuda.Stream | None = None) -> None:
+        """One decode step as one libq4k call per reference dispatch, in the
+        order of encodeTransformerPass + sampleNextTokenSubmit."""
+        c, s, B = self.ctx, self.shape, self.batch
+        shapes = layer_shapes(s)
+        W, O = self.weights, self.out
         for layer in range(s.layers):
-            W = self.weights
             for name in ("q", "k", "v"):
                 M, N = shapes[name]
-                c.gemv(W[(layer, name)], self.x_h, M, N, out=self.out[name], stream=stream)
+                c.gemv(W[(layer, name)], self.x_h, M, N, out=O[(layer, name)], stream=stream)
             M, N = shapes["o"]
-            c.gemv(W[(layer, "o")], self.x_attn, M, N, out=self.out["o"], stream=stream)
+            c.gemv(W[(layer, "o")], self.x_attn, M, N, out=O[(layer, "o")], stream=stream)
             for name in ("gate", "up"):
                 M, N = shapes[name]
-                c.gemv(W[(layer, name)], self.x_h, M, N, out=self.out[name], stream=stream)
-            c.gelu_mul(self.out["gate"], self.out["up"], out=self.act, stream=stream)
+                c.gemv(W[(layer, name)], self.x_h, M, N, out=O[(layer, name)], stream=stream)
+            c.gelu_mul(O[(layer, "gate")], O[(layer, "up")], out=self.act[layer], stream=stream)
             M, N = shapes["down"]
-            c.gemv(W[(layer, "down")], self.act, M, N, out=self.out["down"], stream=stream)
+            c.gemv(W[(layer, "down")], self.act[layer], M, N, out=O[(layer, "down")], stream=stream)
         if B == 1:
             c.lmhead_select(self.lm_head, self.x_h, s.vocab, s.hidden, s.softcap, out=self.sel, stream=stream)
         else:
             c.gemv(self.lm_head, self.x_h, s.vocab, s.hidden, out=self.logits, stream=stream)
-            for b in range(B):
-                c.logit_softcap(self.logits[b], s.softcap, stream=stream)
-                c.topk256(self.logits[b], out=self.topk[b], stream=stream)
-                c.argmax(self.logits[b], out=self.argmax[b:b + 1], stream=stream)
-
-    def run_layer_gemvs(self, stream: torch.cuda.Stream | None = None) -> None:
-        """Only the 7 GEMV launches of every layer (no gelu_mul, no LM head):
-        used to time the GEMV kernel on its own."""
-        c, s = self.ctx, self.shape
-        shapes = layer_shapes(s)
-        for layer in range(s.layers):
-            for name in LAYER_MATS:
-                M, N = shapes[name]
-                x = self.x_attn if name == "o" else (self.act if name == "down" else self.x_h)
-                c.gemv(self.weights[(layer, name)], x, M, N, out=self.out[name], stream=stream)
-
-    def layer_gemv_bytes(self) -> int:
-        s, B = self.shape, self.batch
-        return sum(s.layers * (synth.q4k_bytes(M, N) + 4 * B * (M + N)) for M, N in layer_shapes(s).values())
+            self._select_rows(stream)
 
     def result_tensors(self) -> list[torch.Tensor]:
         """What a decode step hands back to the host: the sampled token and the
@@ -184,8 +233,7 @@ class DecodeStep:
 
 class StepGraph:
     """A decode step captured once as a CUDA graph and replayed per token (the
-    way the engine pre-builds its bind groups and only re-dispatches).  The
-    capture records the same libq4k launches as DecodeStep.run."""
+    way the engine pre-builds its bind groups and only re-dispatches)."""
 
     def __init__(self, step: DecodeStep, stream: torch.cuda.Stream | None = None, body=None):
         self.step = step

@@ -216,6 +216,83 @@ class Context:
         return out
 
 
+class Plan:
+    """A recorded matmul-path step replayed with two launches per stage
+    (q4k_plan_*): the engine's "encode once, submit per token" model
+    (encodeTransformerPass + queue.submit, src/engine.ts:1466-1626, 1748).
+    Tensors are bound at record time, like bind groups, and kept alive by the
+    plan.  Operations in one stage must not depend on each other, except that
+    a GEMV may read the `act` of a gelu_mul recorded in the same stage."""
+
+    def __init__(self, ctx: Context, batch: int = 1):
+        self.ctx = ctx
+        self.batch = batch
+        self._L = ctx._L
+        h = ctypes.c_void_p()
+        ctx._check(self._L.q4k_plan_create(ctx._h, batch, ctypes.byref(h)))
+        self._h = h.value
+        self._keep: list[torch.Tensor] = []
+        self.committed = False
+
+    def _bind(self, *ts):
+        for t in ts:
+            if t is not None:
+                self._keep.append(t)
+
+    def gemv(self, stage: int, weight: torch.Tensor, x: torch.Tensor, y: torch.Tensor, M: int, N: int) -> None:
+        dev = self.ctx.device
+        _need(weight, torch.uint8, "weight", dev)
+        _need(x, torch.float32, "x", dev)
+        _need(y, torch.float32, "y", dev)
+        if x.numel() < self.batch * N or y.numel() < self.batch * M:
+            raise ValueError("x / y smaller than batch x N / batch x M")
+        if weight.numel() < M * (N // QK_K) * BLOCK_BYTES:
+            raise ValueError("weight buffer smaller than M*N/256*144 bytes")
+        self.ctx._check(self._L.q4k_plan_gemv(self._h, stage, _ptr(weight), _ptr(x), _ptr(y), M, N))
+        self._bind(weight, x, y)
+
+    def gelu_mul(self, stage: int, gate: torch.Tensor, up: torch.Tensor, act: torch.Tensor) -> None:
+        dev = self.ctx.device
+        for t, n in ((gate, "gate"), (up, "up"), (act, "act")):
+            _need(t, torch.float32, n, dev)
+        n = gate.numel() // self.batch
+        self.ctx._check(self._L.q4k_plan_gelu_mul(self._h, stage, _ptr(gate), _ptr(up), _ptr(act), n))
+        self._bind(gate, up, act)
+
+    def lmhead(self, stage: int, weight: torch.Tensor, x: torch.Tensor, V: int, N: int, cap: float,
+               out: Selection, row_offset: int = 0) -> None:
+        dev = self.ctx.device
+        _need(weight, torch.uint8, "weight", dev)
+        _need(x, torch.float32, "x", dev)
+        self.ctx._check(self._L.q4k_plan_lmhead(
+            self._h, stage, _ptr(weight), _ptr(x), V, N, cap, row_offset, _ptr(out.logits), _ptr(out.cand_val),
+            _ptr(out.cand_idx), _ptr(out.argmax)))
+        self._bind(weight, x, out.logits, out.cand_val, out.cand_idx, out.argmax)
+
+    def commit(self) -> "Plan":
+        self.ctx._check(self._L.q4k_plan_commit(self._h))
+        self.committed = True
+        return self
+
+    def run(self, stream: torch.cuda.Stream | None = None) -> None:
+        self.ctx._check(self._L.q4k_plan_run(self._h, _stream(stream)))
+
+    def launches(self) -> int:
+        return self._L.q4k_plan_launches(self._h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.q4k_plan_destroy(self._h)
+            self._h = None
+            self._keep.clear()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 _contexts: dict[int, Context] = {}
 
 

@@ -124,6 +124,47 @@ Q4K_API int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint3
 Q4K_API int q4k_merge_candidates(q4k_ctx* ctx, const float* vals, const uint32_t* idx, uint32_t G, float* out_val,
                          uint32_t* out_idx, uint32_t* argmax, void* stream);
 
+/* ---- plans ------------------------------------------------------------
+ * A plan records a decode step's matmul-path operations once and replays
+ * them with two launches per stage, the way the engine records a token's
+ * passes into one command encoder with pre-built bind groups and submits it
+ * (encodeTransformerPass + queue.submit, src/engine.ts:1466-1626, 1748).
+ * Operations of one stage are independent of each other; stage s+1 runs
+ * after stage s.  A gelu_mul whose `act` buffer is the `x` of a GEMV in the
+ * same stage is evaluated while that GEMV's input is prepared (the
+ * geluMul -> linearDown pair of src/engine.ts:1604-1605).  Buffers are
+ * bound by pointer at record time, like bind groups.  q4k_plan_commit
+ * allocates the plan's device memory once; q4k_plan_run allocates nothing. */
+typedef struct q4k_plan q4k_plan;
+
+/* New empty plan whose GEMVs all take `batch` activation rows (1..16). */
+Q4K_API int q4k_plan_create(q4k_ctx* ctx, uint32_t batch, q4k_plan** out);
+
+/* Free a plan and its device memory.  NULL is ignored. */
+Q4K_API void q4k_plan_destroy(q4k_plan* plan);
+
+/* Record y = matmul_quant(w, x) (as q4k_gemv with the plan's batch). */
+Q4K_API int q4k_plan_gemv(q4k_plan* plan, uint32_t stage, const void* w, const float* x, float* y, uint32_t M,
+                          uint32_t N);
+
+/* Record act = gelu_mul(gate, up) (shaders/gelu_mul.wgsl), n a multiple of 256. */
+Q4K_API int q4k_plan_gelu_mul(q4k_plan* plan, uint32_t stage, const float* gate, const float* up, float* act,
+                              uint32_t n);
+
+/* Record the fused LM head of q4k_lmhead_select (batch-1 plans, one per stage). */
+Q4K_API int q4k_plan_lmhead(q4k_plan* plan, uint32_t stage, const void* w, const float* x, uint32_t V, uint32_t N,
+                            float cap, uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
+                            uint32_t* argmax);
+
+/* Finish recording: lay out and upload the launch descriptors. */
+Q4K_API int q4k_plan_commit(q4k_plan* plan);
+
+/* Launch every stage on `stream` (asynchronous, graph-capturable). */
+Q4K_API int q4k_plan_run(q4k_plan* plan, void* stream);
+
+/* Kernel launches one q4k_plan_run issues (-1 before commit). */
+Q4K_API int q4k_plan_launches(const q4k_plan* plan);
+
 #ifdef __cplusplus
 }
 #endif

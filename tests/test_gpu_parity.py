@@ -130,7 +130,10 @@ def test_softcap_and_gelu(ctx, oracle):
     up = rng.standard_normal(50_000).astype(np.float32)
     o = ctx.gelu_mul(to_dev(gte), to_dev(up)).cpu().numpy()
     r = oracle.gelu_mul(gte, up)
-    assert np.max(np.abs(o - r) / np.maximum(np.abs(r), 1e-3)) < 1e-5
+    # CUDA tanhf and libm tanhf may differ by a few ulp; that error is
+    # relative to 0.5*|gate*up| (the tanh term's scale), not to the result.
+    bound = 1e-6 * np.abs(gte * up) + 1e-6 * np.abs(r)
+    assert np.all(np.abs(o - r) <= bound)
 
 
 def _selection_matches(oracle, w, x, V, N, row_offset, sel, cap=30.0, gap_tol=2e-3):
@@ -240,3 +243,82 @@ def test_errors_are_reported(ctx):
         ctx.gemv(w[:144], xm, 1, 256)
     with pytest.raises(ValueError):
         ctx.gemv(w, torch.zeros(256, dtype=torch.float32, device=DEV), 8, 256)  # weight too small
+
+
+def test_plan_matches_single_calls(ctx, oracle):
+    from q4k import Plan
+
+    H, I = 512, 1024
+    wg = to_dev(synth.q4k_matrix(I, H, 31))
+    wu = to_dev(synth.q4k_matrix(I, H, 32))
+    wd_np = synth.q4k_matrix(H, I, 33)
+    wd = to_dev(wd_np)
+    for B in (1, 3):
+        x = to_dev(synth.activations(B, H, 34))
+        g = torch.empty((B, I), dtype=torch.float32, device=DEV)
+        u = torch.empty_like(g)
+        act = torch.empty_like(g)
+        y = torch.empty((B, H), dtype=torch.float32, device=DEV)
+        p = Plan(ctx, batch=B)
+        p.gemv(0, wg, x, g, I, H)
+        p.gemv(0, wu, x, u, I, H)
+        p.gelu_mul(1, g, u, act)
+        p.gemv(1, wd, act, y, H, I)
+        p.commit()
+        assert p.launches() == 4
+        p.run()
+        torch.cuda.synchronize()
+        g1 = ctx.gemv(wg, x, I, H)
+        u1 = ctx.gemv(wu, x, I, H)
+        a1 = ctx.gelu_mul(g1, u1)
+        y1 = ctx.gemv(wd, a1, H, I)
+        for a, b in ((g, g1), (u, u1), (act, a1), (y, y1)):
+            assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+        check_gemv(oracle, y.cpu().numpy(), wd_np, act.cpu().numpy(), H, I)
+        p.close()
+
+
+def test_plan_lmhead_matches_single_call(ctx):
+    from q4k import Plan, Selection
+
+    V, N = 8192, 768
+    w = to_dev(synth.q4k_matrix(V, N, 41))
+    x = to_dev(synth.activations(1, N, 42))
+    ref = ctx.lmhead_select(w, x[0], V, N, 30.0, return_logits=True)
+    sel = Selection(torch.empty(256, device=DEV), torch.empty(256, dtype=torch.int32, device=DEV),
+                    torch.empty(1, dtype=torch.int32, device=DEV), torch.empty(V, device=DEV))
+    p = Plan(ctx, batch=1)
+    p.lmhead(0, w, x, V, N, 30.0, sel)
+    p.commit()
+    for _ in range(2):  # the scratch resets between runs
+        p.run()
+        torch.cuda.synchronize()
+        assert torch.equal(sel.cand_idx, ref.cand_idx) and torch.equal(sel.argmax, ref.argmax)
+        assert torch.equal(sel.logits.view(torch.int32), ref.logits.view(torch.int32))
+    p.close()
+
+
+def test_decode_step_plan_equals_serial(ctx):
+    from q4k.decode import DecodeStep, E2BShape
+
+    shape = E2BShape(layers=2, hidden=512, q=768, kv=256, ffn=1024, vocab=4096)
+    step = DecodeStep(ctx, shape, batch=1)
+    step.run()
+    torch.cuda.synchronize()
+    plan_out = {k: v.clone() for k, v in step.out.items()}
+    plan_sel = (step.sel.cand_idx.clone(), step.sel.argmax.clone())
+    step.run_serial()
+    torch.cuda.synchronize()
+    for k, v in step.out.items():
+        assert torch.equal(v.view(torch.int32), plan_out[k].view(torch.int32)), k
+    assert torch.equal(step.sel.cand_idx, plan_sel[0]) and torch.equal(step.sel.argmax, plan_sel[1])
+
+
+def test_extreme_activation_range(ctx, oracle):
+    # the hi/lo split is scaled per token by a power of two: huge and tiny x
+    M, N = 64, 512
+    w = synth.q4k_matrix(M, N, 51)
+    for scale in (1e-20, 1e-3, 1e4, 1e12):
+        x = (synth.activations(2, N, 52) * np.float32(scale)).astype(np.float32)
+        y = ctx.gemv(to_dev(w), to_dev(x), M, N).cpu().numpy()
+        check_gemv(oracle, y, w, x, M, N)
