@@ -203,10 +203,12 @@ def run_ours(args) -> None:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     barrier(world)
+    torch.cuda.nvtx.range_push("timed")
     start.record(s)
     for _ in range(args.steps):
         graph.replay()
     end.record(s)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     ms_local = start.elapsed_time(end)

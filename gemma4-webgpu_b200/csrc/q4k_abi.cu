@@ -100,6 +100,7 @@ int q4k_create(int device, q4k_ctx** out) {
   char* base = static_cast<char*>(ctx->scratch);
   ctx->select.slots = reinterpret_cast<unsigned long long*>(base);
   ctx->select.counter = reinterpret_cast<uint32_t*>(base + 256 * 8);
+  ctx->select.status = reinterpret_cast<uint32_t*>(base + 256 * 8 + 4);
   ctx->inv_scale = reinterpret_cast<float*>(base + sel_bytes);
   ctx->xfrag = reinterpret_cast<uint2*>(base + sel_bytes + scale_bytes);
   ctx->xfrag_cap = kCtxXfragBytes;
@@ -119,6 +120,23 @@ void q4k_destroy(q4k_ctx* ctx) {
 }
 
 const char* q4k_last_error(const q4k_ctx* ctx) { return ctx ? ctx->err : "null context"; }
+
+int q4k_check(q4k_ctx* ctx) {
+  if (!ctx) return Q4K_ERR_INVALID_ARG;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_check synchronize");
+  uint32_t status = 0;
+  e = cudaMemcpy(&status, ctx->select.status, sizeof(status), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_check status read");
+  if (status != 0) {
+    const uint32_t zero = 0;
+    cudaMemcpy(ctx->select.status, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    return ctx_fail(ctx, Q4K_ERR_TIMEOUT,
+                    "a kernel gave up waiting for its weight copies (bounded wait expired); its outputs are invalid");
+  }
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
 
 int q4k_gemv(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t batch,
              void* stream) {

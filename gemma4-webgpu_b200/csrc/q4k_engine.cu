@@ -207,11 +207,116 @@ __device__ __forceinline__ void sel_unkey(unsigned long long k, float& v, uint32
   idx = 0x7fffffffu - (uint32_t)((k >> 1) & 0x7fffffffu);
 }
 
+// ---- TMA bulk copies and mbarriers ---------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after kSpinLimit polls (each poll may itself block
+// for a short hardware-defined time), so a lost completion cannot hang the GPU.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// 1-D bulk copy global -> shared through the TMA unit, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_u32(p)));
+  return r;
+}
+
 // ---- the engine kernel ----------------------------------------------------------
+
+constexpr int kStages = 4;                                // blocks in flight per warp
+constexpr uint32_t kStageBytes = kTileRows * kBlockBytes;  // 16 rows x one super-block
+constexpr size_t kWarpSmem = kStages * (size_t)kStageBytes;
+
+// Where a warp's copy engine stands: work item, super-block and its task.
+struct Cursor {
+  uint32_t item, b, ti;
+  const uint8_t* w;
+  uint32_t M, nb, item_begin, item_end;
+};
+
+__device__ __forceinline__ void cursor_task(Cursor& cu, const TaskList& tl) {
+  const EngineTask T = task_at(tl, cu.ti);
+  cu.w = T.w;
+  cu.M = T.M;
+  cu.nb = T.N >> 8;
+  cu.item_begin = T.item_begin;
+  cu.item_end = T.item_end;
+}
+
+__device__ __forceinline__ void cursor_seek(Cursor& cu, const TaskList& tl) {
+  while (cu.item < tl.total_items && cu.item >= cu.item_end) {
+    ++cu.ti;
+    cursor_task(cu, tl);
+  }
+}
+
+__device__ __forceinline__ void cursor_next(Cursor& cu, const TaskList& tl, uint32_t stride) {
+  if (++cu.b == cu.nb) {
+    cu.b = 0;
+    cu.item += stride;
+    cursor_seek(cu, tl);
+  }
+}
+
+// Lanes 0..15 copy row (tile row = lane) of the cursor's super-block into the
+// stage; lane 0 first arms the stage's barrier with the byte count.
+__device__ __forceinline__ void issue_stage(const Cursor& cu, uint8_t* stage, uint64_t* bar, uint32_t lane) {
+  if (lane == 0) mbar_arrive_expect_tx(bar, kStageBytes);
+  __syncwarp();
+  if (lane < (uint32_t)kTileRows) {
+    uint32_t row = (cu.item - cu.item_begin) * kTileRows + lane;
+    if (row >= cu.M) row = 0;  // past the last row: copy row 0, result discarded
+    const uint8_t* src = cu.w + (uint64_t)row * cu.nb * kBlockBytes + (uint64_t)cu.b * kBlockBytes;
+    bulk_g2s(stage + lane * kBlockBytes, src, kBlockBytes, bar);
+  }
+}
 
 template <int NT>
 __global__ void __launch_bounds__(kEngineWarps * 32, 2)
     engine_kernel(const TaskList tl, uint32_t batch, int has_select, SelectScratch sel) {
+  extern __shared__ __align__(128) uint8_t smem_dyn[];
+  __shared__ uint64_t s_bar[kEngineWarps][kStages];
   __shared__ float s_bv[kEngineWarps][256];
   __shared__ uint32_t s_bi[kEngineWarps][256];
 
@@ -219,56 +324,96 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 2)
   const uint32_t g = lane >> 2, c = lane & 3u;
   // bytes (2(c&1), 2(c&1)+1) of a packed scale word -> bytes 0 and 2
   const uint32_t bsel = (c & 1u) ? ((4u << 12) | (3u << 8) | (4u << 4) | 2u) : ((4u << 12) | (1u << 8) | (4u << 4) | 0u);
+  uint8_t* wsm = smem_dyn + warp * kWarpSmem;
+  uint64_t* bars = s_bar[warp];
 
-  if (has_select) {
+  if (lane == 0)
+    for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
+  if (has_select)
     for (uint32_t r = lane; r < 256; r += 32) {
       s_bv[warp][r] = kFloorE;
       s_bi[warp][r] = 0u;
     }
-    __syncwarp();
-  }
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncwarp();
 
   const uint32_t total_warps = gridDim.x * kEngineWarps;
+  const uint32_t first = blockIdx.x * kEngineWarps + warp;
+
+  // copy cursor runs kStages super-blocks ahead of the math
+  Cursor F;
+  F.item = first;
+  F.b = 0;
+  F.ti = 0;
+  cursor_task(F, tl);
+  cursor_seek(F, tl);
+  uint32_t issued = 0;
+  for (int st = 0; st < kStages && F.item < tl.total_items; ++st) {
+    issue_stage(F, wsm + st * kStageBytes, &bars[st], lane);
+    cursor_next(F, tl, total_warps);
+    ++issued;
+  }
+
   uint32_t ti = 0;
   EngineTask T = task_at(tl, 0);
-  for (uint32_t item = blockIdx.x * kEngineWarps + warp; item < tl.total_items; item += total_warps) {
-    while (item >= T.item_end) T = task_at(tl, ++ti);
-    const uint32_t nb = T.N >> 8;
-    const uint64_t row_bytes = (uint64_t)nb * kBlockBytes;
-    const uint32_t ra = (item - T.item_begin) * kTileRows + g, rb = ra + 8;
-    const bool va = ra < T.M, vb = rb < T.M;
-    // rows past M read row 0 (valid memory); their results are discarded
-    const uint8_t* pa = T.w + (uint64_t)(va ? ra : 0u) * row_bytes;
-    const uint8_t* pb = T.w + (uint64_t)(vb ? rb : 0u) * row_bytes;
-    const uint2* xf = T.xfrag + lane;
+  uint32_t item = first;
+  while (item < tl.total_items && item >= T.item_end) T = task_at(tl, ++ti);
+  uint32_t b = 0, k = 0;
+  bool timed_out = false;
 
-    float acc[NT][4];
+  float acc[NT][4];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
 
-    BlockRegs cur = load_block(pa, pb, c);
-    for (uint32_t b = 0; b < nb; ++b) {
-      BlockRegs nxt;
-      if (b + 1 < nb) nxt = load_block(pa + (uint64_t)(b + 1) * kBlockBytes, pb + (uint64_t)(b + 1) * kBlockBytes, c);
-      const RowConsts ka = row_consts(cur.ha, c, bsel);
-      const RowConsts kb = row_consts(cur.hb, c, bsel);
-#pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const WordPairs A = dequant_word(word_of(cur.qa0, cur.qa1, w), ka);
-        const WordPairs B = dequant_word(word_of(cur.qb0, cur.qb1, w), kb);
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-          const uint2* f = xf + ((size_t)(n * nb + b) * 16) * 32;
-          const uint2 blo = ldg_v2(f + w * 32);
-          const uint2 bhi = ldg_v2(f + (8 + w) * 32);
-          mma_16816(acc[n], A.lo02, B.lo02, A.lo13, B.lo13, blo);
-          mma_16816(acc[n], A.hi02, B.hi02, A.hi13, B.hi13, bhi);
-        }
-      }
-      if (b + 1 < nb) cur = nxt;
+  while (item < tl.total_items) {
+    const uint32_t slot = k % kStages;
+    if (!mbar_wait(&bars[slot], (k / kStages) & 1u)) {
+      timed_out = true;
+      break;
+    }
+    const uint8_t* stg = wsm + slot * kStageBytes;
+    const uint4 ha = lds128(stg + g * kBlockBytes);
+    const uint4 hb = lds128(stg + (g + 8) * kBlockBytes);
+    const uint4 qa0 = lds128(stg + g * kBlockBytes + 16 + 32 * c);
+    const uint4 qa1 = lds128(stg + g * kBlockBytes + 32 + 32 * c);
+    const uint4 qb0 = lds128(stg + (g + 8) * kBlockBytes + 16 + 32 * c);
+    const uint4 qb1 = lds128(stg + (g + 8) * kBlockBytes + 32 + 32 * c);
+    // the stage is in registers: hand it back to the copy engine
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (F.item < tl.total_items) {
+      issue_stage(F, wsm + slot * kStageBytes, &bars[slot], lane);
+      cursor_next(F, tl, total_warps);
+      ++issued;
     }
 
-    // acc[n][0..1] = (hi, lo) parts of token 4n+c for row ra; [2..3] for rb.
+    const uint32_t nb = T.N >> 8;
+    const RowConsts ka = row_consts(ha, c, bsel);
+    const RowConsts kb = row_consts(hb, c, bsel);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const WordPairs A = dequant_word(word_of(qa0, qa1, w), ka);
+      const WordPairs B = dequant_word(word_of(qb0, qb1, w), kb);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        // only the 2 columns per token of the tile hold data; other lanes use 0
+        const uint32_t cols = 2u * min(4u, batch - 4u * n);
+        uint2 blo = make_uint2(0u, 0u), bhi = make_uint2(0u, 0u);
+        if (g < cols) {
+          const uint2* f = T.xfrag + ((size_t)(n * nb + b) * 16) * 32 + lane;
+          blo = ldg_v2(f + w * 32);
+          bhi = ldg_v2(f + (8 + w) * 32);
+        }
+        mma_16816(acc[n], A.lo02, B.lo02, A.lo13, B.lo13, blo);
+        mma_16816(acc[n], A.hi02, B.hi02, A.hi13, B.hi13, bhi);
+      }
+    }
+    ++k;
+    if (++b < nb) continue;
+
+    // item done: acc[n][0..1] = (hi, lo) parts of token 4n+c for row ra, [2..3] for rb
+    const uint32_t ra = (item - T.item_begin) * kTileRows + g, rb = ra + 8;
+    const bool va = ra < T.M, vb = rb < T.M;
     if (T.kind == kTaskPlain) {
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
@@ -279,25 +424,37 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 2)
           if (vb) T.y[(uint64_t)t * T.M + rb] = (acc[n][2] + acc[n][3]) * inv;
         }
       }
-    } else if (c == 0) {
-      const float inv = T.inv_scale[0];
+    } else {
+      if (c == 0) {
+        const float inv = T.inv_scale[0];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const bool valid = h ? vb : va;
-        if (!valid) continue;
-        const uint32_t row = h ? rb : ra;
-        float v = (h ? (acc[0][2] + acc[0][3]) : (acc[0][0] + acc[0][1])) * inv;
-        if (T.cap > 0.0f) v = softcap(v, T.cap);
-        if (T.logits) T.logits[row] = v;
-        const uint32_t gi = T.row_offset + row;
-        const uint32_t res = gi & 255u;
-        if (better(v, gi, s_bv[warp][res], s_bi[warp][res])) {
-          s_bv[warp][res] = v;
-          s_bi[warp][res] = gi;
+        for (int h = 0; h < 2; ++h) {
+          if (!(h ? vb : va)) continue;
+          const uint32_t row = h ? rb : ra;
+          float v = (h ? (acc[0][2] + acc[0][3]) : (acc[0][0] + acc[0][1])) * inv;
+          if (T.cap > 0.0f) v = softcap(v, T.cap);
+          if (T.logits) T.logits[row] = v;
+          const uint32_t gi = T.row_offset + row;
+          const uint32_t res = gi & 255u;
+          if (better(v, gi, s_bv[warp][res], s_bi[warp][res])) {
+            s_bv[warp][res] = v;
+            s_bi[warp][res] = gi;
+          }
         }
       }
+      __syncwarp();
     }
-    if (T.kind == kTaskSelect) __syncwarp();
+#pragma unroll
+    for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+    b = 0;
+    item += total_warps;
+    while (item < tl.total_items && item >= T.item_end) T = task_at(tl, ++ti);
+  }
+
+  if (timed_out) {
+    // record the failure, then let every copy still in flight land (bounded)
+    if (lane == 0) atomicOr(sel.status, 1u);
+    for (uint32_t j = k; j < issued; ++j) mbar_wait(&bars[j % kStages], (j / kStages) & 1u);
   }
 
   if (!has_select) return;
@@ -316,7 +473,6 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 2)
   last = __shfl_sync(0xffffffffu, last, 0);
   if (!last) return;
   __threadfence();
-  // the select task's output pointers
   EngineTask S = task_at(tl, 0);
   for (uint32_t i = 0; i < tl.n; ++i) {
     S = task_at(tl, i);
@@ -325,10 +481,10 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 2)
   float* fv = s_bv[warp];
   uint32_t* fi = s_bi[warp];
   for (uint32_t r = lane; r < 256; r += 32) {
-    const unsigned long long k = atomicExch(&sel.slots[r], sel_key(kFloorE, 0u));
+    const unsigned long long key = atomicExch(&sel.slots[r], sel_key(kFloorE, 0u));
     float v;
     uint32_t i;
-    sel_unkey(k, v, i);
+    sel_unkey(key, v, i);
     S.cand_val[r] = v;
     S.cand_idx[r] = i;
     fv[r] = v;
@@ -358,7 +514,8 @@ __device__ __forceinline__ float xjob_value(const XJob& J, uint64_t i) {
 }
 
 // One CTA per (job, token): max|x| -> power-of-two scale -> hi/lo f16 split in
-// B-fragment order.  Token columns of a partial last n-tile are zero-filled.
+// B-fragment order (columns 2t%8, 2t%8+1 of n-tile t/4; the engine never reads
+// the columns of tokens >= batch).
 __global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t batch) {
   __shared__ float s_red[8];
   const uint32_t job = blockIdx.x / batch, t = blockIdx.x % batch;
@@ -408,23 +565,14 @@ __global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t b
     dst[4 * col_lo + c] = make_uint2(__half_as_ushort(hl[0]) | ((uint32_t)__half_as_ushort(hl[2]) << 16),
                                      __half_as_ushort(hl[1]) | ((uint32_t)__half_as_ushort(hl[3]) << 16));
   }
-  if (t == batch - 1) {
-    const uint32_t tiles = (batch + 3) / 4;
-    for (uint32_t tt = batch; tt < 4 * tiles; ++tt) {
-      const uint32_t ch = 2 * (tt & 3u);
-      for (uint32_t idx = threadIdx.x; idx < nb * 64; idx += blockDim.x) {
-        const uint32_t b = idx >> 6, i = (idx >> 2) & 15u, c = idx & 3u;
-        uint2* dst = J.xfrag + ((size_t)((tt >> 2) * nb + b) * 16 + i) * 32;
-        dst[4 * ch + c] = make_uint2(0u, 0u);
-        dst[4 * (ch + 1) + c] = make_uint2(0u, 0u);
-      }
-    }
-  }
 }
 
 __global__ void init_select_kernel(SelectScratch sc) {
   sc.slots[threadIdx.x] = sel_key(kFloorE, 0u);
-  if (threadIdx.x == 0) *sc.counter = 0u;
+  if (threadIdx.x == 0) {
+    *sc.counter = 0u;
+    *sc.status = 0u;
+  }
 }
 
 }  // namespace
@@ -448,12 +596,32 @@ cudaError_t launch_engine(const TaskList& tasks, uint32_t batch, bool has_select
   if (grid == 0) grid = 1;
   const int nt = (int)((batch + 3) / 4);
   const int hs = has_select ? 1 : 0;
+  const size_t smem = kEngineWarps * kWarpSmem;
+  static bool attr_done[4] = {false, false, false, false};
+  cudaError_t e = cudaSuccess;
   switch (nt) {
-    case 1: engine_kernel<1><<<grid, kEngineWarps * 32, 0, s>>>(tasks, batch, hs, sel); break;
-    case 2: engine_kernel<2><<<grid, kEngineWarps * 32, 0, s>>>(tasks, batch, hs, sel); break;
-    case 3: engine_kernel<3><<<grid, kEngineWarps * 32, 0, s>>>(tasks, batch, hs, sel); break;
-    default: engine_kernel<4><<<grid, kEngineWarps * 32, 0, s>>>(tasks, batch, hs, sel); break;
+    case 1:
+      if (!attr_done[0]) e = cudaFuncSetAttribute(engine_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[0] = e == cudaSuccess;
+      if (e == cudaSuccess) engine_kernel<1><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
+      break;
+    case 2:
+      if (!attr_done[1]) e = cudaFuncSetAttribute(engine_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[1] = e == cudaSuccess;
+      if (e == cudaSuccess) engine_kernel<2><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
+      break;
+    case 3:
+      if (!attr_done[2]) e = cudaFuncSetAttribute(engine_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[2] = e == cudaSuccess;
+      if (e == cudaSuccess) engine_kernel<3><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
+      break;
+    default:
+      if (!attr_done[3]) e = cudaFuncSetAttribute(engine_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[3] = e == cudaSuccess;
+      if (e == cudaSuccess) engine_kernel<4><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
+      break;
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

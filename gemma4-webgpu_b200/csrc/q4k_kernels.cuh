@@ -13,6 +13,7 @@ namespace q4k {
 struct SelectScratch {
   unsigned long long* slots = nullptr;  // [256]
   uint32_t* counter = nullptr;          // [1]
+  uint32_t* status = nullptr;           // [1] nonzero: a kernel gave up a bounded wait
 };
 
 constexpr size_t kSelectScratchBytes = 256 * sizeof(unsigned long long) + 256;

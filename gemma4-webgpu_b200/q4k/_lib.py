@@ -16,6 +16,7 @@ Q4K_OK = 0
 Q4K_ERR_INVALID_ARG = -1
 Q4K_ERR_CUDA = -2
 Q4K_ERR_UNSUPPORTED = -3
+Q4K_ERR_TIMEOUT = -4
 
 # Every function include/q4k.h declares, with its ctypes signature.
 _P, _U32, _U64, _F, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float, ctypes.c_int
@@ -24,6 +25,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_create": ([_I, ctypes.POINTER(_P)], _I),
     "q4k_destroy": ([_P], None),
     "q4k_last_error": ([_P], ctypes.c_char_p),
+    "q4k_check": ([_P], _I),
     "q4k_matmul_quant": ([_P, _P, _P, _P, _U32, _U32, _P], _I),
     "q4k_gemv": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
     "q4k_dequant_f16": ([_P, _P, _P, _U64, _P], _I),

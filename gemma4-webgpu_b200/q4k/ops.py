@@ -92,6 +92,11 @@ class Context:
     def _check(self, rc: int) -> None:
         _lib.check(rc, self._h)
 
+    def check(self) -> None:
+        """Synchronize and raise Q4KError if a kernel gave up a bounded wait
+        since the last check (q4k_check)."""
+        self._check(self._L.q4k_check(self._h))
+
     # ---- matmulQuant / matmulQuantMR4 -----------------------------------
 
     def matmul_quant(self, input: torch.Tensor, weight: torch.Tensor, output: torch.Tensor, M: int, N: int,

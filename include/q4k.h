@@ -47,6 +47,7 @@ extern "C" {
 #define Q4K_ERR_INVALID_ARG (-1) /* shape, alignment or null pointer rejected */
 #define Q4K_ERR_CUDA (-2)        /* CUDA runtime error (launch, device) */
 #define Q4K_ERR_UNSUPPORTED (-3) /* valid request this build cannot serve */
+#define Q4K_ERR_TIMEOUT (-4)     /* a kernel gave up a bounded wait; outputs invalid */
 
 #define Q4K_QK 256          /* weights per Q4_K super-block */
 #define Q4K_BLOCK_BYTES 144 /* bytes per Q4_K super-block */
@@ -66,6 +67,15 @@ Q4K_API void q4k_destroy(q4k_ctx* ctx);
 
 /* Message of the last failed call on `ctx` ("" if none); never NULL. */
 Q4K_API const char* q4k_last_error(const q4k_ctx* ctx);
+
+/* Synchronize the device and report whether any kernel launched through
+ * `ctx` gave up one of its bounded waits since the last check (every wait
+ * on an asynchronous copy has an iteration limit; on expiry the kernel
+ * records it, drains its copies and returns instead of hanging).  Returns
+ * Q4K_OK or Q4K_ERR_TIMEOUT, and clears the record.  The reference's
+ * counterpart is the device-lost flag checked before public calls
+ * (src/engine.ts:385-388, 1677). */
+Q4K_API int q4k_check(q4k_ctx* ctx);
 
 /* matmul_quant: output[m] = sum_k f32(w[m,k]) * input[k], m < M.
  * Argument order and meaning follow the pipeline's bind group 0
