@@ -59,6 +59,7 @@ int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
       tl.inl.item_end = tiles_of(M);
       tl.inl.kind = kTaskPlain;
       tl.total_items = tiles_of(M);
+      tl.total_cost = tiles_of(M) * (N / Q4K_QK);
       e = launch_engine(tl, b, false, ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv engine launch");
     } else {
@@ -232,6 +233,7 @@ int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint32_t V, u
   tl.inl.row_offset = row_offset;
   tl.inl.cap = cap;
   tl.total_items = tiles_of(V);
+  tl.total_cost = tiles_of(V) * (N / Q4K_QK);
   return ctx_cuda(ctx, launch_engine(tl, 1, true, ctx->select, ctx->sm_count, s), "q4k_lmhead_select launch");
 }
 

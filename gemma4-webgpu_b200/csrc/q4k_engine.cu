@@ -4,11 +4,13 @@
 // (the weight the reference GPU multiplies: src/gguf.ts:168-210 + 425-473,
 // shaders/matmul_quant.wgsl:35), for t < batch <= 16.
 //
-// Work decomposition: a persistent grid of 8-warp CTAs walks a list of work
-// items; an item is a 16-row tile of one GEMV task (tasks = the GEMVs of one
-// launch: a single call, or every GEMV of a plan stage).  A warp owns one
-// item at a time and streams the tile's 144-byte super-blocks straight from
-// HBM into registers with 128-bit loads, one block ahead of the math.
+// Work decomposition: one 16-warp CTA per SM walks a contiguous range of a
+// shared work list; an item is a 16-row tile of one GEMV task (the tasks of a
+// launch are a single call, or every GEMV of a plan stage).  The warps of a
+// CTA take the range's items in turn, so a CTA touches few tasks and keeps
+// their prepared activations in shared memory.  Each warp streams its tiles'
+// 144-byte super-blocks HBM -> shared memory with the TMA bulk-copy engine,
+// two super-blocks per stage, two stages in flight per warp.
 //
 // Per item, lane (g = lane/4, c = lane%4) owns rows g and g+8 of the tile and
 // qs group c (sub-blocks 2c, 2c+1) of every super-block.  For each 32-bit word
@@ -37,12 +39,6 @@ constexpr float kFloorE = -1e30f;
 
 // ---- small PTX helpers -------------------------------------------------------
 
-__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
@@ -62,23 +58,10 @@ __device__ __forceinline__ float fma_h_h_f(uint16_t a, uint16_t b, float c) {
   return d;
 }
 
-// {hi, lo} f32 -> f16x2 (lo in the low half), round to nearest even.
-__device__ __forceinline__ uint32_t cvt_f16x2(float hi, float lo) {
-  uint32_t d;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
-}
-
-__device__ __forceinline__ uint4 ldg_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-  return r;
 }
 
 __device__ __forceinline__ uint2 ldg_v2(const void* p) {
@@ -132,43 +115,47 @@ __device__ __forceinline__ RowConsts row_consts(const uint4& h, uint32_t c, uint
 // One 32-bit word of nibbles (bytes b0..b3 of one row) -> four f16x2 weight
 // pairs: lo02 = (w[b0 lo], w[b2 lo]), lo13 = (w[b1 lo], w[b3 lo]), and the
 // same for the high nibbles.  Low nibbles belong to sub-block j0, high to j1.
+// One PTX block, so the f16 halves feed the mixed FMAs without integer
+// extraction.
 struct WordPairs {
   uint32_t lo02, lo13, hi02, hi13;
 };
 
 __device__ __forceinline__ WordPairs dequant_word(uint32_t v, const RowConsts& r) {
-  const uint32_t kMagic = 0x64006400u;
-  const uint32_t v8 = v >> 8;
-  const uint32_t p_lo02 = hfma2((v & 0x000F000Fu) | kMagic, r.sc0, r.nsc0);   // sc*q, exact
-  const uint32_t p_lo13 = hfma2((v8 & 0x000F000Fu) | kMagic, r.sc0, r.nsc0);
-  const uint32_t p_hi02 = hfma2((v & 0x00F000F0u) | kMagic, r.sc1, r.nsc1);
-  const uint32_t p_hi13 = hfma2((v8 & 0x00F000F0u) | kMagic, r.sc1, r.nsc1);
   WordPairs o;
-  o.lo02 = cvt_f16x2(fma_h_h_f(r.d, (uint16_t)(p_lo02 >> 16), r.ndm0),
-                     fma_h_h_f(r.d, (uint16_t)(p_lo02 & 0xffffu), r.ndm0));
-  o.lo13 = cvt_f16x2(fma_h_h_f(r.d, (uint16_t)(p_lo13 >> 16), r.ndm0),
-                     fma_h_h_f(r.d, (uint16_t)(p_lo13 & 0xffffu), r.ndm0));
-  o.hi02 = cvt_f16x2(fma_h_h_f(r.d, (uint16_t)(p_hi02 >> 16), r.ndm1),
-                     fma_h_h_f(r.d, (uint16_t)(p_hi02 & 0xffffu), r.ndm1));
-  o.hi13 = cvt_f16x2(fma_h_h_f(r.d, (uint16_t)(p_hi13 >> 16), r.ndm1),
-                     fma_h_h_f(r.d, (uint16_t)(p_hi13 & 0xffffu), r.ndm1));
+  asm("{\n\t"
+      ".reg .b32 v8, m0, m1, m2, m3, p0, p1, p2, p3;\n\t"
+      ".reg .b16 a0, a1, b0, b1, c0, c1, d0, d1;\n\t"
+      ".reg .f32 e0, e1, e2, e3, e4, e5, e6, e7;\n\t"
+      "shr.b32 v8, %4, 8;\n\t"
+      "lop3.b32 m0, %4, 0x000F000F, 0x64006400, 0xEA;\n\t"   // (v & mask) | magic
+      "lop3.b32 m1, v8, 0x000F000F, 0x64006400, 0xEA;\n\t"
+      "lop3.b32 m2, %4, 0x00F000F0, 0x64006400, 0xEA;\n\t"
+      "lop3.b32 m3, v8, 0x00F000F0, 0x64006400, 0xEA;\n\t"
+      "fma.rn.f16x2 p0, m0, %5, %6;\n\t"                    // sc*q, exact
+      "fma.rn.f16x2 p1, m1, %5, %6;\n\t"
+      "fma.rn.f16x2 p2, m2, %7, %8;\n\t"
+      "fma.rn.f16x2 p3, m3, %7, %8;\n\t"
+      "mov.b32 {a0, a1}, p0;\n\t"
+      "mov.b32 {b0, b1}, p1;\n\t"
+      "mov.b32 {c0, c1}, p2;\n\t"
+      "mov.b32 {d0, d1}, p3;\n\t"
+      "fma.rn.f32.f16 e0, %11, a0, %9;\n\t"                 // d*sc*q - dmin*m, one rounding
+      "fma.rn.f32.f16 e1, %11, a1, %9;\n\t"
+      "fma.rn.f32.f16 e2, %11, b0, %9;\n\t"
+      "fma.rn.f32.f16 e3, %11, b1, %9;\n\t"
+      "fma.rn.f32.f16 e4, %11, c0, %10;\n\t"
+      "fma.rn.f32.f16 e5, %11, c1, %10;\n\t"
+      "fma.rn.f32.f16 e6, %11, d0, %10;\n\t"
+      "fma.rn.f32.f16 e7, %11, d1, %10;\n\t"
+      "cvt.rn.f16x2.f32 %0, e1, e0;\n\t"                     // f16 RNE, (lo, hi) halves
+      "cvt.rn.f16x2.f32 %1, e3, e2;\n\t"
+      "cvt.rn.f16x2.f32 %2, e5, e4;\n\t"
+      "cvt.rn.f16x2.f32 %3, e7, e6;\n\t"
+      "}"
+      : "=r"(o.lo02), "=r"(o.lo13), "=r"(o.hi02), "=r"(o.hi13)
+      : "r"(v), "r"(r.sc0), "r"(r.nsc0), "r"(r.sc1), "r"(r.nsc1), "f"(r.ndm0), "f"(r.ndm1), "h"(r.d));
   return o;
-}
-
-// The 96 bytes one lane reads per super-block: both rows' headers and qs groups.
-struct BlockRegs {
-  uint4 ha, hb, qa0, qa1, qb0, qb1;
-};
-
-__device__ __forceinline__ BlockRegs load_block(const uint8_t* pa, const uint8_t* pb, uint32_t c) {
-  BlockRegs r;
-  r.ha = ldg_v4(pa);
-  r.hb = ldg_v4(pb);
-  r.qa0 = ldg_v4(pa + 16 + 32 * c);
-  r.qa1 = ldg_v4(pa + 32 + 32 * c);
-  r.qb0 = ldg_v4(pb + 16 + 32 * c);
-  r.qb1 = ldg_v4(pb + 32 + 32 * c);
-  return r;
 }
 
 __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int w) {
@@ -262,11 +249,46 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
   return r;
 }
 
+__device__ __forceinline__ uint4 lds128_u32(uint32_t addr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+  return r;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 r;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(addr));
+  return r;
+}
+
 // ---- the engine kernel ----------------------------------------------------------
 
-constexpr int kStages = 4;                                // blocks in flight per warp
-constexpr uint32_t kStageBytes = kTileRows * kBlockBytes;  // 16 rows x one super-block
-constexpr size_t kWarpSmem = kStages * (size_t)kStageBytes;
+constexpr int kStages = 2;        // stages in flight per warp
+constexpr int kBlocksPerStage = 2;  // super-blocks per stage (per tile row)
+
+// Shared-memory stride of a tile row inside a stage.  Two-block rows get 16
+// bytes of padding so that the 8 rows a quarter-warp reads land in distinct
+// banks (a 144-byte stride already does).
+__host__ __device__ constexpr uint32_t row_stride(uint32_t nblk) {
+  return nblk * kBlockBytes + (nblk == 2 ? 16u : 0u);
+}
+constexpr uint32_t kStageBytes = kTileRows * row_stride(kBlocksPerStage);
+constexpr size_t kWeightSmem = (size_t)kEngineWarps * kStages * kStageBytes;
+constexpr size_t kSelectSmem = (size_t)kEngineWarps * 256 * 8;
+constexpr size_t kTaskSmem = (size_t)kMaxCtaTasks * sizeof(EngineTask);
+constexpr size_t kSmemLimit = 227 * 1024;
+constexpr size_t kStaticSmemHeadroom = 4096;
+
+// Where a CTA reads task descriptors: its shared-memory copy of tasks
+// [t0, t0+nt), the global table, or (table = null) the inline task.
+struct TaskSrc {
+  const EngineTask* table;
+  uint32_t t0;
+};
+
+__device__ __forceinline__ EngineTask task_get(const TaskList& tl, const TaskSrc& ts, uint32_t i) {
+  return ts.table ? ts.table[i - ts.t0] : tl.inl;
+}
 
 // Where a warp's copy engine stands: work item, super-block and its task.
 struct Cursor {
@@ -275,8 +297,8 @@ struct Cursor {
   uint32_t M, nb, item_begin, item_end;
 };
 
-__device__ __forceinline__ void cursor_task(Cursor& cu, const TaskList& tl) {
-  const EngineTask T = task_at(tl, cu.ti);
+__device__ __forceinline__ void cursor_task(Cursor& cu, const TaskList& tl, const TaskSrc& ts) {
+  const EngineTask T = task_get(tl, ts, cu.ti);
   cu.w = T.w;
   cu.M = T.M;
   cu.nb = T.N >> 8;
@@ -284,171 +306,331 @@ __device__ __forceinline__ void cursor_task(Cursor& cu, const TaskList& tl) {
   cu.item_end = T.item_end;
 }
 
-__device__ __forceinline__ void cursor_seek(Cursor& cu, const TaskList& tl) {
-  while (cu.item < tl.total_items && cu.item >= cu.item_end) {
+__device__ __forceinline__ void cursor_seek(Cursor& cu, const TaskList& tl, const TaskSrc& ts, uint32_t end) {
+  while (cu.item < end && cu.item >= cu.item_end) {
     ++cu.ti;
-    cursor_task(cu, tl);
+    cursor_task(cu, tl, ts);
   }
 }
 
-__device__ __forceinline__ void cursor_next(Cursor& cu, const TaskList& tl, uint32_t stride) {
-  if (++cu.b == cu.nb) {
-    cu.b = 0;
-    cu.item += stride;
-    cursor_seek(cu, tl);
-  }
+// Super-blocks of the cursor's stage: up to kBlocksPerStage, not past the row.
+__device__ __forceinline__ uint32_t cursor_blocks(const Cursor& cu) {
+  return min((uint32_t)kBlocksPerStage, cu.nb - cu.b);
 }
 
-// Lanes 0..15 copy row (tile row = lane) of the cursor's super-block into the
-// stage; lane 0 first arms the stage's barrier with the byte count.
+// Lanes 0..15 copy their tile row's super-blocks b..b+nblk-1 (contiguous in
+// the row) into the stage, one row every row_stride(nblk) bytes; lane 0 first
+// arms the stage's barrier with the byte count.
 __device__ __forceinline__ void issue_stage(const Cursor& cu, uint8_t* stage, uint64_t* bar, uint32_t lane) {
-  if (lane == 0) mbar_arrive_expect_tx(bar, kStageBytes);
+  const uint32_t nblk = cursor_blocks(cu);
+  const uint32_t row_span = nblk * kBlockBytes;
+  if (lane == 0) mbar_arrive_expect_tx(bar, kTileRows * row_span);
   __syncwarp();
   if (lane < (uint32_t)kTileRows) {
     uint32_t row = (cu.item - cu.item_begin) * kTileRows + lane;
     if (row >= cu.M) row = 0;  // past the last row: copy row 0, result discarded
     const uint8_t* src = cu.w + (uint64_t)row * cu.nb * kBlockBytes + (uint64_t)cu.b * kBlockBytes;
-    bulk_g2s(stage + lane * kBlockBytes, src, kBlockBytes, bar);
+    bulk_g2s(stage + lane * row_stride(nblk), src, row_span, bar);
   }
 }
 
+
+// The 96 bytes of one super-block a lane needs: both rows' header and qs group.
+struct BlockRegs {
+  uint4 ha, hb, qa0, qa1, qb0, qb1;
+};
+
+__device__ __forceinline__ BlockRegs read_block(const uint8_t* ra_p, const uint8_t* rb_p, uint32_t c) {
+  BlockRegs r;
+  r.ha = lds128(ra_p);
+  r.hb = lds128(rb_p);
+  r.qa0 = lds128(ra_p + 16 + 32 * c);
+  r.qa1 = lds128(ra_p + 32 + 32 * c);
+  r.qb0 = lds128(rb_p + 16 + 32 * c);
+  r.qb1 = lds128(rb_p + 32 + 32 * c);
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+// This lane's B fragments of k-steps w and w+8 (one 16-byte load).
+template <bool SX>
+__device__ __forceinline__ uint4 load_frag(uint64_t addr) {
+  if constexpr (SX) return lds128_u32((uint32_t)addr);
+  return ldg_v4(reinterpret_cast<const void*>(addr));
+}
+
+// The math of one super-block: 2 rows x 64 weights per lane -> 16 (or 16*NT)
+// mma.sync.  base[n]: address of this lane's fragments of word 0 of the
+// block; COLS > 0 fixes the column count (batch = COLS/2 <= 4), making every
+// word offset an immediate.
+template <int NT, int COLS, bool SX>
+__device__ __forceinline__ void block_math(float (&acc)[NT][2][4], const BlockRegs& R, uint32_t c, uint32_t bsel,
+                                           const uint64_t (&base)[NT], const uint32_t (&wstep)[NT]) {
+  const RowConsts ka = row_consts(R.ha, c, bsel);
+  const RowConsts kb = row_consts(R.hb, c, bsel);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const WordPairs A = dequant_word(word_of(R.qa0, R.qa1, w), ka);
+    const WordPairs B = dequant_word(word_of(R.qb0, R.qb1, w), kb);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const uint32_t ws = COLS > 0 ? (uint32_t)COLS * 64u : wstep[n];
+      const uint4 f = load_frag<SX>(base[n] + (uint64_t)(w * ws));
+      mma_16816(acc[n][0], A.lo02, B.lo02, A.lo13, B.lo13, make_uint2(f.x, f.y));
+      mma_16816(acc[n][1], A.hi02, B.hi02, A.hi13, B.hi13, make_uint2(f.z, f.w));
+    }
+  }
+}
+
+// The task fields the math loop keeps in registers.
 template <int NT>
-__global__ void __launch_bounds__(kEngineWarps * 32, 2)
-    engine_kernel(const TaskList tl, uint32_t batch, int has_select, SelectScratch sel) {
-  extern __shared__ __align__(128) uint8_t smem_dyn[];
+struct Hot {
+  uint32_t M, nb, item_begin, item_end, kind;
+  const uint2* xfrag;
+  float* y;
+  uint32_t xs;      // shared-memory byte offset of the prepared activations, or ~0
+  float inv[NT];    // 1/scale of this lane's token in each n-tile
+};
+
+template <int NT>
+__device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts, uint32_t ti, const CtaSched& xc,
+                                          uint32_t c, uint32_t batch) {
+  const EngineTask T = task_get(tl, ts, ti);
+  Hot<NT> h;
+  h.M = T.M;
+  h.nb = T.N >> 8;
+  h.item_begin = T.item_begin;
+  h.item_end = T.item_end;
+  h.kind = T.kind;
+  h.xfrag = T.xfrag;
+  h.y = T.y;
+  h.xs = 0xffffffffu;
+  for (uint32_t j = 0; j < xc.nx; ++j)
+    if (xc.xptr[j] == T.xfrag) h.xs = xc.xoff[j];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) h.inv[n] = T.inv_scale[min(4u * n + c, batch - 1)];
+  return h;
+}
+
+template <int NT, int COLS>
+__global__ void __launch_bounds__(kEngineWarps * 32, 1)
+    engine_kernel(const TaskList tl, uint32_t batch, int has_select, SelectScratch sel, uint32_t xcache_cap) {
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t s_bar[kEngineWarps][kStages];
-  __shared__ float s_bv[kEngineWarps][256];
-  __shared__ uint32_t s_bi[kEngineWarps][256];
+  __shared__ uint64_t s_xbar;
+  __shared__ CtaSched s_sched;
+  __shared__ uint32_t s_next;                    // next unclaimed item of this CTA's range
+  __shared__ uint32_t s_ring[kEngineWarps][4];   // items claimed by each warp, in order
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t g = lane >> 2, c = lane & 3u;
   // bytes (2(c&1), 2(c&1)+1) of a packed scale word -> bytes 0 and 2
   const uint32_t bsel = (c & 1u) ? ((4u << 12) | (3u << 8) | (4u << 4) | 2u) : ((4u << 12) | (1u << 8) | (4u << 4) | 0u);
-  uint8_t* wsm = smem_dyn + warp * kWarpSmem;
+  uint8_t* wsm = smem + warp * (kStages * kStageBytes);
+  EngineTask* s_tasks = reinterpret_cast<EngineTask*>(smem + kWeightSmem);
+  uint8_t* xsm = smem + kWeightSmem + kTaskSmem;
+  float* s_bv = reinterpret_cast<float*>(xsm + xcache_cap) + warp * 512;
+  uint32_t* s_bi = reinterpret_cast<uint32_t*>(s_bv + 256);
   uint64_t* bars = s_bar[warp];
+  uint32_t* ring = s_ring[warp];
 
   if (lane == 0)
     for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
+  if (threadIdx.x == 0) mbar_init(&s_xbar, 1);
   if (has_select)
     for (uint32_t r = lane; r < 256; r += 32) {
-      s_bv[warp][r] = kFloorE;
-      s_bi[warp][r] = 0u;
+      s_bv[r] = kFloorE;
+      s_bi[r] = 0u;
     }
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  __syncwarp();
+  __syncthreads();
 
-  const uint32_t total_warps = gridDim.x * kEngineWarps;
-  const uint32_t first = blockIdx.x * kEngineWarps + warp;
+  // This CTA's share: from the host-made schedule (device task lists), or an
+  // equal share of the single inline task's tiles.  Its task descriptors and
+  // prepared activations are bulk-copied into shared memory.
+  if (threadIdx.x == 0) {
+    if (tl.sched) {
+      s_sched = tl.sched[blockIdx.x];
+    } else {
+      const uint32_t per = (tl.total_items + gridDim.x - 1) / gridDim.x;
+      s_sched.c0 = min(tl.total_items, blockIdx.x * per);
+      s_sched.c1 = min(tl.total_items, s_sched.c0 + per);
+      s_sched.t0 = 0;
+      s_sched.nt = 0;
+      const uint32_t xb = (uint32_t)xfrag_bytes(tl.inl.N, batch);
+      s_sched.nx = (s_sched.c0 < s_sched.c1 && xb <= xcache_cap) ? 1u : 0u;
+      s_sched.xoff[0] = 0;
+      s_sched.xbytes[0] = xb;
+      s_sched.xptr[0] = tl.inl.xfrag;
+    }
+    s_next = s_sched.c0;
+    uint32_t bytes = s_sched.nt * (uint32_t)sizeof(EngineTask);
+    for (uint32_t j = 0; j < s_sched.nx; ++j) bytes += s_sched.xbytes[j];
+    mbar_arrive_expect_tx(&s_xbar, bytes);
+    if (s_sched.nt) bulk_g2s(s_tasks, tl.dev + s_sched.t0, s_sched.nt * (uint32_t)sizeof(EngineTask), &s_xbar);
+    for (uint32_t j = 0; j < s_sched.nx; ++j)
+      for (uint32_t o = 0; o < s_sched.xbytes[j]; o += 32768u)
+        bulk_g2s(xsm + s_sched.xoff[j] + o, reinterpret_cast<const uint8_t*>(s_sched.xptr[j]) + o,
+                 min(32768u, s_sched.xbytes[j] - o), &s_xbar);
+  }
+  __syncthreads();
+  const uint32_t c0 = s_sched.c0, c1 = s_sched.c1;
+  bool timed_out = false;
+  if (!mbar_wait(&s_xbar, 0)) timed_out = true;
+  TaskSrc ts;
+  ts.table = !tl.dev ? nullptr : (s_sched.nt ? s_tasks : tl.dev);
+  ts.t0 = s_sched.nt ? s_sched.t0 : 0u;
+  const uint32_t t_first = s_sched.nt ? s_sched.t0 : 0u;
 
-  // copy cursor runs kStages super-blocks ahead of the math
+  // Items are claimed from the CTA's range by the copy cursor (a shared
+  // counter, so warps that finish early take more) and recorded in the
+  // warp's ring, which the math follows in the same order.
+  uint32_t claims = 0;
+  auto claim = [&]() -> uint32_t {
+    uint32_t it = 0;
+    if (lane == 0) {
+      it = atomicAdd(&s_next, 1u);
+      ring[claims & 3u] = it;
+    }
+    ++claims;
+    return __shfl_sync(0xffffffffu, it, 0);
+  };
+
   Cursor F;
-  F.item = first;
   F.b = 0;
-  F.ti = 0;
-  cursor_task(F, tl);
-  cursor_seek(F, tl);
+  F.ti = t_first;
+  F.item = timed_out ? c1 : claim();
+  cursor_task(F, tl, ts);
+  cursor_seek(F, tl, ts, c1);
   uint32_t issued = 0;
-  for (int st = 0; st < kStages && F.item < tl.total_items; ++st) {
+  for (int st = 0; st < kStages && F.item < c1; ++st) {
     issue_stage(F, wsm + st * kStageBytes, &bars[st], lane);
-    cursor_next(F, tl, total_warps);
+    F.b += cursor_blocks(F);
+    if (F.b == F.nb) {
+      F.b = 0;
+      F.item = claim();
+      cursor_seek(F, tl, ts, c1);
+    }
     ++issued;
   }
+  __syncwarp();
 
-  uint32_t ti = 0;
-  EngineTask T = task_at(tl, 0);
-  uint32_t item = first;
-  while (item < tl.total_items && item >= T.item_end) T = task_at(tl, ++ti);
-  uint32_t b = 0, k = 0;
-  bool timed_out = false;
-
-  float acc[NT][4];
+  // B-fragment column of this lane in each n-tile: any stored column serves,
+  // results of columns past the batch are never read.
+  const uint32_t cols_last = COLS > 0 ? (uint32_t)COLS : 2u * (batch - 4u * (NT - 1));
+  uint32_t lane_off[NT], wstep[NT];
 #pragma unroll
-  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+  for (int n = 0; n < NT; ++n) {
+    const uint32_t cols = n + 1 < NT ? 8u : cols_last;
+    lane_off[n] = ((g % cols) * 4u + c) * 16u;
+    wstep[n] = cols * 64u;
+  }
+  const uint32_t xs_base = smem_u32(xsm);
 
-  while (item < tl.total_items) {
+  uint32_t consumed = 0;
+  uint32_t item = timed_out ? c1 : ring[0];
+  uint32_t ti = t_first;
+  Hot<NT> H = hot_of<NT>(tl, ts, ti, s_sched, c, batch);
+  while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch);
+  uint32_t b = 0, k = 0;
+
+  float acc[NT][2][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) acc[n][h][0] = acc[n][h][1] = acc[n][h][2] = acc[n][h][3] = 0.0f;
+
+  while (item < c1 && !timed_out) {
     const uint32_t slot = k % kStages;
     if (!mbar_wait(&bars[slot], (k / kStages) & 1u)) {
       timed_out = true;
       break;
     }
+    const uint32_t nblk = min((uint32_t)kBlocksPerStage, H.nb - b);
     const uint8_t* stg = wsm + slot * kStageBytes;
-    const uint4 ha = lds128(stg + g * kBlockBytes);
-    const uint4 hb = lds128(stg + (g + 8) * kBlockBytes);
-    const uint4 qa0 = lds128(stg + g * kBlockBytes + 16 + 32 * c);
-    const uint4 qa1 = lds128(stg + g * kBlockBytes + 32 + 32 * c);
-    const uint4 qb0 = lds128(stg + (g + 8) * kBlockBytes + 16 + 32 * c);
-    const uint4 qb1 = lds128(stg + (g + 8) * kBlockBytes + 32 + 32 * c);
-    // the stage is in registers: hand it back to the copy engine
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (F.item < tl.total_items) {
-      issue_stage(F, wsm + slot * kStageBytes, &bars[slot], lane);
-      cursor_next(F, tl, total_warps);
-      ++issued;
-    }
-
-    const uint32_t nb = T.N >> 8;
-    const RowConsts ka = row_consts(ha, c, bsel);
-    const RowConsts kb = row_consts(hb, c, bsel);
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const WordPairs A = dequant_word(word_of(qa0, qa1, w), ka);
-      const WordPairs B = dequant_word(word_of(qb0, qb1, w), kb);
+    const uint32_t rs = row_stride(nblk);
+    const bool sx = H.xs != 0xffffffffu;
+#pragma unroll 1
+    for (uint32_t sb = 0; sb < nblk; ++sb, ++b) {
+      const BlockRegs R = read_block(stg + g * rs + sb * kBlockBytes, stg + (g + 8) * rs + sb * kBlockBytes, c);
+      if (sb + 1 == nblk) {
+        // the whole stage is in registers: hand it back to the copy engine
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (F.item < c1) {
+          issue_stage(F, wsm + slot * kStageBytes, &bars[slot], lane);
+          F.b += cursor_blocks(F);
+          if (F.b == F.nb) {
+            F.b = 0;
+            F.item = claim();
+            cursor_seek(F, tl, ts, c1);
+          }
+          ++issued;
+        }
+      }
+      uint64_t base[NT];
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
-        // only the 2 columns per token of the tile hold data; other lanes use 0
-        const uint32_t cols = 2u * min(4u, batch - 4u * n);
-        uint2 blo = make_uint2(0u, 0u), bhi = make_uint2(0u, 0u);
-        if (g < cols) {
-          const uint2* f = T.xfrag + ((size_t)(n * nb + b) * 16) * 32 + lane;
-          blo = ldg_v2(f + w * 32);
-          bhi = ldg_v2(f + (8 + w) * 32);
-        }
-        mma_16816(acc[n], A.lo02, B.lo02, A.lo13, B.lo13, blo);
-        mma_16816(acc[n], A.hi02, B.hi02, A.hi13, B.hi13, bhi);
+        // n-tiles before the last are full (8 columns): nb*4096 bytes each
+        const uint32_t off = n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n];
+        base[n] = sx ? (uint64_t)(xs_base + H.xs + off)
+                     : reinterpret_cast<uint64_t>(reinterpret_cast<const uint8_t*>(H.xfrag) + off);
       }
+      if (sx)
+        block_math<NT, COLS, true>(acc, R, c, bsel, base, wstep);
+      else
+        block_math<NT, COLS, false>(acc, R, c, bsel, base, wstep);
     }
     ++k;
-    if (++b < nb) continue;
+    if (b < H.nb) continue;
 
-    // item done: acc[n][0..1] = (hi, lo) parts of token 4n+c for row ra, [2..3] for rb
-    const uint32_t ra = (item - T.item_begin) * kTileRows + g, rb = ra + 8;
-    const bool va = ra < T.M, vb = rb < T.M;
-    if (T.kind == kTaskPlain) {
+    // item done: acc[n][*][0..1] = (hi, lo) parts of token 4n+c for row ra, [2..3] for rb
+    const uint32_t ra = (item - H.item_begin) * kTileRows + g, rb = ra + 8;
+    const bool va = ra < H.M, vb = rb < H.M;
+    if (H.kind == kTaskPlain) {
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         const uint32_t t = 4 * n + c;
         if (t < batch) {
-          const float inv = T.inv_scale[t];
-          if (va) T.y[(uint64_t)t * T.M + ra] = (acc[n][0] + acc[n][1]) * inv;
-          if (vb) T.y[(uint64_t)t * T.M + rb] = (acc[n][2] + acc[n][3]) * inv;
+          if (va) H.y[(uint64_t)t * H.M + ra] = ((acc[n][0][0] + acc[n][1][0]) + (acc[n][0][1] + acc[n][1][1])) * H.inv[n];
+          if (vb) H.y[(uint64_t)t * H.M + rb] = ((acc[n][0][2] + acc[n][1][2]) + (acc[n][0][3] + acc[n][1][3])) * H.inv[n];
         }
       }
     } else {
       if (c == 0) {
-        const float inv = T.inv_scale[0];
+        const EngineTask T = task_get(tl, ts, ti);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (!(h ? vb : va)) continue;
           const uint32_t row = h ? rb : ra;
-          float v = (h ? (acc[0][2] + acc[0][3]) : (acc[0][0] + acc[0][1])) * inv;
+          float v = (h ? ((acc[0][0][2] + acc[0][1][2]) + (acc[0][0][3] + acc[0][1][3]))
+                       : ((acc[0][0][0] + acc[0][1][0]) + (acc[0][0][1] + acc[0][1][1]))) * H.inv[0];
           if (T.cap > 0.0f) v = softcap(v, T.cap);
           if (T.logits) T.logits[row] = v;
           const uint32_t gi = T.row_offset + row;
           const uint32_t res = gi & 255u;
-          if (better(v, gi, s_bv[warp][res], s_bi[warp][res])) {
-            s_bv[warp][res] = v;
-            s_bi[warp][res] = gi;
+          if (better(v, gi, s_bv[res], s_bi[res])) {
+            s_bv[res] = v;
+            s_bi[res] = gi;
           }
         }
       }
       __syncwarp();
     }
 #pragma unroll
-    for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) acc[n][h][0] = acc[n][h][1] = acc[n][h][2] = acc[n][h][3] = 0.0f;
     b = 0;
-    item += total_warps;
-    while (item < tl.total_items && item >= T.item_end) T = task_at(tl, ++ti);
+    ++consumed;
+    __syncwarp();
+    item = ring[consumed & 3u];
+    while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch);
   }
 
   if (timed_out) {
@@ -462,12 +644,13 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 2)
   // turns the keys into the 256 candidates + argmax and resets the scratch.
   __syncwarp();
   for (uint32_t r = lane; r < 256; r += 32) {
-    const float v = s_bv[warp][r];
-    const uint32_t i = s_bi[warp][r];
+    const float v = s_bv[r];
+    const uint32_t i = s_bi[r];
     if (!(v == kFloorE && i == 0u)) atomicMax(&sel.slots[r], sel_key(v, i));
   }
   __threadfence();
   __syncwarp();
+  const uint32_t total_warps = gridDim.x * kEngineWarps;
   uint32_t last = 0;
   if (lane == 0) last = (atomicAdd(sel.counter, 1u) == total_warps - 1) ? 1u : 0u;
   last = __shfl_sync(0xffffffffu, last, 0);
@@ -478,8 +661,6 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 2)
     S = task_at(tl, i);
     if (S.kind == kTaskSelect) break;
   }
-  float* fv = s_bv[warp];
-  uint32_t* fi = s_bi[warp];
   for (uint32_t r = lane; r < 256; r += 32) {
     const unsigned long long key = atomicExch(&sel.slots[r], sel_key(kFloorE, 0u));
     float v;
@@ -487,22 +668,22 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 2)
     sel_unkey(key, v, i);
     S.cand_val[r] = v;
     S.cand_idx[r] = i;
-    fv[r] = v;
-    fi[r] = i;
+    s_bv[r] = v;
+    s_bi[r] = i;
   }
   __syncwarp();
   // the reference's argmax tree (shaders/argmax.wgsl:21-27), one warp
-  for (uint32_t stride = 128; stride > 0; stride >>= 1) {
-    for (uint32_t t = lane; t < stride; t += 32) {
-      if (fv[t + stride] > fv[t]) {
-        fv[t] = fv[t + stride];
-        fi[t] = fi[t + stride];
+  for (uint32_t st = 128; st > 0; st >>= 1) {
+    for (uint32_t t = lane; t < st; t += 32) {
+      if (s_bv[t + st] > s_bv[t]) {
+        s_bv[t] = s_bv[t + st];
+        s_bi[t] = s_bi[t + st];
       }
     }
     __syncwarp();
   }
   if (lane == 0) {
-    *S.argmax = fi[0];
+    *S.argmax = s_bi[0];
     *sel.counter = 0u;
   }
 }
@@ -514,8 +695,7 @@ __device__ __forceinline__ float xjob_value(const XJob& J, uint64_t i) {
 }
 
 // One CTA per (job, token): max|x| -> power-of-two scale -> hi/lo f16 split in
-// B-fragment order (columns 2t%8, 2t%8+1 of n-tile t/4; the engine never reads
-// the columns of tokens >= batch).
+// B-fragment order (compact layout of q4k_engine.cuh).
 __global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t batch) {
   __shared__ float s_red[8];
   const uint32_t job = blockIdx.x / batch, t = blockIdx.x % batch;
@@ -544,26 +724,32 @@ __global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t b
   const float s = ldexpf(1.0f, sexp);
   if (threadIdx.x == 0) J.inv_scale[t] = ldexpf(1.0f, -sexp);
 
-  const uint32_t nt = t >> 2, col_hi = 2 * (t & 3u), col_lo = col_hi + 1;
-  for (uint32_t idx = threadIdx.x; idx < nb * 64; idx += blockDim.x) {
-    const uint32_t b = idx >> 6, i = (idx >> 2) & 15u, c = idx & 3u;
-    const uint32_t off = i < 8 ? 4 * i : 32 + 4 * (i - 8);
-    const uint64_t k0 = base + 256u * b + 64u * c + off;
-    float v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = xjob_value(J, k0 + j) * s;
-    __half hh[4], hl[4];
+  const uint32_t nt = t >> 2, cols = 2u * min(4u, batch - 4u * nt);
+  const uint32_t col_hi = 2 * (t & 3u), col_lo = col_hi + 1;
+  uint4* tile = reinterpret_cast<uint4*>(J.xfrag) + (size_t)nt * nb * 256u;
+  for (uint32_t idx = threadIdx.x; idx < nb * 32; idx += blockDim.x) {
+    const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+    // k-step w (low nibbles) starts at k0, k-step w+8 (high nibbles) at k0+32
+    const uint64_t k0 = base + 256u * b + 64u * c + 4u * w;
+    float v[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      hh[j] = __float2half_rn(v[j]);
-      hl[j] = __float2half_rn(v[j] - __half2float(hh[j]));
+      v[j] = xjob_value(J, k0 + j) * s;
+      v[4 + j] = xjob_value(J, k0 + 32 + j) * s;
     }
-    uint2* dst = J.xfrag + ((size_t)(nt * nb + b) * 16 + i) * 32;
-    // (b0, b1) = (x[k0], x[k0+2]), (b2, b3) = (x[k0+1], x[k0+3])
-    dst[4 * col_hi + c] = make_uint2(__half_as_ushort(hh[0]) | ((uint32_t)__half_as_ushort(hh[2]) << 16),
-                                     __half_as_ushort(hh[1]) | ((uint32_t)__half_as_ushort(hh[3]) << 16));
-    dst[4 * col_lo + c] = make_uint2(__half_as_ushort(hl[0]) | ((uint32_t)__half_as_ushort(hl[2]) << 16),
-                                     __half_as_ushort(hl[1]) | ((uint32_t)__half_as_ushort(hl[3]) << 16));
+    uint16_t hh[8], hl[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __half h = __float2half_rn(v[j]);
+      hh[j] = __half_as_ushort(h);
+      hl[j] = __half_as_ushort(__float2half_rn(v[j] - __half2float(h)));
+    }
+    uint4* dst = tile + (size_t)(b * 8 + w) * cols * 4;
+    // per k-step: (b0, b1) = (x[k], x[k+2]), (b2, b3) = (x[k+1], x[k+3])
+    dst[4 * col_hi + c] = make_uint4(hh[0] | ((uint32_t)hh[2] << 16), hh[1] | ((uint32_t)hh[3] << 16),
+                                     hh[4] | ((uint32_t)hh[6] << 16), hh[5] | ((uint32_t)hh[7] << 16));
+    dst[4 * col_lo + c] = make_uint4(hl[0] | ((uint32_t)hl[2] << 16), hl[1] | ((uint32_t)hl[3] << 16),
+                                     hl[4] | ((uint32_t)hl[6] << 16), hl[5] | ((uint32_t)hl[7] << 16));
   }
 }
 
@@ -573,6 +759,28 @@ __global__ void init_select_kernel(SelectScratch sc) {
     *sc.counter = 0u;
     *sc.status = 0u;
   }
+}
+
+size_t xcache_bytes(int hs) {
+  return kSmemLimit - kStaticSmemHeadroom - kWeightSmem - kTaskSmem - (hs ? kSelectSmem : 0);
+}
+
+template <int NT, int COLS>
+cudaError_t launch_variant(const TaskList& tasks, uint32_t batch, int hs, const SelectScratch& sel, uint32_t grid,
+                           cudaStream_t s) {
+  const size_t xcap = xcache_bytes(hs);
+  const size_t smem = kWeightSmem + kTaskSmem + xcap + (hs ? kSelectSmem : 0);
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(kSmemLimit - kStaticSmemHeadroom));
+    if (e != cudaSuccess) return e;
+    attr_dev = dev;
+  }
+  engine_kernel<NT, COLS><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel, (uint32_t)xcap);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -587,42 +795,73 @@ cudaError_t launch_xprep(const JobList& jobs, uint32_t batch, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+uint32_t engine_grid(uint32_t total_items, int sm_count) {
+  uint32_t grid = (total_items + kEngineWarps - 1) / kEngineWarps;
+  if (grid > (uint32_t)sm_count) grid = (uint32_t)sm_count;
+  return grid == 0 ? 1 : grid;
+}
+
+uint32_t engine_xcache_bytes(bool has_select) { return (uint32_t)xcache_bytes(has_select ? 1 : 0); }
+
+// First work item whose super-blocks start at or after cost position p.
+static uint32_t host_item_at_cost(const EngineTask* t, uint32_t n, uint32_t total_cost, uint32_t total_items,
+                                  uint64_t p) {
+  if (p >= total_cost) return total_items;
+  uint32_t lo = 0, hi = n - 1;  // last task with cost_begin <= p
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi + 1) / 2;
+    if (t[mid].cost_begin <= p) lo = mid; else hi = mid - 1;
+  }
+  const uint32_t nb = t[lo].N >> 8;
+  const uint64_t item = t[lo].item_begin + (p - t[lo].cost_begin + nb - 1) / nb;
+  return item < t[lo].item_end ? (uint32_t)item : t[lo].item_end;
+}
+
+void engine_schedule(const EngineTask* tasks, uint32_t n, uint32_t total_cost, uint32_t total_items,
+                     uint32_t batch, uint32_t grid, uint32_t xcache_cap, CtaSched* out) {
+  for (uint32_t b = 0; b < grid; ++b) {
+    CtaSched& S = out[b];
+    S = CtaSched{};
+    S.c0 = host_item_at_cost(tasks, n, total_cost, total_items, (uint64_t)total_cost * b / grid);
+    S.c1 = host_item_at_cost(tasks, n, total_cost, total_items, (uint64_t)total_cost * (b + 1) / grid);
+    if (S.c0 >= S.c1) continue;
+    uint32_t t0 = 0;
+    while (t0 < n && tasks[t0].item_end <= S.c0) ++t0;
+    uint32_t t1 = t0;
+    while (t1 + 1 < n && tasks[t1 + 1].item_begin < S.c1) ++t1;
+    S.t0 = t0;
+    S.nt = (t1 - t0 + 1 <= (uint32_t)kMaxCtaTasks) ? t1 - t0 + 1 : 0u;
+    uint32_t used = 0;
+    for (uint32_t i = t0; i <= t1; ++i) {
+      bool seen = false;
+      for (uint32_t j = 0; j < S.nx; ++j) seen |= (S.xptr[j] == tasks[i].xfrag);
+      const uint32_t bytes = (uint32_t)xfrag_bytes(tasks[i].N, batch);
+      if (seen || S.nx == (uint32_t)kMaxCachedX || used + bytes > xcache_cap) continue;
+      S.xptr[S.nx] = tasks[i].xfrag;
+      S.xoff[S.nx] = used;
+      S.xbytes[S.nx] = bytes;
+      used += bytes;
+      ++S.nx;
+    }
+  }
+}
+
 cudaError_t launch_engine(const TaskList& tasks, uint32_t batch, bool has_select, const SelectScratch& sel,
                           int sm_count, cudaStream_t s) {
-  const uint32_t items = tasks.total_items;
-  uint32_t grid = (items + kEngineWarps - 1) / kEngineWarps;
-  const uint32_t cap = (uint32_t)sm_count * 2u;
-  if (grid > cap) grid = cap;
-  if (grid == 0) grid = 1;
-  const int nt = (int)((batch + 3) / 4);
+  const uint32_t grid = tasks.sched ? tasks.grid : engine_grid(tasks.total_items, sm_count);
   const int hs = has_select ? 1 : 0;
-  const size_t smem = kEngineWarps * kWarpSmem;
-  static bool attr_done[4] = {false, false, false, false};
-  cudaError_t e = cudaSuccess;
-  switch (nt) {
-    case 1:
-      if (!attr_done[0]) e = cudaFuncSetAttribute(engine_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done[0] = e == cudaSuccess;
-      if (e == cudaSuccess) engine_kernel<1><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
-      break;
-    case 2:
-      if (!attr_done[1]) e = cudaFuncSetAttribute(engine_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done[1] = e == cudaSuccess;
-      if (e == cudaSuccess) engine_kernel<2><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
-      break;
-    case 3:
-      if (!attr_done[2]) e = cudaFuncSetAttribute(engine_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done[2] = e == cudaSuccess;
-      if (e == cudaSuccess) engine_kernel<3><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
-      break;
+  switch (batch) {
+    case 1: return launch_variant<1, 2>(tasks, batch, hs, sel, grid, s);
+    case 2: return launch_variant<1, 4>(tasks, batch, hs, sel, grid, s);
+    case 3: return launch_variant<1, 6>(tasks, batch, hs, sel, grid, s);
+    case 4: return launch_variant<1, 8>(tasks, batch, hs, sel, grid, s);
     default:
-      if (!attr_done[3]) e = cudaFuncSetAttribute(engine_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done[3] = e == cudaSuccess;
-      if (e == cudaSuccess) engine_kernel<4><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel);
-      break;
+      switch ((batch + 3) / 4) {
+        case 2: return launch_variant<2, 0>(tasks, batch, hs, sel, grid, s);
+        case 3: return launch_variant<3, 0>(tasks, batch, hs, sel, grid, s);
+        default: return launch_variant<4, 0>(tasks, batch, hs, sel, grid, s);
+      }
   }
-  if (e != cudaSuccess) return e;
-  return cudaGetLastError();
 }
 
 }  // namespace q4k

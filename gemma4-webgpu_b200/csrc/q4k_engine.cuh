@@ -9,23 +9,24 @@
 namespace q4k {
 
 constexpr int kTileRows = 16;       // output rows per work item (one m16 MMA tile)
-constexpr int kEngineWarps = 8;     // warps per engine CTA
+constexpr int kEngineWarps = 16;    // warps per engine CTA (one CTA per SM)
 constexpr int kMaxTokens = 16;      // activation rows per GEMV (4 per n-tile, 4 n-tiles)
 
 // Prepared activation ("x fragments"): x of each token, scaled by a power of
 // two so max|x| < 2^15 and split exactly into f16 hi + f16 lo
 // (x*s = hi + lo + O(2^-22 |x*s|)), stored in the per-lane order of the
-// m16n8k16 B operand.  Column n = 2*(token%4) + part of n-tile token/4.
-// Layout: uint2 [n_tiles][N/256 blocks][16 k-steps][32 lanes].
-inline size_t xfrag_bytes(uint32_t N, uint32_t batch) {
-  const uint32_t nt = (batch + 3) / 4;
-  return (size_t)nt * N * 16;
-}
+// m16n8k16 B operand: n-tile nt holds tokens 4nt..4nt+3, column
+// 2*(token%4) + part (part 0 = hi, 1 = lo).  Only the columns of existing
+// tokens are stored: n-tile nt with cols_nt = 2*min(4, batch-4nt) columns is
+// uint4 [N/256 blocks][8 words][cols_nt][4], each uint4 holding the lane's
+// fragments of k-steps w and w+8 (low- and high-nibble MMAs of word w),
+// n-tiles back to back.  4 bytes per element per token in total.
+__host__ __device__ inline size_t xfrag_bytes(uint32_t N, uint32_t batch) { return (size_t)4 * N * batch; }
 
 enum TaskKind : uint32_t { kTaskPlain = 0, kTaskSelect = 1 };
 
 // One GEMV of an engine launch: y[t*M + m] = sum_k w16[m,k] * x[t,k].
-struct EngineTask {
+struct alignas(16) EngineTask {
   const uint8_t* w;         // Q4_K [M][N/256*144]
   const uint2* xfrag;       // prepared activations (see above)
   const float* inv_scale;   // [batch]: 1/s per token
@@ -36,10 +37,28 @@ struct EngineTask {
   uint32_t* argmax;         // kTaskSelect: [1]
   uint32_t M, N;
   uint32_t item_begin, item_end;  // work items [begin, end) = 16-row tiles
+  uint32_t cost_begin;            // sum of items * (N/256) over earlier tasks
   uint32_t kind;
   uint32_t row_offset;      // kTaskSelect: global index of row 0
   float cap;                // kTaskSelect: softcap (<= 0: none)
   uint32_t pad_;
+  uint32_t pad2_[2];        // 112 bytes: task tables are bulk-copied in 16-byte units
+};
+static_assert(sizeof(EngineTask) == 112, "EngineTask must stay a multiple of 16 bytes");
+
+constexpr int kMaxCachedX = 8;     // distinct prepared activations one CTA keeps in shared memory
+constexpr int kMaxCtaTasks = 64;   // task descriptors one CTA keeps in shared memory
+
+// One CTA's share of an engine launch, computed on the host when a plan is
+// committed: its item range, the tasks that range touches, and the prepared
+// activations it stages in shared memory (offsets into its activation cache).
+struct CtaSched {
+  uint32_t c0, c1;   // work items [c0, c1)
+  uint32_t t0, nt;   // tasks [t0, t0+nt) (nt = 0: read tasks from global memory)
+  uint32_t nx;       // activations to stage
+  uint32_t xoff[kMaxCachedX];
+  uint32_t xbytes[kMaxCachedX];
+  const uint2* xptr[kMaxCachedX];
 };
 
 // One activation to prepare: mode 0 reads x, mode 1 computes
@@ -59,9 +78,12 @@ struct XJob {
 // kernel parameters (single calls).
 struct TaskList {
   const EngineTask* dev;
+  const CtaSched* sched;  // per-CTA schedule of a device task list (grid entries)
   EngineTask inl;
   uint32_t n;
   uint32_t total_items;
+  uint32_t total_cost;  // sum of items * (N/256): the super-blocks of the launch
+  uint32_t grid;        // CTAs the schedule was made for
 };
 
 struct JobList {
@@ -69,6 +91,16 @@ struct JobList {
   XJob inl;
   uint32_t n;
 };
+
+// Engine launch geometry: CTAs for a work list, and the shared-memory
+// activation cache each CTA has (depends on whether an LM head is present).
+uint32_t engine_grid(uint32_t total_items, int sm_count);
+uint32_t engine_xcache_bytes(bool has_select);
+
+// Host-side schedule of a device task list (tasks sorted by item_begin):
+// equal shares of super-blocks per CTA, and what each CTA stages.
+void engine_schedule(const EngineTask* tasks, uint32_t n, uint32_t total_cost, uint32_t total_items,
+                     uint32_t batch, uint32_t grid, uint32_t xcache_bytes, CtaSched* out);
 
 cudaError_t launch_xprep(const JobList& jobs, uint32_t batch, cudaStream_t s);
 cudaError_t launch_engine(const TaskList& tasks, uint32_t batch, bool has_select, const SelectScratch& sel,

@@ -52,7 +52,8 @@ struct Stage {
   // filled by commit
   EngineTask* tasks_dev = nullptr;
   XJob* jobs_dev = nullptr;
-  uint32_t n_tasks = 0, n_jobs = 0, total_items = 0;
+  CtaSched* sched_dev = nullptr;
+  uint32_t n_tasks = 0, n_jobs = 0, total_items = 0, total_cost = 0, grid = 0;
 };
 
 }  // namespace
@@ -181,7 +182,7 @@ int q4k_plan_commit(q4k_plan* p) {
       keys[s].push_back({x, N, gelu});
       return (int)keys[s].size() - 1;
     };
-    uint32_t items = 0;
+    uint32_t items = 0, cost = 0;
     for (const PlanGemv& g : st.gemvs) {
       const int j = job_for(g.x, g.N);
       if (j < 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "gelu_mul output size differs from a GEMV's N");
@@ -192,7 +193,9 @@ int q4k_plan_commit(q4k_plan* p) {
       t.N = g.N;
       t.kind = kTaskPlain;
       t.item_begin = items;
+      t.cost_begin = cost;
       items += tiles_of(g.M);
+      cost += tiles_of(g.M) * (g.N / Q4K_QK);
       t.item_end = items;
       t.pad_ = (uint32_t)j;  // job index until the buffers are laid out
       tasks[s].push_back(t);
@@ -212,7 +215,9 @@ int q4k_plan_commit(q4k_plan* p) {
       t.row_offset = q.row_offset;
       t.cap = q.cap;
       t.item_begin = items;
+      t.cost_begin = cost;
       items += tiles_of(q.V);
+      cost += tiles_of(q.V) * (q.N / Q4K_QK);
       t.item_end = items;
       t.pad_ = (uint32_t)j;
       tasks[s].push_back(t);
@@ -224,10 +229,13 @@ int q4k_plan_commit(q4k_plan* p) {
       if (!used) keys[s].push_back({st.gelus[g].act, st.gelus[g].n, (int)g});
     }
     st.total_items = items;
+    st.total_cost = cost;
     st.n_tasks = (uint32_t)tasks[s].size();
     st.n_jobs = (uint32_t)keys[s].size();
+    st.grid = items ? engine_grid(items, ctx->sm_count) : 0;
     for (const JobKey& k : keys[s]) xbytes += align_up(xfrag_bytes(k.N, B), 256) + 256;
-    desc_bytes += align_up(sizeof(EngineTask) * st.n_tasks, 256) + align_up(sizeof(XJob) * st.n_jobs, 256);
+    desc_bytes += align_up(sizeof(EngineTask) * st.n_tasks, 256) + align_up(sizeof(XJob) * st.n_jobs, 256) +
+                  align_up(sizeof(CtaSched) * st.grid, 256);
   }
   p->bytes = desc_bytes + xbytes;
   if (p->bytes == 0) {
@@ -271,6 +279,15 @@ int q4k_plan_commit(q4k_plan* p) {
     cur += align_up(sizeof(EngineTask) * st.n_tasks, 256);
     st.jobs_dev = reinterpret_cast<XJob*>(cur);
     cur += align_up(sizeof(XJob) * st.n_jobs, 256);
+    st.sched_dev = reinterpret_cast<CtaSched*>(cur);
+    cur += align_up(sizeof(CtaSched) * st.grid, 256);
+    if (st.grid) {
+      std::vector<CtaSched> sched(st.grid);
+      engine_schedule(tasks[s].data(), st.n_tasks, st.total_cost, st.total_items, B, st.grid,
+                      engine_xcache_bytes(!st.selects.empty()), sched.data());
+      e = cudaMemcpy(st.sched_dev, sched.data(), sizeof(CtaSched) * st.grid, cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
+    }
     if (st.n_tasks) {
       e = cudaMemcpy(st.tasks_dev, tasks[s].data(), sizeof(EngineTask) * st.n_tasks, cudaMemcpyHostToDevice);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
@@ -301,8 +318,11 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
     if (st.total_items) {
       TaskList tl{};
       tl.dev = st.tasks_dev;
+      tl.sched = st.sched_dev;
+      tl.grid = st.grid;
       tl.n = st.n_tasks;
       tl.total_items = st.total_items;
+      tl.total_cost = st.total_cost;
       cudaError_t e = launch_engine(tl, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
     }

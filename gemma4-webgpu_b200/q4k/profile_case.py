@@ -2,11 +2,14 @@
 
     python gemma4-webgpu_b200/q4k/profile_case.py gemv [--batch B] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py lmhead [--reps R]
+    python gemma4-webgpu_b200/q4k/profile_case.py sweep [--layers L] [--reps R]
 
 `gemv` rotates over 35 distinct 6144x1536 Q4_K matrices (186 MB, more than
 the 126 MB L2, so each launch reads its weights from HBM); `lmhead` runs the
-fused 262144-row LM head (226 MB).  A few hundred MB of device memory at
-most; the process exits after `reps` launches.
+fused 262144-row LM head (226 MB); `sweep` runs the decode-step plan of
+q4k.decode with L layers (default 8: 159 MB of layer weights plus a
+16384-row LM head).  A few hundred MB of device memory at most; the process
+exits after `reps` runs.
 """
 from __future__ import annotations
 
@@ -23,7 +26,8 @@ from q4k import Context, synth  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "lmhead"])
+    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep"])
+    ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=40)
     a = ap.parse_args()
@@ -36,6 +40,12 @@ def main() -> None:
         y = torch.empty((a.batch, M), dtype=torch.float32, device=dev)
         for r in range(a.reps):
             ctx.gemv(ws[r % len(ws)], x, M, N, out=y)
+    elif a.kernel == "sweep":
+        from q4k.decode import DecodeStep, E2BShape
+
+        step = DecodeStep(ctx, E2BShape(layers=a.layers, vocab=16384), batch=a.batch)
+        for _ in range(a.reps):
+            step.run()
     else:
         V, N = 262144, 1536
         w = torch.from_numpy(synth.q4k_matrix(V, N, synth.seed_for(3, 999))).to(dev)
