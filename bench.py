@@ -33,7 +33,7 @@ sys.path.insert(0, str(ROOT / "gemma4-webgpu_b200"))
 
 METRIC = "Q4_K GEMV achieved HBM GB/s vs ~8 TB/s; synthetic E2B decode tokens/s"
 UNIT = "GB/s"
-PROFILE_TRAFFIC = ROOT / "profiles" / "traffic.json"
+PROFILE_TRAFFIC = ROOT / "profiles" / "traffic.txt"
 
 
 def peaks() -> dict:
@@ -278,8 +278,11 @@ def run_ours(args) -> None:
 
     pk = peaks()
     traffic = None
-    if PROFILE_TRAFFIC.exists():
-        traffic = json.loads(PROFILE_TRAFFIC.read_text()).get("stage0_engine", {}).get("bytes_per_launch")
+    if PROFILE_TRAFFIC.exists() and args.batch == 1:
+        for line in PROFILE_TRAFFIC.read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 2 and parts[0] == "stage0_engine":
+                traffic = int(parts[1])
     roofline = {
         "kernel": "engine_kernel, plan stage 0 (210 GEMVs + fused LM head in one launch; timed with its prep launch)",
         "bound": "hbm",
