@@ -17,6 +17,7 @@ Q4K_ERR_INVALID_ARG = -1
 Q4K_ERR_CUDA = -2
 Q4K_ERR_UNSUPPORTED = -3
 Q4K_ERR_TIMEOUT = -4
+Q4K_ERR_SCRATCH_LIMIT = -5
 
 # Every function include/q4k.h declares, with its ctypes signature.
 _P, _U32, _U64, _F, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float, ctypes.c_int
@@ -35,6 +36,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_gelu_mul": ([_P, _P, _P, _P, _U32, _P], _I),
     "q4k_lmhead_select": ([_P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_merge_candidates": ([_P, _P, _P, _U32, _P, _P, _P, _P], _I),
+    "q4k_lmhead_select_static": ([_P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_plan_create": ([_P, _U32, ctypes.POINTER(_P)], _I),
     "q4k_plan_destroy": ([_P], None),
     "q4k_plan_gemv": ([_P, _U32, _P, _P, _P, _U32, _U32], _I),

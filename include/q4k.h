@@ -48,6 +48,7 @@ extern "C" {
 #define Q4K_ERR_CUDA (-2)        /* CUDA runtime error (launch, device) */
 #define Q4K_ERR_UNSUPPORTED (-3) /* valid request this build cannot serve */
 #define Q4K_ERR_TIMEOUT (-4)     /* a kernel gave up a bounded wait; outputs invalid */
+#define Q4K_ERR_SCRATCH_LIMIT (-5) /* request larger than q4k_lmhead_select_static's fixed scratch */
 
 #define Q4K_QK 256          /* weights per Q4_K super-block */
 #define Q4K_BLOCK_BYTES 144 /* bytes per Q4_K super-block */
@@ -133,6 +134,27 @@ Q4K_API int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint3
  * No reference counterpart: the reference is single-device. */
 Q4K_API int q4k_merge_candidates(q4k_ctx* ctx, const float* vals, const uint32_t* idx, uint32_t G, float* out_val,
                          uint32_t* out_idx, uint32_t* argmax, void* stream);
+
+/* The fused LM head of q4k_lmhead_select for callers that cannot allocate
+ * device memory: no context, no cudaMalloc/cudaFree, no allocating library
+ * call.  It exists for real-time decode loops that must never enter the
+ * driver's allocator (an allocation can block on device-wide
+ * synchronization), and for embedders whose device memory is owned and
+ * budgeted by another runtime, so they cannot call q4k_create (which
+ * allocates the context's scratch).  No counterpart in the reference.
+ *
+ * Its scratch is a fixed array inside libq4k.so (67,328 bytes on every GPU
+ * that loads the library, held until the process exits), which limits the
+ * row length to N <= 16384; larger N returns Q4K_ERR_SCRATCH_LIMIT.  The
+ * first call on a device looks up that array's device address (with the
+ * device current), so make the first call on each device before any stream
+ * capture.  Every call shares the one array and resets its selection state
+ * first: calls that overlap on the GPU (other streams, other host threads)
+ * race and give wrong results; order them on one stream.  Arguments and
+ * outputs as q4k_lmhead_select; errors are return codes only. */
+Q4K_API int q4k_lmhead_select_static(const void* w, const float* x, uint32_t V, uint32_t N, float cap,
+                                     uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
+                                     uint32_t* argmax, void* stream);
 
 /* ---- plans ------------------------------------------------------------
  * A plan records a decode step's matmul-path operations once and replays
