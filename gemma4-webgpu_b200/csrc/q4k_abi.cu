@@ -38,6 +38,10 @@ int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     const float* xc = x + (uint64_t)done * N;
     float* yc = y + (uint64_t)done * M;
     if (xfrag_bytes(N, b) <= ctx->xfrag_cap) {
+      CUtensorMap map;
+      uint32_t tile_bytes = 0;
+      cudaError_t e = encode_weight_map(&map, w, M, N, &tile_bytes);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv weight tensor map");
       JobList jl{};
       jl.n = 1;
       jl.inl.x = xc;
@@ -45,7 +49,7 @@ int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
       jl.inl.inv_scale = ctx->inv_scale;
       jl.inl.N = N;
       jl.inl.mode = 0;
-      cudaError_t e = launch_xprep(jl, b, s);
+      e = launch_xprep(jl, b, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv activation prep launch");
       TaskList tl{};
       tl.n = 1;
@@ -58,9 +62,10 @@ int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
       tl.inl.item_begin = 0;
       tl.inl.item_end = tiles_of(M);
       tl.inl.kind = kTaskPlain;
+      tl.inl.tile_bytes = tile_bytes;
       tl.total_items = tiles_of(M);
       tl.total_cost = tiles_of(M) * (N / Q4K_QK);
-      e = launch_engine(tl, b, false, ctx->select, ctx->sm_count, s);
+      e = launch_engine(tl, map, b, false, ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv engine launch");
     } else {
       cudaError_t e = launch_gemv(w, xc, yc, M, N, b, N, M, 0, s);
@@ -208,13 +213,17 @@ int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint32_t V, u
   if (xfrag_bytes(N, 1) > ctx->xfrag_cap)
     return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "N=%u exceeds the context's activation scratch", N);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap map;
+  uint32_t tile_bytes = 0;
+  cudaError_t e = encode_weight_map(&map, w, V, N, &tile_bytes);
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_lmhead_select weight tensor map");
   JobList jl{};
   jl.n = 1;
   jl.inl.x = x;
   jl.inl.xfrag = ctx->xfrag;
   jl.inl.inv_scale = ctx->inv_scale;
   jl.inl.N = N;
-  cudaError_t e = launch_xprep(jl, 1, s);
+  e = launch_xprep(jl, 1, s);
   if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_lmhead_select activation prep launch");
   TaskList tl{};
   tl.n = 1;
@@ -232,9 +241,10 @@ int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint32_t V, u
   tl.inl.kind = kTaskSelect;
   tl.inl.row_offset = row_offset;
   tl.inl.cap = cap;
+  tl.inl.tile_bytes = tile_bytes;
   tl.total_items = tiles_of(V);
   tl.total_cost = tiles_of(V) * (N / Q4K_QK);
-  return ctx_cuda(ctx, launch_engine(tl, 1, true, ctx->select, ctx->sm_count, s), "q4k_lmhead_select launch");
+  return ctx_cuda(ctx, launch_engine(tl, map, 1, true, ctx->select, ctx->sm_count, s), "q4k_lmhead_select launch");
 }
 
 int q4k_merge_candidates(q4k_ctx* ctx, const float* vals, const uint32_t* idx, uint32_t G, float* out_val,

@@ -231,6 +231,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// 2-D tile copy of a tensor-map box at (x, y) into shared memory, completing
+// on `bar` (no multicast).
+__device__ __forceinline__ void tma_tile_g2s(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 1-D bulk copy global -> shared through the TMA unit, completing on `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -266,13 +277,12 @@ __device__ __forceinline__ uint2 lds64(uint32_t addr) {
 constexpr int kStages = 2;        // stages in flight per warp
 constexpr int kBlocksPerStage = 2;  // super-blocks per stage (per tile row)
 
-// Shared-memory stride of a tile row inside a stage.  Two-block rows get 16
-// bytes of padding so that the 8 rows a quarter-warp reads land in distinct
-// banks (a 144-byte stride already does).
-__host__ __device__ constexpr uint32_t row_stride(uint32_t nblk) {
-  return nblk * kBlockBytes + (nblk == 2 ? 16u : 0u);
-}
-constexpr uint32_t kStageBytes = kTileRows * row_stride(kBlocksPerStage);
+// A stage holds one weight-map box: 16 tile rows of 2 super-blocks plus 16
+// bytes (the box width; 144 bytes for one-block rows), so the 8 rows a
+// quarter-warp reads land in distinct banks.
+constexpr uint32_t kBoxWords2 = 2 * kBlockBytes / 4 + 4;  // 76 words = 304 bytes
+constexpr uint32_t kBoxWords1 = kBlockBytes / 4;          // 36 words = 144 bytes
+constexpr uint32_t kStageBytes = kTileRows * kBoxWords2 * 4;
 constexpr size_t kWeightSmem = (size_t)kEngineWarps * kStages * kStageBytes;
 constexpr size_t kSelectSmem = (size_t)kEngineWarps * 256 * 8;
 constexpr size_t kTaskSmem = (size_t)kMaxCtaTasks * sizeof(EngineTask);
@@ -284,6 +294,7 @@ constexpr size_t kStaticSmemHeadroom = 4096;
 struct TaskSrc {
   const EngineTask* table;
   uint32_t t0;
+  const CUtensorMap* pmap;  // the launch's own weight map (inline task)
 };
 
 __device__ __forceinline__ EngineTask task_get(const TaskList& tl, const TaskSrc& ts, uint32_t i) {
@@ -293,14 +304,14 @@ __device__ __forceinline__ EngineTask task_get(const TaskList& tl, const TaskSrc
 // Where a warp's copy engine stands: work item, super-block and its task.
 struct Cursor {
   uint32_t item, b, ti;
-  const uint8_t* w;
-  uint32_t M, nb, item_begin, item_end;
+  const CUtensorMap* map;
+  uint32_t tile_bytes, nb, item_begin, item_end;
 };
 
 __device__ __forceinline__ void cursor_task(Cursor& cu, const TaskList& tl, const TaskSrc& ts) {
   const EngineTask T = task_get(tl, ts, cu.ti);
-  cu.w = T.w;
-  cu.M = T.M;
+  cu.map = T.tmap ? T.tmap : ts.pmap;
+  cu.tile_bytes = T.tile_bytes;
   cu.nb = T.N >> 8;
   cu.item_begin = T.item_begin;
   cu.item_end = T.item_end;
@@ -318,19 +329,13 @@ __device__ __forceinline__ uint32_t cursor_blocks(const Cursor& cu) {
   return min((uint32_t)kBlocksPerStage, cu.nb - cu.b);
 }
 
-// Lanes 0..15 copy their tile row's super-blocks b..b+nblk-1 (contiguous in
-// the row) into the stage, one row every row_stride(nblk) bytes; lane 0 first
-// arms the stage's barrier with the byte count.
+// Lane 0 copies the tile's super-blocks b, b+1 of its 16 rows (one map box,
+// rows tile_bytes apart) into the stage and arms the stage's barrier with the
+// box size; rows past M and words past the row end arrive as zeros.
 __device__ __forceinline__ void issue_stage(const Cursor& cu, uint8_t* stage, uint64_t* bar, uint32_t lane) {
-  const uint32_t nblk = cursor_blocks(cu);
-  const uint32_t row_span = nblk * kBlockBytes;
-  if (lane == 0) mbar_arrive_expect_tx(bar, kTileRows * row_span);
-  __syncwarp();
-  if (lane < (uint32_t)kTileRows) {
-    uint32_t row = (cu.item - cu.item_begin) * kTileRows + lane;
-    if (row >= cu.M) row = 0;  // past the last row: copy row 0, result discarded
-    const uint8_t* src = cu.w + (uint64_t)row * cu.nb * kBlockBytes + (uint64_t)cu.b * kBlockBytes;
-    bulk_g2s(stage + lane * row_stride(nblk), src, row_span, bar);
+  if (lane == 0) {
+    mbar_arrive_expect_tx(bar, kTileRows * cu.tile_bytes);
+    tma_tile_g2s(stage, cu.map, cu.b * (kBlockBytes / 4), (cu.item - cu.item_begin) * kTileRows, bar);
   }
 }
 
@@ -390,7 +395,7 @@ __device__ __forceinline__ void block_math(float (&acc)[NT][2][4], const BlockRe
 // The task fields the math loop keeps in registers.
 template <int NT>
 struct Hot {
-  uint32_t M, nb, item_begin, item_end, kind;
+  uint32_t M, nb, item_begin, item_end, kind, tile_bytes;
   const uint2* xfrag;
   float* y;
   uint32_t xs;      // shared-memory byte offset of the prepared activations, or ~0
@@ -407,6 +412,7 @@ __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts,
   h.item_begin = T.item_begin;
   h.item_end = T.item_end;
   h.kind = T.kind;
+  h.tile_bytes = T.tile_bytes;
   h.xfrag = T.xfrag;
   h.y = T.y;
   h.xs = 0xffffffffu;
@@ -419,8 +425,11 @@ __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts,
 
 template <int NT, int COLS>
 __global__ void __launch_bounds__(kEngineWarps * 32, 1)
-    engine_kernel(const TaskList tl, uint32_t batch, int has_select, SelectScratch sel, uint32_t xcache_cap) {
-  extern __shared__ __align__(128) uint8_t smem[];
+    engine_kernel(const TaskList tl, const __grid_constant__ CUtensorMap wmap, uint32_t batch, int has_select,
+                  SelectScratch sel, uint32_t xcache_cap) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // tile copies land on 128-byte boundaries
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
   __shared__ uint64_t s_bar[kEngineWarps][kStages];
   __shared__ uint64_t s_xbar;
   __shared__ CtaSched s_sched;
@@ -485,6 +494,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   TaskSrc ts;
   ts.table = !tl.dev ? nullptr : (s_sched.nt ? s_tasks : tl.dev);
   ts.t0 = s_sched.nt ? s_sched.t0 : 0u;
+  ts.pmap = &wmap;
   const uint32_t t_first = s_sched.nt ? s_sched.t0 : 0u;
 
   // Items are claimed from the CTA's range by the copy cursor (a shared
@@ -553,7 +563,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     }
     const uint32_t nblk = min((uint32_t)kBlocksPerStage, H.nb - b);
     const uint8_t* stg = wsm + slot * kStageBytes;
-    const uint32_t rs = row_stride(nblk);
+    const uint32_t rs = H.tile_bytes;
     const bool sx = H.xs != 0xffffffffu;
 #pragma unroll 1
     for (uint32_t sb = 0; sb < nblk; ++sb, ++b) {
@@ -761,15 +771,17 @@ __global__ void init_select_kernel(SelectScratch sc) {
   }
 }
 
+constexpr size_t kAlignSlack = 128;  // room to align the dynamic shared memory base
+
 size_t xcache_bytes(int hs) {
-  return kSmemLimit - kStaticSmemHeadroom - kWeightSmem - kTaskSmem - (hs ? kSelectSmem : 0);
+  return kSmemLimit - kStaticSmemHeadroom - kAlignSlack - kWeightSmem - kTaskSmem - (hs ? kSelectSmem : 0);
 }
 
 template <int NT, int COLS>
-cudaError_t launch_variant(const TaskList& tasks, uint32_t batch, int hs, const SelectScratch& sel, uint32_t grid,
-                           cudaStream_t s) {
+cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, int hs,
+                           const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
   const size_t xcap = xcache_bytes(hs);
-  const size_t smem = kWeightSmem + kTaskSmem + xcap + (hs ? kSelectSmem : 0);
+  const size_t smem = kAlignSlack + kWeightSmem + kTaskSmem + xcap + (hs ? kSelectSmem : 0);
   static int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -779,7 +791,7 @@ cudaError_t launch_variant(const TaskList& tasks, uint32_t batch, int hs, const 
     if (e != cudaSuccess) return e;
     attr_dev = dev;
   }
-  engine_kernel<NT, COLS><<<grid, kEngineWarps * 32, smem, s>>>(tasks, batch, hs, sel, (uint32_t)xcap);
+  engine_kernel<NT, COLS><<<grid, kEngineWarps * 32, smem, s>>>(tasks, map, batch, hs, sel, (uint32_t)xcap);
   return cudaGetLastError();
 }
 
@@ -802,6 +814,47 @@ uint32_t engine_grid(uint32_t total_items, int sm_count) {
 }
 
 uint32_t engine_xcache_bytes(bool has_select) { return (uint32_t)xcache_bytes(has_select ? 1 : 0); }
+
+namespace {
+using EncodeTiledFn = decltype(&cuTensorMapEncodeTiled);
+
+// The driver's tensor-map encoder, looked up once through the runtime (the
+// library does not link libcuda directly).
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+cudaError_t encode_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N, uint32_t* tile_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const uint64_t nb = N / kQK;
+  const cuuint64_t dims[2] = {nb * (kBlockBytes / 4), M};
+  const cuuint64_t strides[1] = {nb * kBlockBytes};
+  const cuuint32_t estr[2] = {1, 1};
+  // Two-block boxes are 76 words wide; if the encoder refuses a box wider
+  // than a 2-block row, fall back to the exact 72-word row.
+  const cuuint32_t widths[2] = {nb >= 2 ? kBoxWords2 : kBoxWords1, nb >= 2 ? 2 * kBoxWords1 : kBoxWords1};
+  for (cuuint32_t box_w : widths) {
+    const cuuint32_t box[2] = {box_w, (cuuint32_t)kTileRows};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS) {
+      *tile_bytes = box_w * 4;
+      return cudaSuccess;
+    }
+  }
+  return cudaErrorInvalidValue;
+}
 
 // First work item whose super-blocks start at or after cost position p.
 static uint32_t host_item_at_cost(const EngineTask* t, uint32_t n, uint32_t total_cost, uint32_t total_items,
@@ -846,20 +899,20 @@ void engine_schedule(const EngineTask* tasks, uint32_t n, uint32_t total_cost, u
   }
 }
 
-cudaError_t launch_engine(const TaskList& tasks, uint32_t batch, bool has_select, const SelectScratch& sel,
-                          int sm_count, cudaStream_t s) {
+cudaError_t launch_engine(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, bool has_select,
+                          const SelectScratch& sel, int sm_count, cudaStream_t s) {
   const uint32_t grid = tasks.sched ? tasks.grid : engine_grid(tasks.total_items, sm_count);
   const int hs = has_select ? 1 : 0;
   switch (batch) {
-    case 1: return launch_variant<1, 2>(tasks, batch, hs, sel, grid, s);
-    case 2: return launch_variant<1, 4>(tasks, batch, hs, sel, grid, s);
-    case 3: return launch_variant<1, 6>(tasks, batch, hs, sel, grid, s);
-    case 4: return launch_variant<1, 8>(tasks, batch, hs, sel, grid, s);
+    case 1: return launch_variant<1, 2>(tasks, map, batch, hs, sel, grid, s);
+    case 2: return launch_variant<1, 4>(tasks, map, batch, hs, sel, grid, s);
+    case 3: return launch_variant<1, 6>(tasks, map, batch, hs, sel, grid, s);
+    case 4: return launch_variant<1, 8>(tasks, map, batch, hs, sel, grid, s);
     default:
       switch ((batch + 3) / 4) {
-        case 2: return launch_variant<2, 0>(tasks, batch, hs, sel, grid, s);
-        case 3: return launch_variant<3, 0>(tasks, batch, hs, sel, grid, s);
-        default: return launch_variant<4, 0>(tasks, batch, hs, sel, grid, s);
+        case 2: return launch_variant<2, 0>(tasks, map, batch, hs, sel, grid, s);
+        case 3: return launch_variant<3, 0>(tasks, map, batch, hs, sel, grid, s);
+        default: return launch_variant<4, 0>(tasks, map, batch, hs, sel, grid, s);
       }
   }
 }

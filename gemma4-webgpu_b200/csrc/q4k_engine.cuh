@@ -1,6 +1,7 @@
 // The Q4_K GEMV engine: task and activation-preparation descriptors shared by
 // the engine kernels (q4k_engine.cu), the single-call entry points and plans.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -41,8 +42,9 @@ struct alignas(16) EngineTask {
   uint32_t kind;
   uint32_t row_offset;      // kTaskSelect: global index of row 0
   float cap;                // kTaskSelect: softcap (<= 0: none)
-  uint32_t pad_;
-  uint32_t pad2_[2];        // 112 bytes: task tables are bulk-copied in 16-byte units
+  const CUtensorMap* tmap;  // TMA map of w (device memory); null: the launch's own map
+  uint32_t tile_bytes;      // bytes per tile row in a weight stage (the map's box width)
+  uint32_t aux;             // host-side bookkeeping while a plan is laid out
 };
 static_assert(sizeof(EngineTask) == 112, "EngineTask must stay a multiple of 16 bytes");
 
@@ -92,6 +94,13 @@ struct JobList {
   uint32_t n;
 };
 
+// The weight matrix as a 2-D TMA tensor of 32-bit words, [M rows][N/256*36
+// words], read in boxes of 16 rows x 2 super-blocks (+16 bytes, so tile rows
+// sit 304 bytes apart in shared memory and the lanes' 16-byte reads of 8
+// rows fall in distinct banks).  Rows past M and words past the row end
+// read as zeros.  *tile_bytes = the box width in bytes.
+cudaError_t encode_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N, uint32_t* tile_bytes);
+
 // Engine launch geometry: CTAs for a work list, and the shared-memory
 // activation cache each CTA has (depends on whether an LM head is present).
 uint32_t engine_grid(uint32_t total_items, int sm_count);
@@ -103,7 +112,9 @@ void engine_schedule(const EngineTask* tasks, uint32_t n, uint32_t total_cost, u
                      uint32_t batch, uint32_t grid, uint32_t xcache_bytes, CtaSched* out);
 
 cudaError_t launch_xprep(const JobList& jobs, uint32_t batch, cudaStream_t s);
-cudaError_t launch_engine(const TaskList& tasks, uint32_t batch, bool has_select, const SelectScratch& sel,
-                          int sm_count, cudaStream_t s);
+// `map`: the weight map of an inline task (tasks.dev == null); ignored for
+// device task lists, whose tasks carry their own maps.
+cudaError_t launch_engine(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, bool has_select,
+                          const SelectScratch& sel, int sm_count, cudaStream_t s);
 
 }  // namespace q4k

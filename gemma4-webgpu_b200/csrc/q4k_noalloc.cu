@@ -79,6 +79,9 @@ extern "C" int q4k_lmhead_select_static(const void* w, const float* x, uint32_t 
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return Q4K_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap map;
+  uint32_t tile_bytes = 0;
+  if (encode_weight_map(&map, w, V, N, &tile_bytes) != cudaSuccess) return Q4K_ERR_CUDA;
 
   // The array keeps the previous call's contents: put the selection keys,
   // counter and status back to their starting values before this call.
@@ -106,8 +109,9 @@ extern "C" int q4k_lmhead_select_static(const void* w, const float* x, uint32_t 
   tl.inl.kind = kTaskSelect;
   tl.inl.row_offset = row_offset;
   tl.inl.cap = cap;
+  tl.inl.tile_bytes = tile_bytes;
   tl.total_items = tiles_of(V);
   tl.total_cost = tiles_of(V) * (N / Q4K_QK);
-  if (launch_engine(tl, 1, true, sel, sms, s) != cudaSuccess) return Q4K_ERR_CUDA;
+  if (launch_engine(tl, map, 1, true, sel, sms, s) != cudaSuccess) return Q4K_ERR_CUDA;
   return Q4K_OK;
 }

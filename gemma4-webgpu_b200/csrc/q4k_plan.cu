@@ -51,6 +51,7 @@ struct Stage {
   std::vector<PlanSelect> selects;
   // filled by commit
   EngineTask* tasks_dev = nullptr;
+  CUtensorMap* maps_dev = nullptr;
   XJob* jobs_dev = nullptr;
   CtaSched* sched_dev = nullptr;
   uint32_t n_tasks = 0, n_jobs = 0, total_items = 0, total_cost = 0, grid = 0;
@@ -82,6 +83,9 @@ int check_plan(q4k_plan* p) {
 }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Plan tasks carry their own maps; the launch parameter is unused.
+const CUtensorMap kNoMap{};
 
 }  // namespace
 
@@ -197,7 +201,7 @@ int q4k_plan_commit(q4k_plan* p) {
       items += tiles_of(g.M);
       cost += tiles_of(g.M) * (g.N / Q4K_QK);
       t.item_end = items;
-      t.pad_ = (uint32_t)j;  // job index until the buffers are laid out
+      t.aux = (uint32_t)j;  // job index until the buffers are laid out
       tasks[s].push_back(t);
     }
     for (const PlanSelect& q : st.selects) {
@@ -219,7 +223,7 @@ int q4k_plan_commit(q4k_plan* p) {
       items += tiles_of(q.V);
       cost += tiles_of(q.V) * (q.N / Q4K_QK);
       t.item_end = items;
-      t.pad_ = (uint32_t)j;
+      t.aux = (uint32_t)j;
       tasks[s].push_back(t);
     }
     // gelu_mul ops nobody consumes still run (their act output is written)
@@ -234,8 +238,8 @@ int q4k_plan_commit(q4k_plan* p) {
     st.n_jobs = (uint32_t)keys[s].size();
     st.grid = items ? engine_grid(items, ctx->sm_count) : 0;
     for (const JobKey& k : keys[s]) xbytes += align_up(xfrag_bytes(k.N, B), 256) + 256;
-    desc_bytes += align_up(sizeof(EngineTask) * st.n_tasks, 256) + align_up(sizeof(XJob) * st.n_jobs, 256) +
-                  align_up(sizeof(CtaSched) * st.grid, 256);
+    desc_bytes += align_up(sizeof(EngineTask) * st.n_tasks, 256) + align_up(sizeof(CUtensorMap) * st.n_tasks, 256) +
+                  align_up(sizeof(XJob) * st.n_jobs, 256) + align_up(sizeof(CtaSched) * st.grid, 256);
   }
   p->bytes = desc_bytes + xbytes;
   if (p->bytes == 0) {
@@ -270,10 +274,24 @@ int q4k_plan_commit(q4k_plan* p) {
       xcur += 256;
     }
     for (EngineTask& t : tasks[s]) {
-      const XJob& J = jobs[t.pad_];
+      const XJob& J = jobs[t.aux];
       t.xfrag = J.xfrag;
       t.inv_scale = J.inv_scale;
-      t.pad_ = 0;
+      t.aux = 0;
+    }
+    // one weight tensor map per task, in the plan's memory
+    st.maps_dev = reinterpret_cast<CUtensorMap*>(cur);
+    cur += align_up(sizeof(CUtensorMap) * st.n_tasks, 256);
+    std::vector<CUtensorMap> maps(st.n_tasks);
+    for (uint32_t i = 0; i < st.n_tasks; ++i) {
+      EngineTask& t = tasks[s][i];
+      e = encode_weight_map(&maps[i], t.w, t.M, t.N, &t.tile_bytes);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit weight tensor map");
+      t.tmap = st.maps_dev + i;
+    }
+    if (st.n_tasks) {
+      e = cudaMemcpy(st.maps_dev, maps.data(), sizeof(CUtensorMap) * st.n_tasks, cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
     }
     st.tasks_dev = reinterpret_cast<EngineTask*>(cur);
     cur += align_up(sizeof(EngineTask) * st.n_tasks, 256);
@@ -323,7 +341,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
       tl.n = st.n_tasks;
       tl.total_items = st.total_items;
       tl.total_cost = st.total_cost;
-      cudaError_t e = launch_engine(tl, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
+      cudaError_t e = launch_engine(tl, kNoMap, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
     }
   }
