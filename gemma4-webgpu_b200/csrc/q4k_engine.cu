@@ -650,50 +650,61 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   }
 
   if (!has_select) return;
-  // Publish this warp's per-residue candidates; the last warp of the grid
-  // turns the keys into the 256 candidates + argmax and resets the scratch.
-  __syncwarp();
-  for (uint32_t r = lane; r < 256; r += 32) {
-    const float v = s_bv[r];
-    const uint32_t i = s_bi[r];
+  // Merge the CTA's 16 per-warp candidate sets in shared memory (thread r
+  // owns residue r) and publish one key per touched residue; the last CTA of
+  // the grid turns the keys into the 256 candidates + argmax and resets the
+  // scratch.  One publish per CTA keeps the same-address atomics few.
+  __shared__ uint32_t s_last;
+  __syncthreads();
+  float* s_all = reinterpret_cast<float*>(xsm + xcache_cap);  // warp w: values at w*512, indices at w*512+256
+  if (threadIdx.x < 256) {
+    const uint32_t r = threadIdx.x;
+    float v = s_all[r];
+    uint32_t i = reinterpret_cast<const uint32_t*>(s_all)[256 + r];
+#pragma unroll 1
+    for (int w = 1; w < kEngineWarps; ++w) {
+      const float wv = s_all[w * 512 + r];
+      const uint32_t wi = reinterpret_cast<const uint32_t*>(s_all)[w * 512 + 256 + r];
+      if (better(wv, wi, v, i)) {
+        v = wv;
+        i = wi;
+      }
+    }
     if (!(v == kFloorE && i == 0u)) atomicMax(&sel.slots[r], sel_key(v, i));
+    __threadfence();
   }
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(sel.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
   __threadfence();
-  __syncwarp();
-  const uint32_t total_warps = gridDim.x * kEngineWarps;
-  uint32_t last = 0;
-  if (lane == 0) last = (atomicAdd(sel.counter, 1u) == total_warps - 1) ? 1u : 0u;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
-  __threadfence();
-  EngineTask S = task_at(tl, 0);
-  for (uint32_t i = 0; i < tl.n; ++i) {
-    S = task_at(tl, i);
-    if (S.kind == kTaskSelect) break;
-  }
-  for (uint32_t r = lane; r < 256; r += 32) {
+  const EngineTask S = task_at(tl, tl.select_task);
+  float* f_v = s_all;
+  uint32_t* f_i = reinterpret_cast<uint32_t*>(s_all) + 256;
+  if (threadIdx.x < 256) {
+    const uint32_t r = threadIdx.x;
     const unsigned long long key = atomicExch(&sel.slots[r], sel_key(kFloorE, 0u));
     float v;
     uint32_t i;
     sel_unkey(key, v, i);
     S.cand_val[r] = v;
     S.cand_idx[r] = i;
-    s_bv[r] = v;
-    s_bi[r] = i;
+    f_v[r] = v;
+    f_i[r] = i;
   }
-  __syncwarp();
-  // the reference's argmax tree (shaders/argmax.wgsl:21-27), one warp
+  __syncthreads();
+  // the reference's argmax tree (shaders/argmax.wgsl:21-27): the partner wins
+  // only when strictly greater
   for (uint32_t st = 128; st > 0; st >>= 1) {
-    for (uint32_t t = lane; t < st; t += 32) {
-      if (s_bv[t + st] > s_bv[t]) {
-        s_bv[t] = s_bv[t + st];
-        s_bi[t] = s_bi[t + st];
-      }
+    const uint32_t t = threadIdx.x;
+    if (t < st && f_v[t + st] > f_v[t]) {
+      f_v[t] = f_v[t + st];
+      f_i[t] = f_i[t + st];
     }
-    __syncwarp();
+    __syncthreads();
   }
-  if (lane == 0) {
-    *S.argmax = s_bi[0];
+  if (threadIdx.x == 0) {
+    *S.argmax = f_i[0];
     *sel.counter = 0u;
   }
 }

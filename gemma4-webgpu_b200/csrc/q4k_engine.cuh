@@ -86,6 +86,7 @@ struct TaskList {
   uint32_t total_items;
   uint32_t total_cost;  // sum of items * (N/256): the super-blocks of the launch
   uint32_t grid;        // CTAs the schedule was made for
+  uint32_t select_task; // index of the kTaskSelect task, if the launch has one
 };
 
 struct JobList {

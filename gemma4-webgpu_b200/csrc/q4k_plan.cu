@@ -54,7 +54,7 @@ struct Stage {
   CUtensorMap* maps_dev = nullptr;
   XJob* jobs_dev = nullptr;
   CtaSched* sched_dev = nullptr;
-  uint32_t n_tasks = 0, n_jobs = 0, total_items = 0, total_cost = 0, grid = 0;
+  uint32_t n_tasks = 0, n_jobs = 0, total_items = 0, total_cost = 0, grid = 0, select_task = 0;
 };
 
 }  // namespace
@@ -205,6 +205,7 @@ int q4k_plan_commit(q4k_plan* p) {
       tasks[s].push_back(t);
     }
     for (const PlanSelect& q : st.selects) {
+      st.select_task = (uint32_t)tasks[s].size();
       const int j = job_for(q.x, q.N);
       if (j < 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "gelu_mul output size differs from the LM head's N");
       EngineTask t{};
@@ -341,6 +342,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
       tl.n = st.n_tasks;
       tl.total_items = st.total_items;
       tl.total_cost = st.total_cost;
+      tl.select_task = st.select_task;
       cudaError_t e = launch_engine(tl, kNoMap, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
     }
