@@ -11,7 +11,10 @@ more than the 126 MB L2, so every step streams the weights from HBM.
 
 N > 1 (torchrun, one rank per GPU): every rank runs its own replica of the
 step (independent sequences, no collective on the data path: the M=1 sweep
-does not shard); value = bytes all ranks moved / max-over-ranks time.
+does not shard); value = bytes all ranks moved / max-over-ranks time.  At
+N > 1 the line also carries kernels.lmhead_sharded: config 2's LM head split
+by vocabulary rows over the N ranks (q4k.sharded), timed as the max over
+ranks, and whether its merged candidates equal the unsharded head's.
 
 --impl reference times the CPU restatement of the reference's algorithm
 (oracle/, the reference itself is TypeScript + WGSL and cannot run here) on
@@ -248,6 +251,36 @@ def run_ours(args) -> None:
         del lm_graph
     lm_bytes = 226_492_416 + 4 * 1536 + 2052
 
+    # config 2 at N > 1: the LM head split by vocabulary rows over the ranks,
+    # one all-gather of 2 KB of candidates per rank, merged on every rank
+    sharded = None
+    if world > 1 and args.batch == 1:
+        from q4k.sharded import ShardedLMHead
+
+        head = ShardedLMHead(262144, 1536, 30.0, ctx=ctx)
+        w_shard = step.lm_head[head.row0:head.row0 + head.rows]
+        x0 = step.x_h[0]
+        for _ in range(args.warmup):
+            merged = head(w_shard, x0)
+        torch.cuda.synchronize()
+        step.plan().run()  # the unsharded head on the same input, for the check below
+        torch.cuda.synchronize()
+        same = bool(torch.equal(merged.cand_idx, step.sel.cand_idx) and torch.equal(merged.argmax, step.sel.argmax))
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            head(w_shard, x0)
+        b.record()
+        torch.cuda.synchronize()
+        sh_ms = max_over_ranks(a.elapsed_time(b) / reps, world, dev)
+        same = max_over_ranks(0.0 if same else 1.0, world, dev) == 0.0
+        sh_gbs = lm_bytes / (sh_ms / 1e3) / 1e9
+        sharded = {"ms": round(sh_ms, 4), "GB/s": round(sh_gbs, 1), "shards": world,
+                   "rows_per_rank": head.rows, "frac_of_peak": None,
+                   "collective": "all_gather 2 KB/rank (NCCL) + on-device merge",
+                   "matches_unsharded": same}
+
     # end to end through the public API: pinned host inputs in, results out
     x_host = [torch.empty_like(step.x_h, device="cpu").pin_memory(),
               torch.empty_like(step.x_attn, device="cpu").pin_memory()]
@@ -303,6 +336,9 @@ def run_ours(args) -> None:
     if lm_ms:
         kernels["lmhead_select"] = {"ms": round(lm_ms, 4), "GB/s": round(lm_bytes / (lm_ms / 1e3) / 1e9, 1),
                                     "frac_of_peak": round(lm_bytes / (lm_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
+    if sharded:
+        sharded["frac_of_peak"] = round(sharded["GB/s"] / (world * pk["hbm_gbs"]), 4)
+        kernels["lmhead_sharded"] = sharded
 
     cpu = None
     if world == 1 and not args.no_cpu:
