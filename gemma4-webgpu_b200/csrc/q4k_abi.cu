@@ -97,7 +97,7 @@ int q4k_create(int device, q4k_ctx** out) {
   ctx->device = device;
   ctx->sm_count = prop.multiProcessorCount;
   const size_t sel_bytes = 256 * sizeof(unsigned long long) + 256;
-  const size_t scale_bytes = 256;
+  const size_t scale_bytes = kCtxScaleSlots * sizeof(float);
   const size_t total = sel_bytes + scale_bytes + kCtxXfragBytes;
   if (cudaMalloc(&ctx->scratch, total) != cudaSuccess) {
     delete ctx;
@@ -149,7 +149,17 @@ int q4k_gemv(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, 
   int rc = check_matmul(ctx, w, x, y, M, N, batch);
   if (rc != Q4K_OK) return rc;
   if (M == 0) return Q4K_OK;
+  if (batch >= kGemmMinRows)
+    return run_gemm(ctx, static_cast<const uint8_t*>(w), x, y, M, N, batch, static_cast<cudaStream_t>(stream));
   return run_gemv(ctx, static_cast<const uint8_t*>(w), x, y, M, N, batch, static_cast<cudaStream_t>(stream));
+}
+
+int q4k_gemm(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
+             void* stream) {
+  int rc = check_matmul(ctx, w, x, y, M, N, T);
+  if (rc != Q4K_OK) return rc;
+  if (M == 0) return Q4K_OK;
+  return run_gemm(ctx, static_cast<const uint8_t*>(w), x, y, M, N, T, static_cast<cudaStream_t>(stream));
 }
 
 int q4k_matmul_quant(q4k_ctx* ctx, const float* input, const void* weight, float* output, uint32_t M, uint32_t N,

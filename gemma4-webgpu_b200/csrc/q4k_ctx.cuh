@@ -17,15 +17,17 @@ struct q4k_ctx {
   // Single-call scratch: prepared activations of one GEMV and their scales.
   uint2* xfrag = nullptr;
   size_t xfrag_cap = 0;  // bytes
-  float* inv_scale = nullptr;  // [kMaxTokens]
+  float* inv_scale = nullptr;  // [kCtxScaleSlots]: 1/scale per activation row
   void* scratch = nullptr;     // the one allocation holding all of the above
   char err[512] = {0};
 };
 
 namespace q4k {
 
-// Prepared-activation scratch a context allocates once (q4k_create).
+// Prepared-activation scratch a context allocates once (q4k_create), and the
+// activation rows one single call prepares at most (per-row scales).
 constexpr size_t kCtxXfragBytes = 16u << 20;
+constexpr uint32_t kCtxScaleSlots = 1024;
 
 inline int ctx_fail(q4k_ctx* ctx, int code, const char* fmt, ...) {
   if (ctx) {
@@ -48,5 +50,13 @@ inline int ctx_cuda(q4k_ctx* ctx, cudaError_t e, const char* what) {
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 inline uint32_t tiles_of(uint32_t M) { return (M + kTileRows - 1) / kTileRows; }
+
+// q4k_gemv hands requests of at least this many activation rows to the GEMM.
+constexpr uint32_t kGemmMinRows = 64;
+
+// Batched Q4_K GEMM (tcgen05, q4k_gemm.cu): y[t][m] = sum_k w16[m][k] x[t][k]
+// for T activation rows, on the context's scratch.
+int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
+             cudaStream_t s);
 
 }  // namespace q4k

@@ -29,8 +29,10 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "q4k_dequant.cuh"
 #include "q4k_device.cuh"
 #include "q4k_engine.cuh"
+#include "q4k_ptx.cuh"
 
 namespace q4k {
 namespace {
@@ -38,31 +40,6 @@ namespace {
 constexpr float kFloorE = -1e30f;
 
 // ---- small PTX helpers -------------------------------------------------------
-
-__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// d(f32) = a(f16) * b(f16) + c(f32), one rounding (sm_100 mixed-precision FMA).
-__device__ __forceinline__ float fma_h_h_f(uint16_t a, uint16_t b, float c) {
-  float d;
-  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
 
 __device__ __forceinline__ uint2 ldg_v2(const void* p) {
   uint2 r;
@@ -77,85 +54,6 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y));
-}
-
-// ---- per (row, super-block) constants ------------------------------------------
-
-// What one lane needs to dequantize its qs group c of one row's block:
-// sub-block j0 = 2c (low nibbles) and j1 = 2c+1 (high nibbles).
-struct RowConsts {
-  uint32_t sc0, nsc0;  // f16x2 (sc_j0, sc_j0), (-1024 sc_j0, ...)
-  uint32_t sc1, nsc1;  // f16x2 (sc_j1/16, ...), (-64 sc_j1, ...)
-  float ndm0, ndm1;    // -dmin*m_j0, -dmin*m_j1 (exact in f32)
-  uint16_t d;          // f16 bits of d
-};
-
-// sel: prmt selector picking the (j0, j1) bytes of a packed scale word into
-// bytes 0 and 2, zeros elsewhere (precomputed from c).
-__device__ __forceinline__ RowConsts row_consts(const uint4& h, uint32_t c, uint32_t sel) {
-  RowConsts r;
-  const ScaleMin4 sm = unpack_scale_min(h.y, h.z, h.w);
-  const uint32_t scw = c < 2 ? sm.sc_lo : sm.sc_hi;
-  const uint32_t mw = c < 2 ? sm.m_lo : sm.m_hi;
-  const uint32_t kMagic = 0x64006400u;  // f16x2 (1024, 1024)
-  const uint32_t sc = hsub2(prmt(scw, 0u, sel) | kMagic, kMagic);  // (sc_j0, sc_j1) f16x2, exact
-  const uint32_t mm = hsub2(prmt(mw, 0u, sel) | kMagic, kMagic);   // (m_j0, m_j1)
-  r.sc0 = prmt(sc, sc, 0x1010u);
-  r.nsc0 = hmul2(r.sc0, 0xE400E400u);                     // * (-1024)
-  const uint32_t s1 = prmt(sc, sc, 0x3232u);
-  r.sc1 = hmul2(s1, 0x2C002C00u);                         // * (1/16)
-  r.nsc1 = hmul2(s1, 0xD400D400u);                        // * (-64)
-  const uint16_t ndmin = (uint16_t)((h.x >> 16) ^ 0x8000u);  // -dmin
-  r.ndm0 = fma_h_h_f(ndmin, (uint16_t)(mm & 0xffffu), 0.0f);
-  r.ndm1 = fma_h_h_f(ndmin, (uint16_t)(mm >> 16), 0.0f);
-  r.d = (uint16_t)(h.x & 0xffffu);
-  return r;
-}
-
-// One 32-bit word of nibbles (bytes b0..b3 of one row) -> four f16x2 weight
-// pairs: lo02 = (w[b0 lo], w[b2 lo]), lo13 = (w[b1 lo], w[b3 lo]), and the
-// same for the high nibbles.  Low nibbles belong to sub-block j0, high to j1.
-// One PTX block, so the f16 halves feed the mixed FMAs without integer
-// extraction.
-struct WordPairs {
-  uint32_t lo02, lo13, hi02, hi13;
-};
-
-__device__ __forceinline__ WordPairs dequant_word(uint32_t v, const RowConsts& r) {
-  WordPairs o;
-  asm("{\n\t"
-      ".reg .b32 v8, m0, m1, m2, m3, p0, p1, p2, p3;\n\t"
-      ".reg .b16 a0, a1, b0, b1, c0, c1, d0, d1;\n\t"
-      ".reg .f32 e0, e1, e2, e3, e4, e5, e6, e7;\n\t"
-      "shr.b32 v8, %4, 8;\n\t"
-      "lop3.b32 m0, %4, 0x000F000F, 0x64006400, 0xEA;\n\t"   // (v & mask) | magic
-      "lop3.b32 m1, v8, 0x000F000F, 0x64006400, 0xEA;\n\t"
-      "lop3.b32 m2, %4, 0x00F000F0, 0x64006400, 0xEA;\n\t"
-      "lop3.b32 m3, v8, 0x00F000F0, 0x64006400, 0xEA;\n\t"
-      "fma.rn.f16x2 p0, m0, %5, %6;\n\t"                    // sc*q, exact
-      "fma.rn.f16x2 p1, m1, %5, %6;\n\t"
-      "fma.rn.f16x2 p2, m2, %7, %8;\n\t"
-      "fma.rn.f16x2 p3, m3, %7, %8;\n\t"
-      "mov.b32 {a0, a1}, p0;\n\t"
-      "mov.b32 {b0, b1}, p1;\n\t"
-      "mov.b32 {c0, c1}, p2;\n\t"
-      "mov.b32 {d0, d1}, p3;\n\t"
-      "fma.rn.f32.f16 e0, %11, a0, %9;\n\t"                 // d*sc*q - dmin*m, one rounding
-      "fma.rn.f32.f16 e1, %11, a1, %9;\n\t"
-      "fma.rn.f32.f16 e2, %11, b0, %9;\n\t"
-      "fma.rn.f32.f16 e3, %11, b1, %9;\n\t"
-      "fma.rn.f32.f16 e4, %11, c0, %10;\n\t"
-      "fma.rn.f32.f16 e5, %11, c1, %10;\n\t"
-      "fma.rn.f32.f16 e6, %11, d0, %10;\n\t"
-      "fma.rn.f32.f16 e7, %11, d1, %10;\n\t"
-      "cvt.rn.f16x2.f32 %0, e1, e0;\n\t"                     // f16 RNE, (lo, hi) halves
-      "cvt.rn.f16x2.f32 %1, e3, e2;\n\t"
-      "cvt.rn.f16x2.f32 %2, e5, e4;\n\t"
-      "cvt.rn.f16x2.f32 %3, e7, e6;\n\t"
-      "}"
-      : "=r"(o.lo02), "=r"(o.lo13), "=r"(o.hi02), "=r"(o.hi13)
-      : "r"(v), "r"(r.sc0), "r"(r.nsc0), "r"(r.sc1), "r"(r.nsc1), "f"(r.ndm0), "f"(r.ndm1), "h"(r.d));
-  return o;
 }
 
 __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int w) {
@@ -192,84 +90,6 @@ __device__ __forceinline__ void sel_unkey(unsigned long long k, float& v, uint32
   if (k & 1ull) b = 0x80000000u;
   v = __uint_as_float(b);
   idx = 0x7fffffffu - (uint32_t)((k >> 1) & 0x7fffffffu);
-}
-
-// ---- TMA bulk copies and mbarriers ---------------------------------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: gives up after kSpinLimit polls (each poll may itself block
-// for a short hardware-defined time), so a lost completion cannot hang the GPU.
-constexpr uint32_t kSpinLimit = 1u << 22;
-
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-
-// 2-D tile copy of a tensor-map box at (x, y) into shared memory, completing
-// on `bar` (no multicast).
-__device__ __forceinline__ void tma_tile_g2s(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y,
-                                             uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// 1-D bulk copy global -> shared through the TMA unit, completing on `bar`.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ uint4 lds128(const void* p) {
-  uint4 r;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_u32(p)));
-  return r;
-}
-
-__device__ __forceinline__ uint4 lds128_u32(uint32_t addr) {
-  uint4 r;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
-  return r;
-}
-
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 r;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(addr));
-  return r;
 }
 
 // ---- the engine kernel ----------------------------------------------------------
@@ -439,7 +259,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t g = lane >> 2, c = lane & 3u;
   // bytes (2(c&1), 2(c&1)+1) of a packed scale word -> bytes 0 and 2
-  const uint32_t bsel = (c & 1u) ? ((4u << 12) | (3u << 8) | (4u << 4) | 2u) : ((4u << 12) | (1u << 8) | (4u << 4) | 0u);
+  const uint32_t bsel = scale_sel(c);
   uint8_t* wsm = smem + warp * (kStages * kStageBytes);
   EngineTask* s_tasks = reinterpret_cast<EngineTask*>(smem + kWeightSmem);
   uint8_t* xsm = smem + kWeightSmem + kTaskSmem;

@@ -1,0 +1,416 @@
+// Batched Q4_K GEMM for sm_100a: Y[t][m] = sum_k w16[m][k] * x[t][k] for T
+// activation rows at once (prefill, or many independent sequences sharing
+// the weights).  The reference has only the one-row matmul_quant
+// (shaders/matmul_quant.wgsl:21-54); this is that operation for T >= 64 rows,
+// with the same weights w16 = f16_rne(f32(d*sc*q - dmin*m)) (src/gguf.ts:
+// 168-210 + 425-473).
+//
+// Here the work is a dense contraction, so it runs on the 5th-generation
+// tensor cores: one CTA computes a 256-row x 128-activation-row tile of Y
+// (64 activation rows when 128-row tiles would leave SMs idle) as two
+// 128-row blocks, each with tcgen05.mma (M = 128, N = 2 x activation rows,
+// K = 16 per instruction) into its own fp32 accumulator in tensor memory
+// (2 x 256 columns); both blocks read the same B tile, so the activation
+// operand is fetched once per 256 weight rows.  Per 64-wide K step:
+//   * the B operand, x split exactly into f16 hi + lo parts (two operand rows
+//     per activation row, scaled per row by a power of two), arrives by one
+//     TMA tensor copy in the 128-byte swizzled K-major layout;
+//   * the A operand, the 256 x 64 f16 weights, is dequantized by 8 warps
+//     from the Q4_K bytes (loaded four K steps ahead) into the same swizzled
+//     layout, computed before the stage is free and stored once it is;
+//   * one thread issues the 8 MMAs and commits them to the stage's "empty"
+//     barrier, which frees the stage for the producers.
+// Three operand stages are in flight.  The epilogue (8 warps: per accumulator one per
+// 32-lane quarter of tensor memory) reads the accumulators, adds each activation
+// row's hi and lo columns, undoes the scale and stores Y.  f16 x f16
+// products are exact and the hi/lo split carries x to ~2^-22, so the result
+// is the f32 dot product of the reference's f16 weights with x, up to fp32
+// accumulation order.
+//
+// Every mbarrier wait is bounded; on expiry the CTA records the failure in
+// the status word, lets its copies land and returns.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q4k_ctx.cuh"
+#include "q4k_dequant.cuh"
+#include "q4k_device.cuh"
+#include "q4k_ptx.cuh"
+
+namespace q4k {
+namespace {
+
+constexpr uint32_t kGMmaM = 128;                        // MMA M = TMEM lanes
+constexpr uint32_t kGHalves = 2;                        // MMA row blocks per CTA (one accumulator each)
+constexpr uint32_t kGRows = kGMmaM * kGHalves;          // weight rows per CTA tile
+constexpr uint32_t kGTokens = 128;                      // max activation rows per tile (MMA N = 2 per row)
+constexpr uint32_t kGK = 64;                            // K per stage: 128 bytes of f16 per operand row
+constexpr uint32_t kGStages = 3;
+constexpr uint32_t kGASub = kGMmaM * kGK * 2;           // 16 KB: one 128-row A block
+constexpr uint32_t kGABytes = kGHalves * kGASub;        // 32 KB
+constexpr uint32_t kGBBytes = 2 * kGTokens * kGK * 2;   // 32 KB
+constexpr uint32_t kGDqWarps = 8;                       // dequantizing warps, also the epilogue
+constexpr uint32_t kGThreads = (2 + kGDqWarps) * 32;    // + B-copy warp + MMA warp
+constexpr uint32_t kGAccCols = 2 * kGTokens;            // fp32 columns of one accumulator
+constexpr uint32_t kGTmemCols = kGHalves * kGAccCols;   // 512: all of tensor memory
+constexpr size_t kGSmem = 1024 + (size_t)kGStages * (kGABytes + kGBBytes);
+
+// UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzled
+// layout: 128-byte rows, 8-row groups 1024 bytes apart (stride offset), the
+// leading offset unused (1), descriptor version 1, layout type 2 (128B).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D fp32, A and B f16 and K-major, M = 128.
+__device__ __forceinline__ uint32_t idesc_f16(uint32_t n) {
+  return (1u << 4) | ((n >> 3) << 17) | ((kGMmaM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrives on `bar` once every MMA this thread issued before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this warp's 32 tensor-memory lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// K order inside the operand tiles.  The A producers write each 16-byte
+// chunk of 8 weights in the order dequant_word yields them, elements
+// (0, 2, 1, 3, 4, 6, 5, 7) of the chunk; the B operand (x) is stored in the
+// same order, so the contraction over K is unchanged.  Position p of a chunk
+// holds element chunk_elem(p) (bits 0 and 1 swapped).
+__host__ __device__ constexpr uint32_t chunk_elem(uint32_t p) {
+  return (p & ~3u) | ((p & 1u) << 1) | ((p >> 1) & 1u);
+}
+
+struct GemmArgs {
+  const uint8_t* w;        // Q4_K [M][N/256*144]
+  float* y;                // [T][M]
+  const float* inv_scale;  // [T]: 1/scale of each activation row
+  uint32_t M, N, T;
+  uint32_t tile_tokens;    // activation rows per CTA tile (64 or 128; the B map's box is 2x that)
+  uint32_t* status;        // bit 0: a bounded wait expired
+};
+
+// The raw Q4_K bytes one A-producer thread (one row) needs for one K step:
+// the super-block header and the step's 32-byte qs group.  The loads are
+// unconditional (the caller clamps the row, and steps past the end reload
+// the last one), so no register move waits on them before their step.
+struct RawGroup {
+  uint4 hd, q0, q1;
+};
+
+__device__ __forceinline__ RawGroup load_group(const uint8_t* wrow, uint32_t ks, uint32_t ksteps) {
+  RawGroup g;
+  const uint32_t k = ks < ksteps ? ks : ksteps - 1;
+  const uint8_t* b = wrow + (size_t)(k >> 2) * kBlockBytes;
+  g.hd = ldg_nc_v4(b);
+  g.q0 = ldg_nc_v4(b + 16 + 32 * (k & 3u));
+  g.q1 = ldg_nc_v4(b + 32 + 32 * (k & 3u));
+  return g;
+}
+
+// One tile row's 64 weights of a K step as the 8 swizzle chunks they occupy
+// (chunks 0-3: low nibbles, local k 0..31; chunks 4-7: high, k 32..63).
+struct RowChunks {
+  uint4 c[8];
+};
+
+__device__ __forceinline__ RowChunks dequant_group(const RawGroup& g, uint32_t j) {
+  RowChunks o;
+  const RowConsts rc = row_consts(g.hd, j, scale_sel(j));
+  const uint32_t wd[8] = {g.q0.x, g.q0.y, g.q0.z, g.q0.w, g.q1.x, g.q1.y, g.q1.z, g.q1.w};
+#pragma unroll
+  for (uint32_t c = 0; c < 4; ++c) {
+    const WordPairs p0 = dequant_word(wd[2 * c], rc), p1 = dequant_word(wd[2 * c + 1], rc);
+    o.c[c] = make_uint4(p0.lo02, p0.lo13, p1.lo02, p1.lo13);
+    o.c[4 + c] = make_uint4(p0.hi02, p0.hi13, p1.hi02, p1.hi13);
+  }
+  return o;
+}
+
+__global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap bmap, const GemmArgs a) {
+  extern __shared__ uint8_t g_smem_raw[];
+  // swizzled operand tiles start on 1024-byte boundaries
+  uint8_t* smem = g_smem_raw + ((1024u - (smem_u32(g_smem_raw) & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kGStages * kGABytes;
+  __shared__ uint64_t full_a[kGStages], full_b[kGStages], empty_bar[kGStages], done_bar;
+  __shared__ uint32_t s_tmem;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t row0 = blockIdx.x * kGRows, tok0 = blockIdx.y * a.tile_tokens;
+  const uint32_t ntok = min(a.tile_tokens, a.T - tok0);
+  const uint32_t b_bytes = 2 * a.tile_tokens * kGK * 2;  // one B box
+  const uint32_t n_mma = 2u * ((ntok + 7u) & ~7u);
+  const uint32_t ksteps = a.N / kGK;
+  bool failed = false;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kGStages; ++s) {
+      mbar_init(&full_a[s], kGDqWarps);
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kGTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    // B producer: one TMA box (2 x tile_tokens operand rows x 64 halves) per stage
+    if (lane == 0) {
+      uint32_t issued = 0;
+      for (uint32_t ks = 0; ks < ksteps; ++ks) {
+        const uint32_t s = ks % kGStages, use = ks / kGStages;
+        if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u)) {
+          failed = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_b[s], b_bytes);
+        tma_tile_g2s(sB + s * kGBBytes, &bmap, ks * kGK, 2 * tok0, &full_b[s]);
+        ++issued;
+      }
+      // every issued copy has landed before the CTA can exit
+      for (uint32_t ks = (issued > kGStages ? issued - kGStages : 0); ks < issued; ++ks)
+        if (!mbar_wait(&full_b[ks % kGStages], (ks / kGStages) & 1u)) failed = true;
+    }
+  } else if (warp == 1) {
+    // MMA issuer: per stage and 16-wide k slice, one 128 x n_mma x 16 MMA per
+    // row block, both reading the same B tile
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(n_mma);
+      for (uint32_t ks = 0; ks < ksteps; ++ks) {
+        const uint32_t s = ks % kGStages, ph = (ks / kGStages) & 1u;
+        if (!mbar_wait(&full_a[s], ph) || !mbar_wait(&full_b[s], ph)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + s * kGABytes), b0 = smem_u32(sB + s * kGBBytes);
+#pragma unroll
+        for (uint32_t kk = 0; kk < kGK / 16; ++kk) {
+          const uint64_t bd = smem_desc_sw128(b0 + 32 * kk);
+#pragma unroll
+          for (uint32_t hb = 0; hb < kGHalves; ++hb)
+            umma_f16(tmem + hb * kGAccCols, smem_desc_sw128(a0 + hb * kGASub + 32 * kk), bd, idesc, (ks | kk) != 0);
+        }
+        umma_commit(&empty_bar[s]);
+      }
+      umma_commit(&done_bar);  // the accumulators are final once every MMA above completes
+    }
+  } else {
+    // A producers: thread r (0..255) dequantizes tile row r's 64 weights of
+    // each K step (its 32-byte qs group, both nibbles: low -> local k 0..31
+    // of sub-block 2j, high -> local k 32..63 of sub-block 2j+1) into row
+    // r%128 of A block r/128.  The raw bytes of the next four steps are in
+    // flight in fixed registers, and a step's weights are computed before
+    // waiting for its stage to be free, so only the stores sit between the
+    // tensor core releasing a stage and refilling it.  A warp covers 32
+    // consecutive rows: the 8 lanes of each 16-byte store phase hit 8
+    // different swizzled chunks.
+    const uint32_t r = threadIdx.x - 64;
+    const uint32_t nb = a.N >> 8;
+    // rows past M read row M-1: their accumulator rows are never stored
+    const uint8_t* wrow = a.w + (size_t)min(row0 + r, a.M - 1) * nb * kBlockBytes;
+    const uint32_t rb = r & (kGMmaM - 1), sw = rb & 7u;  // 128-byte swizzle: chunk index ^ row%8
+    auto produce = [&](const RawGroup& g, uint32_t ks) -> bool {
+      const RowChunks ch = dequant_group(g, ks & 3u);
+      const uint32_t s = ks % kGStages, use = ks / kGStages;
+      if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u)) return false;
+      uint8_t* dst = sA + s * kGABytes + (r / kGMmaM) * kGASub + rb * 128;
+#pragma unroll
+      for (uint32_t c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = ch.c[c];
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_a[s]);
+      return true;
+    };
+    RawGroup ga = load_group(wrow, 0, ksteps), gb = load_group(wrow, 1, ksteps);
+    RawGroup gc = load_group(wrow, 2, ksteps), gd = load_group(wrow, 3, ksteps);
+    for (uint32_t ks = 0; ks < ksteps && !failed; ks += 4) {
+      if (!produce(ga, ks)) { failed = true; break; }
+      ga = load_group(wrow, ks + 4, ksteps);
+      if (ks + 1 >= ksteps) break;
+      if (!produce(gb, ks + 1)) { failed = true; break; }
+      gb = load_group(wrow, ks + 5, ksteps);
+      if (ks + 2 >= ksteps) break;
+      if (!produce(gc, ks + 2)) { failed = true; break; }
+      gc = load_group(wrow, ks + 6, ksteps);
+      if (ks + 3 >= ksteps) break;
+      if (!produce(gd, ks + 3)) { failed = true; break; }
+      gd = load_group(wrow, ks + 7, ksteps);
+    }
+    // epilogue: warp w reads accumulator (w-2)/4 (rows 128*that ..) in its
+    // tensor-memory lane quarter w%4
+    if (!mbar_wait(&done_bar, 0)) {
+      failed = true;
+    } else {
+      tc_fence_after();
+      const uint32_t q = warp & 3u, hb = (warp - 2) >> 2;
+      const uint32_t erow = row0 + hb * kGMmaM + 32 * q + lane;
+      for (uint32_t c0 = 0; c0 < n_mma; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((32u * q) << 16) + hb * kGAccCols + c0, v);
+#pragma unroll
+        for (uint32_t t = 0; t < 16; ++t) {
+          const uint32_t tok = tok0 + c0 / 2 + t;
+          if (tok < a.T && erow < a.M) a.y[(size_t)tok * a.M + erow] = (v[2 * t] + v[2 * t + 1]) * a.inv_scale[tok];
+        }
+      }
+    }
+  }
+  if (failed) atomicOr(a.status, 1u);
+  if (warp == 1 && lane == 0 && failed) mbar_wait(&done_bar, 0);  // MMAs still running must finish first
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGTmemCols) : "memory");
+  }
+}
+
+// x [T][N] f32 -> B operand [2T][N] f16: row 2t = hi(x_t * s_t), row 2t+1 =
+// lo = x_t*s_t - hi, s_t a power of two with max|x_t| * s_t < 2^15, each
+// 8-element chunk in the A tiles' K order (chunk_elem).
+__global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* x, __half* b, float* inv_scale, uint32_t N) {
+  __shared__ float s_red[8];
+  const uint32_t t = blockIdx.x;
+  const float* xr = x + (size_t)t * N;
+  float mx = 0.0f;
+  for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) mx = fmaxf(mx, fabsf(xr[k]));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = s_red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, s_red[i]);
+  int e = 0, sexp = 0;
+  if (mx > 0.0f && mx <= 3.402823466e38f) {
+    frexpf(mx, &e);
+    sexp = 15 - e;
+    sexp = sexp > 100 ? 100 : (sexp < -100 ? -100 : sexp);
+  }
+  const float s = ldexpf(1.0f, sexp);
+  if (threadIdx.x == 0) inv_scale[t] = ldexpf(1.0f, -sexp);
+  __half* hi = b + (size_t)(2 * t) * N;
+  __half* lo = hi + N;
+  for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) {
+    const float v = xr[(k & ~7u) | chunk_elem(k & 7u)] * s;  // the A tiles' K order
+    const __half hv = __float2half_rn(v);
+    hi[k] = hv;
+    lo[k] = __float2half_rn(v - __half2float(hv));
+  }
+}
+
+using EncodeTiledFn = decltype(&cuTensorMapEncodeTiled);
+
+EncodeTiledFn gemm_encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+}  // namespace
+
+int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
+             cudaStream_t s) {
+  EncodeTiledFn enc = gemm_encode_fn();
+  if (!enc) return ctx_fail(ctx, Q4K_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  static int attr_dev = -1;
+  if (attr_dev != ctx->device) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGSmem);
+    if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm shared-memory attribute");
+    attr_dev = ctx->device;
+  }
+  // activation rows per pass: the B operand (4 bytes per element per row)
+  // and the per-row scales fit the context scratch
+  uint32_t cap = (uint32_t)(ctx->xfrag_cap / (4ull * N));
+  cap = cap > kCtxScaleSlots ? kCtxScaleSlots : cap;
+  cap -= cap % kGTokens;
+  if (cap == 0) return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "N=%u too large for the GEMM scratch", N);
+  __half* bbuf = reinterpret_cast<__half*>(ctx->xfrag);
+  for (uint32_t done = 0; done < T;) {
+    const uint32_t tc = (T - done) < cap ? (T - done) : cap;
+    gemm_xprep_kernel<<<tc, 256, 0, s>>>(x + (size_t)done * N, bbuf, ctx->inv_scale, N);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm activation prep launch");
+    // 64-row activation tiles when 128-row ones leave SMs idle and the
+    // smaller tiles still fit in one wave
+    const uint32_t row_tiles = (M + kGRows - 1) / kGRows;
+    const uint32_t sms = (uint32_t)ctx->sm_count;
+    const uint32_t tile = (row_tiles * ((tc + kGTokens - 1) / kGTokens) < sms && row_tiles * ((tc + 63) / 64) <= sms)
+                              ? 64u : kGTokens;
+    CUtensorMap bmap;
+    const cuuint64_t dims[2] = {N, 2ull * tc};
+    const cuuint64_t strides[1] = {2ull * N};
+    const cuuint32_t box[2] = {kGK, 2 * tile};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bbuf, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return ctx_fail(ctx, Q4K_ERR_CUDA, "q4k_gemm activation tensor map");
+    GemmArgs ga;
+    ga.w = w;
+    ga.y = y + (size_t)done * M;
+    ga.inv_scale = ctx->inv_scale;
+    ga.M = M;
+    ga.N = N;
+    ga.T = tc;
+    ga.tile_tokens = tile;
+    ga.status = ctx->select.status;
+    const dim3 grid((M + kGRows - 1) / kGRows, (tc + ga.tile_tokens - 1) / ga.tile_tokens);
+    gemm_kernel<<<grid, kGThreads, kGSmem, s>>>(bmap, ga);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm launch");
+    done += tc;
+  }
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
+}  // namespace q4k

@@ -132,6 +132,25 @@ class Context:
         self._check(self._L.q4k_gemv(self._h, _ptr(weight), _ptr(x), _ptr(out), M, N, batch, _stream(stream)))
         return out
 
+    def gemm(self, weight: torch.Tensor, x: torch.Tensor, M: int, N: int, out: torch.Tensor | None = None,
+             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """y[t, m] for x [T, N] on the tensor cores (q4k_gemm): the batched
+        prefill form of matmul_quant for many activation rows."""
+        _need(weight, torch.uint8, "weight", self.device)
+        _need(x, torch.float32, "x", self.device)
+        if x.numel() % N:
+            raise ValueError(f"x has {x.numel()} elements, not a multiple of N={N}")
+        T = x.numel() // N
+        if weight.numel() < M * (N // QK_K) * BLOCK_BYTES:
+            raise ValueError("weight buffer smaller than M*N/256*144 bytes")
+        if out is None:
+            out = torch.empty((T, M), dtype=torch.float32, device=self.device)
+        _need(out, torch.float32, "out", self.device)
+        if out.numel() < T * M:
+            raise ValueError("out smaller than T*M")
+        self._check(self._L.q4k_gemm(self._h, _ptr(weight), _ptr(x), _ptr(out), M, N, T, _stream(stream)))
+        return out
+
     def dequant_f16(self, weight: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """The f16 weights the reference uploads (as int16 bit patterns)."""
         _need(weight, torch.uint8, "weight", self.device)

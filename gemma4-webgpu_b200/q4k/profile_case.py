@@ -3,13 +3,15 @@
     python gemma4-webgpu_b200/q4k/profile_case.py gemv [--batch B] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py lmhead [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py sweep [--layers L] [--reps R]
+    python gemma4-webgpu_b200/q4k/profile_case.py gemm [--batch T] [--reps R]
 
 `gemv` rotates over 35 distinct 6144x1536 Q4_K matrices (186 MB, more than
 the 126 MB L2, so each launch reads its weights from HBM); `lmhead` runs the
 fused 262144-row LM head (226 MB); `sweep` runs the decode-step plan of
 q4k.decode with L layers (default 8: 159 MB of layer weights plus a
-16384-row LM head).  A few hundred MB of device memory at most; the process
-exits after `reps` runs.
+16384-row LM head); `gemm` runs q4k_gemm on one 6144x1536 matrix with T
+activation rows (default 512).  A few hundred MB of device memory at most;
+the process exits after `reps` runs.
 """
 from __future__ import annotations
 
@@ -26,7 +28,7 @@ from q4k import Context, synth  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep"])
+    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep", "gemm"])
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=40)
@@ -40,6 +42,14 @@ def main() -> None:
         y = torch.empty((a.batch, M), dtype=torch.float32, device=dev)
         for r in range(a.reps):
             ctx.gemv(ws[r % len(ws)], x, M, N, out=y)
+    elif a.kernel == "gemm":
+        M, N = 6144, 1536
+        w = torch.from_numpy(synth.q4k_matrix(M, N, synth.seed_for(4, 1))).to(dev)
+        T = a.batch if a.batch > 1 else 512
+        x = torch.from_numpy(synth.activations(T, N, 2)).to(dev)
+        y = torch.empty((T, M), dtype=torch.float32, device=dev)
+        for _ in range(a.reps):
+            ctx.gemm(w, x, M, N, out=y)
     elif a.kernel == "sweep":
         from q4k.decode import DecodeStep, E2BShape
 

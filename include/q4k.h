@@ -90,9 +90,18 @@ Q4K_API int q4k_matmul_quant(q4k_ctx* ctx, const float* input, const void* weigh
 /* Batched form: y[b*M + m] = sum_k f32(w[m,k]) * x[b*N + k] for b < batch.
  * One weight stream serves all `batch` activation rows (the MR4 pipeline's
  * shared input read, shaders/matmul_quant_mr4.wgsl:107-115, turned around:
- * several inputs share one weight read).  batch >= 1. */
+ * several inputs share one weight read).  batch >= 1; batch >= 64 runs as
+ * q4k_gemm. */
 Q4K_API int q4k_gemv(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t batch,
              void* stream);
+
+/* Batched form for many activation rows (prefill, or T independent sequences
+ * sharing the weights): y[t*M + m] = sum_k f32(w[m,k]) * x[t*N + k], t < T,
+ * on the tensor cores (tcgen05).  The reference has only the one-row
+ * matmul_quant (shaders/matmul_quant.wgsl:21-54), run once per row; q4k_gemv
+ * hands batch >= 64 to this path.  Any T >= 1. */
+Q4K_API int q4k_gemm(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
+                     void* stream);
 
 /* The f16 weights the reference uploads for a Q4_K tensor (its
  * dequantizeQ4_K + f32ToF16Array + createF16Buffer, src/gguf.ts:168-210,

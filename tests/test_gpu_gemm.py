@@ -1,0 +1,69 @@
+"""GPU parity of the batched Q4_K GEMM (q4k_gemm, tcgen05) against the oracle.
+
+Same tolerance as the GEMV (per output 1e-3*|y_ref| + 1e-6*||w_row||*||x||,
+L2 relative 1e-4): the weights are the reference's f16 values exactly and x
+enters the tensor core split into exact f16 hi + lo parts, so only the fp32
+accumulation order differs from the oracle's.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from q4k import synth  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def to_dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def check(oracle, y, w, x, M, N):
+    y_ref = oracle.q4k_gemv(w, x, M, N)
+    _, wn = oracle.q4k_gemv_f64(w, x, M, N)
+    ok, ratio, l2 = oracle.tolerance_ok(y.reshape(y_ref.shape), y_ref, wn, x)
+    assert ok, f"per-output bound exceeded: worst ratio {ratio:.3g}"
+    assert l2 <= 1e-4, f"L2 relative {l2:.3g}"
+
+
+@pytest.mark.parametrize("M,N,T", [
+    (128, 256, 64), (256, 1536, 64), (300, 768, 100), (2048, 1536, 128), (1536, 2048, 200),
+    (130, 6144, 65), (1024, 1536, 512), (64, 512, 1), (200, 1024, 17),
+])
+def test_gemm_shapes(ctx, oracle, M, N, T):
+    w = synth.q4k_matrix(M, N, synth.seed_for(4, M + N))
+    x = synth.activations(T, N, synth.seed_for(4, 700 + T))
+    y = ctx.gemm(to_dev(w), to_dev(x), M, N).cpu().numpy()
+    check(oracle, y, w, x, M, N)
+
+
+def test_gemv_hands_large_batches_to_the_gemm(ctx, oracle):
+    M, N, T = 512, 1536, 96
+    w = synth.q4k_matrix(M, N, 91)
+    x = synth.activations(T, N, 92)
+    wd, xd = to_dev(w), to_dev(x)
+    y_gemv = ctx.gemv(wd, xd, M, N)
+    y_gemm = ctx.gemm(wd, xd, M, N)
+    torch.cuda.synchronize()
+    assert torch.equal(y_gemv.view(torch.int32), y_gemm.view(torch.int32))
+    check(oracle, y_gemv.cpu().numpy(), w, x, M, N)
+
+
+def test_gemm_repeatable_and_leaves_neighbours(ctx):
+    M, N, T = 384, 1536, 130
+    w = to_dev(synth.q4k_matrix(M, N, 93))
+    x = to_dev(synth.activations(T, N, 94))
+    canary = torch.full((T * M + 64,), 7.25, dtype=torch.float32, device=DEV)
+    y = canary[:T * M].view(T, M)
+    ctx.gemm(w, x, M, N, out=y)
+    first = y.clone()
+    ctx.gemm(w, x, M, N, out=y)
+    torch.cuda.synchronize()
+    assert torch.equal(first.view(torch.int32), y.view(torch.int32))
+    assert torch.all(canary[T * M:] == 7.25)
+    ctx.check()
