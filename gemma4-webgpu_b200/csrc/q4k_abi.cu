@@ -49,9 +49,15 @@ int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
       jl.inl.inv_scale = ctx->inv_scale;
       jl.inl.N = N;
       jl.inl.mode = 0;
-      e = launch_xprep(jl, b, s);
-      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv activation prep launch");
+      // the engine prepares the activation itself when it fits each CTA's cache
+      const bool prep = xfrag_bytes(N, b) <= engine_xcache_bytes(false);
+      if (!prep) {
+        e = launch_xprep(jl, b, s);
+        if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv activation prep launch");
+      }
       TaskList tl{};
+      tl.prep = prep ? 1u : 0u;
+      tl.inl_job = jl.inl;
       tl.n = 1;
       tl.inl.w = w;
       tl.inl.xfrag = ctx->xfrag;
@@ -233,9 +239,14 @@ int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint32_t V, u
   jl.inl.xfrag = ctx->xfrag;
   jl.inl.inv_scale = ctx->inv_scale;
   jl.inl.N = N;
-  e = launch_xprep(jl, 1, s);
-  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_lmhead_select activation prep launch");
+  const bool prep = xfrag_bytes(N, 1) <= engine_xcache_bytes(true);
+  if (!prep) {
+    e = launch_xprep(jl, 1, s);
+    if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_lmhead_select activation prep launch");
+  }
   TaskList tl{};
+  tl.prep = prep ? 1u : 0u;
+  tl.inl_job = jl.inl;
   tl.n = 1;
   tl.inl.w = static_cast<const uint8_t*>(w);
   tl.inl.xfrag = ctx->xfrag;

@@ -92,6 +92,94 @@ __device__ __forceinline__ void sel_unkey(unsigned long long k, float& v, uint32
   idx = 0x7fffffffu - (uint32_t)((k >> 1) & 0x7fffffffu);
 }
 
+// ---- activation preparation --------------------------------------------------------
+
+__device__ __forceinline__ float xjob_value(const XJob& J, uint64_t i) {
+  return J.mode ? gelu_mul_value(J.gate[i], J.up[i]) : J.x[i];
+}
+
+// Max |value| of token t of job J over a block of NW warps (stores the
+// gelu_mul output on the way when `store_act`); every thread gets the max.
+template <int NW>
+__device__ float job_token_max(const XJob& J, uint32_t t, bool store_act, float* s_red) {
+  const uint64_t base = (uint64_t)t * J.N;
+  float mx = 0.0f;
+  for (uint32_t k = threadIdx.x; k < J.N; k += NW * 32) {
+    const float v = xjob_value(J, base + k);
+    if (store_act) J.act[base + k] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = s_red[0];
+#pragma unroll
+  for (int i = 1; i < NW; ++i) mx = fmaxf(mx, s_red[i]);
+  __syncthreads();
+  return mx;
+}
+
+// Power-of-two scale s with max|x| * s < 2^15 (exponent clamped), as
+// (s, 1/s).
+__device__ __forceinline__ float2 token_scale(float mx) {
+  int e = 0, sexp = 0;
+  if (mx > 0.0f && mx <= 3.402823466e38f) {
+    frexpf(mx, &e);  // mx < 2^e
+    sexp = 15 - e;
+    sexp = sexp > 100 ? 100 : (sexp < -100 ? -100 : sexp);
+  }
+  return make_float2(ldexpf(1.0f, sexp), ldexpf(1.0f, -sexp));
+}
+
+// Token t of job J, scaled by s and split into f16 hi/lo, into the job's
+// fragment array `frags` (global or shared memory; layout of
+// q4k_engine.cuh), by a block of NW warps.
+template <int NW>
+__device__ void job_token_frags(const XJob& J, uint32_t t, uint32_t batch, float s, uint4* frags) {
+  const uint32_t nb = J.N >> 8;
+  const uint64_t base = (uint64_t)t * J.N;
+  const uint32_t nt = t >> 2, cols = 2u * min(4u, batch - 4u * nt);
+  const uint32_t col_hi = 2 * (t & 3u), col_lo = col_hi + 1;
+  uint4* tile = frags + (size_t)nt * nb * 256u;
+  for (uint32_t idx = threadIdx.x; idx < nb * 32; idx += NW * 32) {
+    const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+    // k-step w (low nibbles) starts at k0, k-step w+8 (high nibbles) at k0+32
+    const uint64_t k0 = base + 256u * b + 64u * c + 4u * w;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j] = xjob_value(J, k0 + j) * s;
+      v[4 + j] = xjob_value(J, k0 + 32 + j) * s;
+    }
+    uint16_t hh[8], hl[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __half h = __float2half_rn(v[j]);
+      hh[j] = __half_as_ushort(h);
+      hl[j] = __half_as_ushort(__float2half_rn(v[j] - __half2float(h)));
+    }
+    uint4* dst = tile + (size_t)(b * 8 + w) * cols * 4;
+    // per k-step: (b0, b1) = (x[k], x[k+2]), (b2, b3) = (x[k+1], x[k+3])
+    dst[4 * col_hi + c] = make_uint4(hh[0] | ((uint32_t)hh[2] << 16), hh[1] | ((uint32_t)hh[3] << 16),
+                                     hh[4] | ((uint32_t)hh[6] << 16), hh[5] | ((uint32_t)hh[7] << 16));
+    dst[4 * col_lo + c] = make_uint4(hl[0] | ((uint32_t)hl[2] << 16), hl[1] | ((uint32_t)hl[3] << 16),
+                                     hl[4] | ((uint32_t)hl[6] << 16), hl[5] | ((uint32_t)hl[7] << 16));
+  }
+}
+
+// One CTA per (job, token) for launches that do not prepare in the engine:
+// max|x| -> power-of-two scale -> hi/lo f16 split into the job's global
+// fragment array.
+__global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t batch) {
+  __shared__ float s_red[8];
+  const uint32_t job = blockIdx.x / batch, t = blockIdx.x % batch;
+  const XJob J = jl.dev ? jl.dev[job] : jl.inl;
+  const float mx = job_token_max<8>(J, t, J.mode && J.act, s_red);
+  const float2 sc = token_scale(mx);
+  if (threadIdx.x == 0) J.inv_scale[t] = sc.y;
+  job_token_frags<8>(J, t, batch, sc.x, reinterpret_cast<uint4*>(J.xfrag));
+}
+
 // ---- the engine kernel ----------------------------------------------------------
 
 constexpr int kStages = 2;        // stages in flight per warp
@@ -224,7 +312,7 @@ struct Hot {
 
 template <int NT>
 __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts, uint32_t ti, const CtaSched& xc,
-                                          uint32_t c, uint32_t batch) {
+                                          uint32_t c, uint32_t batch, const float (*s_inv)[kMaxTokens]) {
   const EngineTask T = task_get(tl, ts, ti);
   Hot<NT> h;
   h.M = T.M;
@@ -236,10 +324,15 @@ __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts,
   h.xfrag = T.xfrag;
   h.y = T.y;
   h.xs = 0xffffffffu;
+  uint32_t slot = 0;
   for (uint32_t j = 0; j < xc.nx; ++j)
-    if (xc.xptr[j] == T.xfrag) h.xs = xc.xoff[j];
+    if (xc.xptr[j] == T.xfrag) {
+      h.xs = xc.xoff[j];
+      slot = j;
+    }
 #pragma unroll
-  for (int n = 0; n < NT; ++n) h.inv[n] = T.inv_scale[min(4u * n + c, batch - 1)];
+  for (int n = 0; n < NT; ++n)
+    h.inv[n] = tl.prep ? s_inv[slot][min(4u * n + c, batch - 1)] : T.inv_scale[min(4u * n + c, batch - 1)];
   return h;
 }
 
@@ -255,6 +348,8 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   __shared__ CtaSched s_sched;
   __shared__ uint32_t s_next;                    // next unclaimed item of this CTA's range
   __shared__ uint32_t s_ring[kEngineWarps][4];   // items claimed by each warp, in order
+  __shared__ float s_inv[kMaxCachedX][kMaxTokens];  // prep: 1/scale of each cached activation and token
+  __shared__ float s_red[kEngineWarps];
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t g = lane >> 2, c = lane & 3u;
@@ -296,16 +391,21 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       s_sched.xoff[0] = 0;
       s_sched.xbytes[0] = xb;
       s_sched.xptr[0] = tl.inl.xfrag;
+      s_sched.xjob[0] = 0;
+      // an inline job's gelu_mul output is stored by CTA 0
+      s_sched.act_mask = (blockIdx.x == 0) ? 1u : 0u;
     }
     s_next = s_sched.c0;
     uint32_t bytes = s_sched.nt * (uint32_t)sizeof(EngineTask);
-    for (uint32_t j = 0; j < s_sched.nx; ++j) bytes += s_sched.xbytes[j];
+    if (!tl.prep)
+      for (uint32_t j = 0; j < s_sched.nx; ++j) bytes += s_sched.xbytes[j];
     mbar_arrive_expect_tx(&s_xbar, bytes);
     if (s_sched.nt) bulk_g2s(s_tasks, tl.dev + s_sched.t0, s_sched.nt * (uint32_t)sizeof(EngineTask), &s_xbar);
-    for (uint32_t j = 0; j < s_sched.nx; ++j)
-      for (uint32_t o = 0; o < s_sched.xbytes[j]; o += 32768u)
-        bulk_g2s(xsm + s_sched.xoff[j] + o, reinterpret_cast<const uint8_t*>(s_sched.xptr[j]) + o,
-                 min(32768u, s_sched.xbytes[j] - o), &s_xbar);
+    if (!tl.prep)
+      for (uint32_t j = 0; j < s_sched.nx; ++j)
+        for (uint32_t o = 0; o < s_sched.xbytes[j]; o += 32768u)
+          bulk_g2s(xsm + s_sched.xoff[j] + o, reinterpret_cast<const uint8_t*>(s_sched.xptr[j]) + o,
+                   min(32768u, s_sched.xbytes[j] - o), &s_xbar);
   }
   __syncthreads();
   const uint32_t c0 = s_sched.c0, c1 = s_sched.c1;
@@ -350,6 +450,22 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   }
   __syncwarp();
 
+  // Prepare-in-engine launches: with the first weight stages in flight, the
+  // whole CTA turns each cached job's activation (x, or gelu_mul(gate, up))
+  // into scaled hi/lo fragments in shared memory.
+  if (tl.prep) {
+    for (uint32_t j = 0; j < s_sched.nx; ++j) {
+      const XJob J = tl.dev ? tl.jobs[s_sched.xjob[j]] : tl.inl_job;
+      const bool store_act = J.mode && J.act && ((s_sched.act_mask >> j) & 1u);
+      for (uint32_t t = 0; t < batch; ++t) {
+        const float2 sc = token_scale(job_token_max<kEngineWarps>(J, t, store_act, s_red));
+        if (threadIdx.x == 0) s_inv[j][t] = sc.y;
+        job_token_frags<kEngineWarps>(J, t, batch, sc.x, reinterpret_cast<uint4*>(xsm + s_sched.xoff[j]));
+      }
+    }
+    __syncthreads();
+  }
+
   // B-fragment column of this lane in each n-tile: any stored column serves,
   // results of columns past the batch are never read.
   const uint32_t cols_last = COLS > 0 ? (uint32_t)COLS : 2u * (batch - 4u * (NT - 1));
@@ -365,8 +481,8 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   uint32_t consumed = 0;
   uint32_t item = timed_out ? c1 : ring[0];
   uint32_t ti = t_first;
-  Hot<NT> H = hot_of<NT>(tl, ts, ti, s_sched, c, batch);
-  while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch);
+  Hot<NT> H = hot_of<NT>(tl, ts, ti, s_sched, c, batch, s_inv);
+  while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch, s_inv);
   uint32_t b = 0, k = 0;
 
   float acc[NT][2][4];
@@ -460,7 +576,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     ++consumed;
     __syncwarp();
     item = ring[consumed & 3u];
-    while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch);
+    while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch, s_inv);
   }
 
   if (timed_out) {
@@ -526,71 +642,6 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   if (threadIdx.x == 0) {
     *S.argmax = f_i[0];
     *sel.counter = 0u;
-  }
-}
-
-// ---- activation preparation --------------------------------------------------------
-
-__device__ __forceinline__ float xjob_value(const XJob& J, uint64_t i) {
-  return J.mode ? gelu_mul_value(J.gate[i], J.up[i]) : J.x[i];
-}
-
-// One CTA per (job, token): max|x| -> power-of-two scale -> hi/lo f16 split in
-// B-fragment order (compact layout of q4k_engine.cuh).
-__global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t batch) {
-  __shared__ float s_red[8];
-  const uint32_t job = blockIdx.x / batch, t = blockIdx.x % batch;
-  const XJob J = jl.dev ? jl.dev[job] : jl.inl;
-  const uint32_t N = J.N, nb = N >> 8;
-  const uint64_t base = (uint64_t)t * N;
-
-  float mx = 0.0f;
-  for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) {
-    const float v = xjob_value(J, base + k);
-    if (J.mode && J.act) J.act[base + k] = v;
-    mx = fmaxf(mx, fabsf(v));
-  }
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  mx = s_red[0];
-  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, s_red[i]);
-  int e = 0;
-  int sexp = 0;
-  if (mx > 0.0f && mx <= 3.402823466e38f) {
-    frexpf(mx, &e);  // mx < 2^e
-    sexp = 15 - e;
-    sexp = sexp > 100 ? 100 : (sexp < -100 ? -100 : sexp);
-  }
-  const float s = ldexpf(1.0f, sexp);
-  if (threadIdx.x == 0) J.inv_scale[t] = ldexpf(1.0f, -sexp);
-
-  const uint32_t nt = t >> 2, cols = 2u * min(4u, batch - 4u * nt);
-  const uint32_t col_hi = 2 * (t & 3u), col_lo = col_hi + 1;
-  uint4* tile = reinterpret_cast<uint4*>(J.xfrag) + (size_t)nt * nb * 256u;
-  for (uint32_t idx = threadIdx.x; idx < nb * 32; idx += blockDim.x) {
-    const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
-    // k-step w (low nibbles) starts at k0, k-step w+8 (high nibbles) at k0+32
-    const uint64_t k0 = base + 256u * b + 64u * c + 4u * w;
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[j] = xjob_value(J, k0 + j) * s;
-      v[4 + j] = xjob_value(J, k0 + 32 + j) * s;
-    }
-    uint16_t hh[8], hl[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const __half h = __float2half_rn(v[j]);
-      hh[j] = __half_as_ushort(h);
-      hl[j] = __half_as_ushort(__float2half_rn(v[j] - __half2float(h)));
-    }
-    uint4* dst = tile + (size_t)(b * 8 + w) * cols * 4;
-    // per k-step: (b0, b1) = (x[k], x[k+2]), (b2, b3) = (x[k+1], x[k+3])
-    dst[4 * col_hi + c] = make_uint4(hh[0] | ((uint32_t)hh[2] << 16), hh[1] | ((uint32_t)hh[3] << 16),
-                                     hh[4] | ((uint32_t)hh[6] << 16), hh[5] | ((uint32_t)hh[7] << 16));
-    dst[4 * col_lo + c] = make_uint4(hl[0] | ((uint32_t)hl[2] << 16), hl[1] | ((uint32_t)hl[3] << 16),
-                                     hl[4] | ((uint32_t)hl[6] << 16), hl[5] | ((uint32_t)hl[7] << 16));
   }
 }
 
@@ -722,12 +773,26 @@ void engine_schedule(const EngineTask* tasks, uint32_t n, uint32_t total_cost, u
       const uint32_t bytes = (uint32_t)xfrag_bytes(tasks[i].N, batch);
       if (seen || S.nx == (uint32_t)kMaxCachedX || used + bytes > xcache_cap) continue;
       S.xptr[S.nx] = tasks[i].xfrag;
+      S.xjob[S.nx] = tasks[i].aux;  // the task's preparation job
       S.xoff[S.nx] = used;
       S.xbytes[S.nx] = bytes;
       used += bytes;
       ++S.nx;
     }
   }
+}
+
+bool schedule_covers_tasks(const EngineTask* tasks, uint32_t n, const CtaSched* sched, uint32_t grid) {
+  for (uint32_t b = 0; b < grid; ++b) {
+    const CtaSched& S = sched[b];
+    for (uint32_t i = 0; i < n; ++i) {
+      if (tasks[i].item_end <= S.c0 || tasks[i].item_begin >= S.c1) continue;
+      bool found = false;
+      for (uint32_t j = 0; j < S.nx; ++j) found |= (S.xptr[j] == tasks[i].xfrag);
+      if (!found) return false;
+    }
+  }
+  return true;
 }
 
 cudaError_t launch_engine(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, bool has_select,

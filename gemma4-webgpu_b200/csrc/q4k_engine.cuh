@@ -60,7 +60,9 @@ struct CtaSched {
   uint32_t nx;       // activations to stage
   uint32_t xoff[kMaxCachedX];
   uint32_t xbytes[kMaxCachedX];
-  const uint2* xptr[kMaxCachedX];
+  const uint2* xptr[kMaxCachedX];  // the tasks' xfrag pointer each slot stands for
+  uint32_t xjob[kMaxCachedX];      // prepare-in-engine launches: the job of each slot
+  uint32_t act_mask;               // bit j: this CTA stores slot j's gelu_mul output
 };
 
 // One activation to prepare: mode 0 reads x, mode 1 computes
@@ -78,10 +80,17 @@ struct XJob {
 
 // Tasks / jobs either live in device memory (plans) or are passed inline as
 // kernel parameters (single calls).
+// prep != 0: every CTA prepares the activations of its task range itself,
+// straight into its shared-memory cache (from `jobs`, or `inl_job` for an
+// inline task), so no preparation launch precedes the engine; the host
+// chooses this only when every task's activation fits each CTA's cache.
 struct TaskList {
   const EngineTask* dev;
   const CtaSched* sched;  // per-CTA schedule of a device task list (grid entries)
+  const XJob* jobs;       // device job table (prep with a device task list)
   EngineTask inl;
+  XJob inl_job;
+  uint32_t prep;
   uint32_t n;
   uint32_t total_items;
   uint32_t total_cost;  // sum of items * (N/256): the super-blocks of the launch
@@ -111,6 +120,10 @@ uint32_t engine_xcache_bytes(bool has_select);
 // equal shares of super-blocks per CTA, and what each CTA stages.
 void engine_schedule(const EngineTask* tasks, uint32_t n, uint32_t total_cost, uint32_t total_items,
                      uint32_t batch, uint32_t grid, uint32_t xcache_bytes, CtaSched* out);
+
+// Whether every CTA of a schedule caches the activation of every task in its
+// range (the condition for preparing activations in the engine).
+bool schedule_covers_tasks(const EngineTask* tasks, uint32_t n, const CtaSched* sched, uint32_t grid);
 
 cudaError_t launch_xprep(const JobList& jobs, uint32_t batch, cudaStream_t s);
 // `map`: the weight map of an inline task (tasks.dev == null); ignored for

@@ -92,8 +92,11 @@ extern "C" int q4k_lmhead_select_static(const void* w, const float* x, uint32_t 
   jl.inl.xfrag = xfrag;
   jl.inl.inv_scale = inv_scale;
   jl.inl.N = N;
-  if (launch_xprep(jl, 1, s) != cudaSuccess) return Q4K_ERR_CUDA;
+  const bool prep = xfrag_bytes(N, 1) <= engine_xcache_bytes(true);
+  if (!prep && launch_xprep(jl, 1, s) != cudaSuccess) return Q4K_ERR_CUDA;
   TaskList tl{};
+  tl.prep = prep ? 1u : 0u;
+  tl.inl_job = jl.inl;
   tl.n = 1;
   tl.inl.w = static_cast<const uint8_t*>(w);
   tl.inl.xfrag = xfrag;

@@ -55,6 +55,7 @@ struct Stage {
   XJob* jobs_dev = nullptr;
   CtaSched* sched_dev = nullptr;
   uint32_t n_tasks = 0, n_jobs = 0, total_items = 0, total_cost = 0, grid = 0, select_task = 0;
+  bool prep = false;  // activations prepared inside the engine launch (no preparation launch)
 };
 
 }  // namespace
@@ -277,8 +278,7 @@ int q4k_plan_commit(q4k_plan* p) {
     for (EngineTask& t : tasks[s]) {
       const XJob& J = jobs[t.aux];
       t.xfrag = J.xfrag;
-      t.inv_scale = J.inv_scale;
-      t.aux = 0;
+      t.inv_scale = J.inv_scale;  // t.aux keeps the job index (the CTA schedules name jobs by it)
     }
     // one weight tensor map per task, in the plan's memory
     st.maps_dev = reinterpret_cast<CUtensorMap*>(cur);
@@ -304,6 +304,22 @@ int q4k_plan_commit(q4k_plan* p) {
       std::vector<CtaSched> sched(st.grid);
       engine_schedule(tasks[s].data(), st.n_tasks, st.total_cost, st.total_items, B, st.grid,
                       engine_xcache_bytes(!st.selects.empty()), sched.data());
+      // Prepare activations inside the engine when every CTA caches every
+      // activation it uses and each stored gelu_mul output has a CTA that
+      // prepares it (the first such CTA stores it).
+      st.prep = schedule_covers_tasks(tasks[s].data(), st.n_tasks, sched.data(), st.grid);
+      for (uint32_t j = 0; st.prep && j < st.n_jobs; ++j) {
+        if (!(jobs[j].mode && jobs[j].act)) continue;
+        bool owned = false;
+        for (uint32_t b = 0; b < st.grid && !owned; ++b)
+          for (uint32_t k = 0; k < sched[b].nx; ++k)
+            if (sched[b].xjob[k] == j) {
+              sched[b].act_mask |= 1u << k;
+              owned = true;
+              break;
+            }
+        if (!owned) st.prep = false;
+      }
       e = cudaMemcpy(st.sched_dev, sched.data(), sizeof(CtaSched) * st.grid, cudaMemcpyHostToDevice);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
     }
@@ -327,7 +343,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
   if (!p->committed) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan not committed");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   for (const Stage& st : p->stages) {
-    if (st.n_jobs) {
+    if (st.n_jobs && !st.prep) {
       JobList jl{};
       jl.dev = st.jobs_dev;
       jl.n = st.n_jobs;
@@ -343,6 +359,8 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
       tl.total_items = st.total_items;
       tl.total_cost = st.total_cost;
       tl.select_task = st.select_task;
+      tl.jobs = st.jobs_dev;
+      tl.prep = st.prep ? 1u : 0u;
       cudaError_t e = launch_engine(tl, kNoMap, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
     }
@@ -354,7 +372,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
 int q4k_plan_launches(const q4k_plan* p) {
   if (!p || !p->committed) return -1;
   int n = 0;
-  for (const Stage& st : p->stages) n += (st.n_jobs ? 1 : 0) + (st.total_items ? 1 : 0);
+  for (const Stage& st : p->stages) n += (st.n_jobs && !st.prep ? 1 : 0) + (st.total_items ? 1 : 0);
   return n;
 }
 

@@ -265,7 +265,8 @@ def test_plan_matches_single_calls(ctx, oracle):
         p.gelu_mul(1, g, u, act)
         p.gemv(1, wd, act, y, H, I)
         p.commit()
-        assert p.launches() == 4
+        # each stage's activations fit every CTA's cache: one engine launch per stage
+        assert p.launches() == 2
         p.run()
         torch.cuda.synchronize()
         g1 = ctx.gemv(wg, x, I, H)
