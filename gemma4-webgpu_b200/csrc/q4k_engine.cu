@@ -167,6 +167,87 @@ __device__ void job_token_frags(const XJob& J, uint32_t t, uint32_t batch, float
   }
 }
 
+// Token t of job J in one pass when its 8-element groups fit kPrepGroups
+// per thread: each thread evaluates its groups once (x, or gelu_mul of gate
+// and up, stored to J.act when `store_act`), keeps them in registers for the
+// block-wide max, then writes their scaled hi/lo fragments.  Returns 1/s.
+// Falls back to two passes (values evaluated twice) for longer rows.
+constexpr uint32_t kPrepGroups = 4;
+
+template <int NW>
+__device__ float job_token_prep(const XJob& J, uint32_t t, uint32_t batch, bool store_act, uint4* frags,
+                                float* s_red) {
+  const uint32_t nb = J.N >> 8, groups = nb * 32;
+  if (groups > kPrepGroups * NW * 32) {
+    const float2 sc = token_scale(job_token_max<NW>(J, t, store_act, s_red));
+    job_token_frags<NW>(J, t, batch, sc.x, frags);
+    return sc.y;
+  }
+  const uint64_t base = (uint64_t)t * J.N;
+  float v[kPrepGroups][8];
+  float mx = 0.0f;
+#pragma unroll
+  for (uint32_t i = 0; i < kPrepGroups; ++i) {
+    const uint32_t idx = threadIdx.x + i * NW * 32;
+    if (idx < groups) {
+      const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+      const uint64_t k0 = base + 256u * b + 64u * c + 4u * w;  // elements k0..k0+3 and k0+32..k0+35
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint64_t k = k0 + 32u * h;
+        float4 q;
+        if (J.mode) {
+          const float4 g = *reinterpret_cast<const float4*>(J.gate + k);
+          const float4 u = *reinterpret_cast<const float4*>(J.up + k);
+          q = make_float4(gelu_mul_value(g.x, u.x), gelu_mul_value(g.y, u.y), gelu_mul_value(g.z, u.z),
+                          gelu_mul_value(g.w, u.w));
+          if (store_act) *reinterpret_cast<float4*>(J.act + k) = q;
+        } else {
+          q = *reinterpret_cast<const float4*>(J.x + k);
+        }
+        v[i][4 * h + 0] = q.x;
+        v[i][4 * h + 1] = q.y;
+        v[i][4 * h + 2] = q.z;
+        v[i][4 * h + 3] = q.w;
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = s_red[0];
+#pragma unroll
+  for (int i = 1; i < NW; ++i) mx = fmaxf(mx, s_red[i]);
+  __syncthreads();
+  const float2 sc = token_scale(mx);
+  const uint32_t nt = t >> 2, cols = 2u * min(4u, batch - 4u * nt);
+  const uint32_t col_hi = 2 * (t & 3u), col_lo = col_hi + 1;
+  uint4* tile = frags + (size_t)nt * nb * 256u;
+#pragma unroll
+  for (uint32_t i = 0; i < kPrepGroups; ++i) {
+    const uint32_t idx = threadIdx.x + i * NW * 32;
+    if (idx < groups) {
+      const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+      uint16_t hh[8], hl[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float x = v[i][j] * sc.x;
+        const __half h = __float2half_rn(x);
+        hh[j] = __half_as_ushort(h);
+        hl[j] = __half_as_ushort(__float2half_rn(x - __half2float(h)));
+      }
+      uint4* dst = tile + (size_t)(b * 8 + w) * cols * 4;
+      // per k-step: (b0, b1) = (x[k], x[k+2]), (b2, b3) = (x[k+1], x[k+3])
+      dst[4 * col_hi + c] = make_uint4(hh[0] | ((uint32_t)hh[2] << 16), hh[1] | ((uint32_t)hh[3] << 16),
+                                       hh[4] | ((uint32_t)hh[6] << 16), hh[5] | ((uint32_t)hh[7] << 16));
+      dst[4 * col_lo + c] = make_uint4(hl[0] | ((uint32_t)hl[2] << 16), hl[1] | ((uint32_t)hl[3] << 16),
+                                       hl[4] | ((uint32_t)hl[6] << 16), hl[5] | ((uint32_t)hl[7] << 16));
+    }
+  }
+  return sc.y;
+}
+
 // One CTA per (job, token) for launches that do not prepare in the engine:
 // max|x| -> power-of-two scale -> hi/lo f16 split into the job's global
 // fragment array.
@@ -174,10 +255,8 @@ __global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t b
   __shared__ float s_red[8];
   const uint32_t job = blockIdx.x / batch, t = blockIdx.x % batch;
   const XJob J = jl.dev ? jl.dev[job] : jl.inl;
-  const float mx = job_token_max<8>(J, t, J.mode && J.act, s_red);
-  const float2 sc = token_scale(mx);
-  if (threadIdx.x == 0) J.inv_scale[t] = sc.y;
-  job_token_frags<8>(J, t, batch, sc.x, reinterpret_cast<uint4*>(J.xfrag));
+  const float inv = job_token_prep<8>(J, t, batch, J.mode && J.act, reinterpret_cast<uint4*>(J.xfrag), s_red);
+  if (threadIdx.x == 0) J.inv_scale[t] = inv;
 }
 
 // ---- the engine kernel ----------------------------------------------------------
@@ -458,9 +537,9 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       const XJob J = tl.dev ? tl.jobs[s_sched.xjob[j]] : tl.inl_job;
       const bool store_act = J.mode && J.act && ((s_sched.act_mask >> j) & 1u);
       for (uint32_t t = 0; t < batch; ++t) {
-        const float2 sc = token_scale(job_token_max<kEngineWarps>(J, t, store_act, s_red));
-        if (threadIdx.x == 0) s_inv[j][t] = sc.y;
-        job_token_frags<kEngineWarps>(J, t, batch, sc.x, reinterpret_cast<uint4*>(xsm + s_sched.xoff[j]));
+        const float inv = job_token_prep<kEngineWarps>(J, t, batch, store_act,
+                                                       reinterpret_cast<uint4*>(xsm + s_sched.xoff[j]), s_red);
+        if (threadIdx.x == 0) s_inv[j][t] = inv;
       }
     }
     __syncthreads();

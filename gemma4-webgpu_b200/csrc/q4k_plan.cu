@@ -132,6 +132,8 @@ int q4k_plan_gelu_mul(q4k_plan* p, uint32_t stage, const float* gate, const floa
   if (!gate || !up || !act) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
   if (n == 0 || n % Q4K_QK != 0)
     return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan gelu_mul size %u must be a multiple of 256", n);
+  if (!aligned16(gate) || !aligned16(up) || !aligned16(act))
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "gelu_mul pointers must be 16-byte aligned");
   Stage* st = stage_of(p, stage);
   if (!st) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "stage %u out of range", stage);
   st->gelus.push_back({gate, up, act, n});
