@@ -251,6 +251,17 @@ def run_ours(args) -> None:
         del lm_graph
     lm_bytes = 226_492_416 + 4 * 1536 + 2052
 
+    # config 3 at M = 4 (the MR4 kernel's shape): the same sweep for 4
+    # activation rows per step, on the same resident weights
+    sweep4 = None
+    if args.batch == 1:
+        step4 = DecodeStep(ctx, E2BShape(), batch=4, share_weights_with=step)
+        s4_ms, s4_graph = time_body(step4.run, reps)
+        sweep4 = {"ms": round(s4_ms, 4), "tokens_per_s": round(world * 4 / (s4_ms / 1e3), 1),
+                  "GB/s": round(step4.algorithmic_bytes() / (s4_ms / 1e3) / 1e9, 1),
+                  "launches": step4.launches_per_step()}
+        del s4_graph, step4
+
     # config 2 at N > 1: the LM head split by vocabulary rows over the ranks,
     # one all-gather of 2 KB of candidates per rank, merged on every rank
     sharded = None
@@ -336,6 +347,8 @@ def run_ours(args) -> None:
     if lm_ms:
         kernels["lmhead_select"] = {"ms": round(lm_ms, 4), "GB/s": round(lm_bytes / (lm_ms / 1e3) / 1e9, 1),
                                     "frac_of_peak": round(lm_bytes / (lm_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
+    if sweep4:
+        kernels["sweep_batch4"] = sweep4
     if sharded:
         sharded["frac_of_peak"] = round(sharded["GB/s"] / (world * pk["hbm_gbs"]), 4)
         kernels["lmhead_sharded"] = sharded

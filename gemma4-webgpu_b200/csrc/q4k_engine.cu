@@ -290,10 +290,18 @@ __device__ __forceinline__ EngineTask task_get(const TaskList& tl, const TaskSrc
 
 // Where a warp's copy engine stands: work item, super-block and its task.
 struct Cursor {
-  uint32_t item, b, ti;
+  uint32_t item, b, b_hi, ti;
   const CUtensorMap* map;
   uint32_t tile_bytes, nb, item_begin, item_end;
 };
+
+// The item's super-block range for this warp: all of the row, or quarter q
+// of it when the launch splits each tile's K range over KS warps.
+__device__ __forceinline__ void cursor_range(Cursor& cu, uint32_t q, uint32_t ks) {
+  const uint32_t part = cu.nb / ks;
+  cu.b = q * part;
+  cu.b_hi = cu.b + part;
+}
 
 __device__ __forceinline__ void cursor_task(Cursor& cu, const TaskList& tl, const TaskSrc& ts) {
   const EngineTask T = task_get(tl, ts, cu.ti);
@@ -311,9 +319,9 @@ __device__ __forceinline__ void cursor_seek(Cursor& cu, const TaskList& tl, cons
   }
 }
 
-// Super-blocks of the cursor's stage: up to kBlocksPerStage, not past the row.
+// Super-blocks of the cursor's stage: up to kBlocksPerStage, not past the range.
 __device__ __forceinline__ uint32_t cursor_blocks(const Cursor& cu) {
-  return min((uint32_t)kBlocksPerStage, cu.nb - cu.b);
+  return min((uint32_t)kBlocksPerStage, cu.b_hi - cu.b);
 }
 
 // Lane 0 copies the tile's super-blocks b, b+1 of its 16 rows (one map box,
@@ -415,7 +423,7 @@ __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts,
   return h;
 }
 
-template <int NT, int COLS>
+template <int NT, int COLS, int KS>
 __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     engine_kernel(const TaskList tl, const __grid_constant__ CUtensorMap wmap, uint32_t batch, int has_select,
                   SelectScratch sel, uint32_t xcache_cap) {
@@ -429,6 +437,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   __shared__ uint32_t s_ring[kEngineWarps][4];   // items claimed by each warp, in order
   __shared__ float s_inv[kMaxCachedX][kMaxTokens];  // prep: 1/scale of each cached activation and token
   __shared__ float s_red[kEngineWarps];
+  __shared__ uint64_t s_gbar[kEngineWarps];          // K-split launches: one per tile group
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t g = lane >> 2, c = lane & 3u;
@@ -445,6 +454,13 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   if (lane == 0)
     for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
   if (threadIdx.x == 0) mbar_init(&s_xbar, 1);
+  // K-split launches (tl.ksplit = KS > 1): the KS warps of a group take the
+  // same tiles, each a 1/KS slice of the row's super-blocks, and add their
+  // partial sums through shared memory; tiles go to groups in turn.
+  constexpr uint32_t ks_n = KS;  // == tl.ksplit (1: no split)
+  const uint32_t gq = warp % ks_n, grp = warp / ks_n, ngrp = kEngineWarps / ks_n;
+  if (threadIdx.x == 0 && ks_n > 1)
+    for (uint32_t i = 0; i < ngrp; ++i) mbar_init(&s_gbar[i], ks_n);
   if (has_select)
     for (uint32_t r = lane; r < 256; r += 32) {
       s_bv[r] = kFloorE;
@@ -499,11 +515,12 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   // Items are claimed from the CTA's range by the copy cursor (a shared
   // counter, so warps that finish early take more) and recorded in the
   // warp's ring, which the math follows in the same order.
+  // (K-split launches: a group's tiles are fixed, c0 + grp + ngrp*i.)
   uint32_t claims = 0;
   auto claim = [&]() -> uint32_t {
     uint32_t it = 0;
     if (lane == 0) {
-      it = atomicAdd(&s_next, 1u);
+      it = ks_n > 1 ? c0 + grp + ngrp * claims : atomicAdd(&s_next, 1u);
       ring[claims & 3u] = it;
     }
     ++claims;
@@ -511,19 +528,19 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   };
 
   Cursor F;
-  F.b = 0;
   F.ti = t_first;
   F.item = timed_out ? c1 : claim();
   cursor_task(F, tl, ts);
   cursor_seek(F, tl, ts, c1);
+  cursor_range(F, gq, ks_n);
   uint32_t issued = 0;
   for (int st = 0; st < kStages && F.item < c1; ++st) {
     issue_stage(F, wsm + st * kStageBytes, &bars[st], lane);
     F.b += cursor_blocks(F);
-    if (F.b == F.nb) {
-      F.b = 0;
+    if (F.b == F.b_hi) {
       F.item = claim();
       cursor_seek(F, tl, ts, c1);
+      cursor_range(F, gq, ks_n);
     }
     ++issued;
   }
@@ -562,7 +579,8 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   uint32_t ti = t_first;
   Hot<NT> H = hot_of<NT>(tl, ts, ti, s_sched, c, batch, s_inv);
   while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch, s_inv);
-  uint32_t b = 0, k = 0;
+  uint32_t b = gq * (H.nb / ks_n), b_hi = b + H.nb / ks_n, k = 0, tiles = 0;
+  float* s_part = reinterpret_cast<float*>(xsm + xcache_cap);  // K-split partial sums
 
   float acc[NT][2][4];
 #pragma unroll
@@ -576,7 +594,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       timed_out = true;
       break;
     }
-    const uint32_t nblk = min((uint32_t)kBlocksPerStage, H.nb - b);
+    const uint32_t nblk = min((uint32_t)kBlocksPerStage, b_hi - b);
     const uint8_t* stg = wsm + slot * kStageBytes;
     const uint32_t rs = H.tile_bytes;
     const bool sx = H.xs != 0xffffffffu;
@@ -590,10 +608,10 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
         if (F.item < c1) {
           issue_stage(F, wsm + slot * kStageBytes, &bars[slot], lane);
           F.b += cursor_blocks(F);
-          if (F.b == F.nb) {
-            F.b = 0;
+          if (F.b == F.b_hi) {
             F.item = claim();
             cursor_seek(F, tl, ts, c1);
+            cursor_range(F, gq, ks_n);
           }
           ++issued;
         }
@@ -612,12 +630,48 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
         block_math<NT, COLS, false>(acc, R, c, bsel, base, wstep);
     }
     ++k;
-    if (b < H.nb) continue;
+    if (b < b_hi) continue;
 
     // item done: acc[n][*][0..1] = (hi, lo) parts of token 4n+c for row ra, [2..3] for rb
     const uint32_t ra = (item - H.item_begin) * kTileRows + g, rb = ra + 8;
     const bool va = ra < H.M, vb = rb < H.M;
-    if (H.kind == kTaskPlain) {
+    if constexpr (KS > 1) {
+      // K-split: leave this warp's slice sums, wait for the group's other
+      // warps (bounded), and warp 0 of the group adds the slices in order.
+      const uint32_t par = tiles & 1u;
+      float* mine = s_part + (((par * ngrp + grp) * ks_n + gq) * kTileRows) * 4;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint32_t t = 4 * n + c;
+        if (t < batch) {
+          mine[g * 4 + t] = (acc[n][0][0] + acc[n][1][0]) + (acc[n][0][1] + acc[n][1][1]);
+          mine[(g + 8) * 4 + t] = (acc[n][0][2] + acc[n][1][2]) + (acc[n][0][3] + acc[n][1][3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_gbar[grp]);
+      if (!mbar_wait(&s_gbar[grp], par)) {
+        timed_out = true;
+        break;
+      }
+      if (gq == 0) {
+        const float* all = s_part + (((par * ngrp + grp) * ks_n) * kTileRows) * 4;
+        const uint32_t t = c;
+        if (t < batch) {
+          float sa = all[g * 4 + t], sb = all[(g + 8) * 4 + t];
+          for (uint32_t q = 1; q < ks_n; ++q) {
+            sa += all[(q * kTileRows + g) * 4 + t];
+            sb += all[(q * kTileRows + g + 8) * 4 + t];
+          }
+          if (va) H.y[(uint64_t)t * H.M + ra] = sa * H.inv[0];
+          if (vb) H.y[(uint64_t)t * H.M + rb] = sb * H.inv[0];
+        }
+      }
+      ++tiles;
+    }
+    if (KS > 1) {
+      // (the group combine above wrote y)
+    } else if (H.kind == kTaskPlain) {
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         const uint32_t t = 4 * n + c;
@@ -651,11 +705,12 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int h = 0; h < 2; ++h) acc[n][h][0] = acc[n][h][1] = acc[n][h][2] = acc[n][h][3] = 0.0f;
-    b = 0;
     ++consumed;
     __syncwarp();
     item = ring[consumed & 3u];
     while (item < c1 && item >= H.item_end) H = hot_of<NT>(tl, ts, ++ti, s_sched, c, batch, s_inv);
+    b = gq * (H.nb / ks_n);
+    b_hi = b + H.nb / ks_n;
   }
 
   if (timed_out) {
@@ -734,25 +789,30 @@ __global__ void init_select_kernel(SelectScratch sc) {
 
 constexpr size_t kAlignSlack = 128;  // room to align the dynamic shared memory base
 
+// K-split partial sums: 2 tile parities x kEngineWarps slices x 16 rows x 4 tokens.
+constexpr size_t kPartSmem = (size_t)2 * kEngineWarps * kTileRows * 4 * sizeof(float);
+
+// hs: the launch has an LM head (per-warp candidate tables); else the same
+// space holds K-split partial sums.
 size_t xcache_bytes(int hs) {
-  return kSmemLimit - kStaticSmemHeadroom - kAlignSlack - kWeightSmem - kTaskSmem - (hs ? kSelectSmem : 0);
+  return kSmemLimit - kStaticSmemHeadroom - kAlignSlack - kWeightSmem - kTaskSmem - (hs ? kSelectSmem : kPartSmem);
 }
 
-template <int NT, int COLS>
+template <int NT, int COLS, int KS = 1>
 cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, int hs,
                            const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
   const size_t xcap = xcache_bytes(hs);
-  const size_t smem = kAlignSlack + kWeightSmem + kTaskSmem + xcap + (hs ? kSelectSmem : 0);
+  const size_t smem = kAlignSlack + kWeightSmem + kTaskSmem + xcap + (hs ? kSelectSmem : kPartSmem);
   static int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(kSmemLimit - kStaticSmemHeadroom));
     if (e != cudaSuccess) return e;
     attr_dev = dev;
   }
-  engine_kernel<NT, COLS><<<grid, kEngineWarps * 32, smem, s>>>(tasks, map, batch, hs, sel, (uint32_t)xcap);
+  engine_kernel<NT, COLS, KS><<<grid, kEngineWarps * 32, smem, s>>>(tasks, map, batch, hs, sel, (uint32_t)xcap);
   return cudaGetLastError();
 }
 
@@ -878,6 +938,15 @@ cudaError_t launch_engine(const TaskList& tasks, const CUtensorMap& map, uint32_
                           const SelectScratch& sel, int sm_count, cudaStream_t s) {
   const uint32_t grid = tasks.sched ? tasks.grid : engine_grid(tasks.total_items, sm_count);
   const int hs = has_select ? 1 : 0;
+  if (tasks.ksplit == 4) {
+    switch (batch) {
+      case 1: return launch_variant<1, 2, 4>(tasks, map, batch, hs, sel, grid, s);
+      case 2: return launch_variant<1, 4, 4>(tasks, map, batch, hs, sel, grid, s);
+      case 3: return launch_variant<1, 6, 4>(tasks, map, batch, hs, sel, grid, s);
+      case 4: return launch_variant<1, 8, 4>(tasks, map, batch, hs, sel, grid, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (batch) {
     case 1: return launch_variant<1, 2>(tasks, map, batch, hs, sel, grid, s);
     case 2: return launch_variant<1, 4>(tasks, map, batch, hs, sel, grid, s);

@@ -96,6 +96,8 @@ struct TaskList {
   uint32_t total_cost;  // sum of items * (N/256): the super-blocks of the launch
   uint32_t grid;        // CTAs the schedule was made for
   uint32_t select_task; // index of the kTaskSelect task, if the launch has one
+  uint32_t ksplit;      // > 1: KS warps share each tile, one K slice each (plain tasks, batch <= 4,
+                        // every task's N/256 a multiple of KS)
 };
 
 struct JobList {

@@ -56,6 +56,7 @@ struct Stage {
   CtaSched* sched_dev = nullptr;
   uint32_t n_tasks = 0, n_jobs = 0, total_items = 0, total_cost = 0, grid = 0, select_task = 0;
   bool prep = false;  // activations prepared inside the engine launch (no preparation launch)
+  uint32_t ksplit = 0;  // warps sharing each tile (long rows only; see TaskList::ksplit)
 };
 
 }  // namespace
@@ -238,6 +239,17 @@ int q4k_plan_commit(q4k_plan* p) {
     }
     st.total_items = items;
     st.total_cost = cost;
+    // Rows of >= 16 super-blocks (the FFN down projection) make few, long
+    // items: a stage of only such GEMVs shares each tile across 4 warps,
+    // each taking a quarter of the row, so the items balance over the warps.
+    {
+      bool long_rows = B <= 4 && st.selects.empty() && !tasks[s].empty();
+      for (const EngineTask& t : tasks[s]) {
+        const uint32_t nb = t.N / Q4K_QK;
+        long_rows = long_rows && nb >= 16 && nb % 4 == 0;
+      }
+      st.ksplit = long_rows ? 4u : 0u;
+    }
     st.n_tasks = (uint32_t)tasks[s].size();
     st.n_jobs = (uint32_t)keys[s].size();
     st.grid = items ? engine_grid(items, ctx->sm_count) : 0;
@@ -363,6 +375,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
       tl.select_task = st.select_task;
       tl.jobs = st.jobs_dev;
       tl.prep = st.prep ? 1u : 0u;
+      tl.ksplit = st.ksplit;
       cudaError_t e = launch_engine(tl, kNoMap, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
     }

@@ -78,17 +78,25 @@ class DecodeStep:
     batch: int = 1
     weights: dict = field(default_factory=dict)  # (layer, name) -> uint8 tensor
     lm_head: torch.Tensor | None = None
+    share_weights_with: "DecodeStep | None" = None  # reuse another step's (same-shape) device weights
 
     def __post_init__(self):
         dev = self.ctx.device
         s, B = self.shape, self.batch
         shapes = layer_shapes(s)
-        for layer in range(s.layers):
-            for name in LAYER_MATS:
-                M, N = shapes[name]
-                w = synth.q4k_matrix(M, N, matrix_seed(layer, name))
-                self.weights[(layer, name)] = torch.from_numpy(w).to(dev)
-        self.lm_head = torch.from_numpy(synth.q4k_matrix(s.vocab, s.hidden, LMHEAD_SEED)).to(dev)
+        if self.share_weights_with is not None:
+            other = self.share_weights_with
+            if other.shape != s:
+                raise ValueError("shared weights need the same shape")
+            self.weights = other.weights
+            self.lm_head = other.lm_head
+        else:
+            for layer in range(s.layers):
+                for name in LAYER_MATS:
+                    M, N = shapes[name]
+                    w = synth.q4k_matrix(M, N, matrix_seed(layer, name))
+                    self.weights[(layer, name)] = torch.from_numpy(w).to(dev)
+            self.lm_head = torch.from_numpy(synth.q4k_matrix(s.vocab, s.hidden, LMHEAD_SEED)).to(dev)
         self.x_h = torch.from_numpy(synth.activations(B, s.hidden, synth.seed_for(CONFIG, 100))).to(dev)
         self.x_attn = torch.from_numpy(synth.activations(B, s.q, synth.seed_for(CONFIG, 101))).to(dev)
         f32 = dict(dtype=torch.float32, device=dev)

@@ -279,6 +279,31 @@ def test_plan_matches_single_calls(ctx, oracle):
         p.close()
 
 
+@pytest.mark.parametrize("B", [1, 3, 4])
+def test_plan_long_rows_split_across_warps(ctx, oracle, B):
+    # a stage of rows with >= 16 super-blocks shares each 16-row tile between
+    # 4 warps (one quarter of K each) and adds their sums in a fixed order:
+    # two runs give the same bits, and both match the oracle
+    from q4k import Plan
+
+    M, N = 1000, 6144
+    w_np = synth.q4k_matrix(M, N, 61)
+    x_np = synth.activations(B, N, 62)
+    w, x = to_dev(w_np), to_dev(x_np)
+    y = torch.empty((B, M), dtype=torch.float32, device=DEV)
+    p = Plan(ctx, batch=B)
+    p.gemv(0, w, x, y, M, N)
+    p.commit()
+    p.run()
+    torch.cuda.synchronize()
+    first = y.clone()
+    p.run()
+    torch.cuda.synchronize()
+    assert torch.equal(first.view(torch.int32), y.view(torch.int32))
+    check_gemv(oracle, y.cpu().numpy(), w_np, x_np, M, N)
+    p.close()
+
+
 def test_plan_lmhead_matches_single_call(ctx):
     from q4k import Plan, Selection
 
