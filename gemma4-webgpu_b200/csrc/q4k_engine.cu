@@ -92,6 +92,17 @@ __device__ __forceinline__ void sel_unkey(unsigned long long k, float& v, uint32
   idx = 0x7fffffffu - (uint32_t)((k >> 1) & 0x7fffffffu);
 }
 
+// ---- programmatic dependent launch ----------------------------------------------------
+// Engine launches are made with programmatic stream serialization: a launch
+// may start while the previous kernel on the stream finishes, runs its
+// prologue on static data only (schedule, task descriptors, the first weight
+// stages), and waits for the previous kernel's completion and memory before
+// it reads activations or writes outputs.  Each CTA signals its dependents
+// once its work loop is done.
+
+__device__ __forceinline__ void wait_prior_grids() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- activation preparation --------------------------------------------------------
 
 __device__ __forceinline__ float xjob_value(const XJob& J, uint64_t i) {
@@ -451,6 +462,9 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   uint64_t* bars = s_bar[warp];
   uint32_t* ring = s_ring[warp];
 
+  // launches that copy prepared activations from global memory read data a
+  // previous kernel wrote: wait for it before anything else
+  if (!tl.prep) wait_prior_grids();
   if (lane == 0)
     for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
   if (threadIdx.x == 0) mbar_init(&s_xbar, 1);
@@ -550,6 +564,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   // whole CTA turns each cached job's activation (x, or gelu_mul(gate, up))
   // into scaled hi/lo fragments in shared memory.
   if (tl.prep) {
+    wait_prior_grids();  // the activations and outputs belong to the previous kernels until now
     for (uint32_t j = 0; j < s_sched.nx; ++j) {
       const XJob J = tl.dev ? tl.jobs[s_sched.xjob[j]] : tl.inl_job;
       const bool store_act = J.mode && J.act && ((s_sched.act_mask >> j) & 1u);
@@ -713,6 +728,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     b_hi = b + H.nb / ks_n;
   }
 
+  allow_dependents();
   if (timed_out) {
     // record the failure, then let every copy still in flight land (bounded)
     if (lane == 0) atomicOr(sel.status, 1u);
@@ -812,8 +828,17 @@ cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, uint32
     if (e != cudaSuccess) return e;
     attr_dev = dev;
   }
-  engine_kernel<NT, COLS, KS><<<grid, kEngineWarps * 32, smem, s>>>(tasks, map, batch, hs, sel, (uint32_t)xcap);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kEngineWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, engine_kernel<NT, COLS, KS>, tasks, map, batch, hs, sel, (uint32_t)xcap);
 }
 
 }  // namespace
