@@ -911,8 +911,8 @@ static uint32_t host_item_at_cost(const EngineTask* t, uint32_t n, uint32_t tota
     const uint32_t mid = (lo + hi + 1) / 2;
     if (t[mid].cost_begin <= p) lo = mid; else hi = mid - 1;
   }
-  const uint32_t nb = t[lo].N >> 8;
-  const uint64_t item = t[lo].item_begin + (p - t[lo].cost_begin + nb - 1) / nb;
+  const uint32_t ic = item_cost(t[lo].N, t[lo].kind);
+  const uint64_t item = t[lo].item_begin + (p - t[lo].cost_begin + ic - 1) / ic;
   return item < t[lo].item_end ? (uint32_t)item : t[lo].item_end;
 }
 

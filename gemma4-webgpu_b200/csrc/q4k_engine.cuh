@@ -93,7 +93,7 @@ struct TaskList {
   uint32_t prep;
   uint32_t n;
   uint32_t total_items;
-  uint32_t total_cost;  // sum of items * (N/256): the super-blocks of the launch
+  uint32_t total_cost;  // sum of item_cost over the work items of the launch
   uint32_t grid;        // CTAs the schedule was made for
   uint32_t select_task; // index of the kTaskSelect task, if the launch has one
   uint32_t ksplit;      // > 1: KS warps share each tile, one K slice each (plain tasks, batch <= 4,
@@ -112,6 +112,13 @@ struct JobList {
 // rows fall in distinct banks).  Rows past M and words past the row end
 // read as zeros.  *tile_bytes = the box width in bytes.
 cudaError_t encode_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N, uint32_t* tile_bytes);
+
+// Schedule cost of one work item (16 rows) of a task: its super-blocks per
+// row, in units of 1/20; LM-head items (softcap + per-residue selection in
+// the epilogue) count 5 % more.
+__host__ __device__ inline uint32_t item_cost(uint32_t N, uint32_t kind) {
+  return (N >> 8) * (kind == kTaskSelect ? 21u : 20u);
+}
 
 // Engine launch geometry: CTAs for a work list, and the shared-memory
 // activation cache each CTA has (depends on whether an LM head is present).

@@ -203,7 +203,7 @@ int q4k_plan_commit(q4k_plan* p) {
       t.item_begin = items;
       t.cost_begin = cost;
       items += tiles_of(g.M);
-      cost += tiles_of(g.M) * (g.N / Q4K_QK);
+      cost += tiles_of(g.M) * item_cost(g.N, kTaskPlain);
       t.item_end = items;
       t.aux = (uint32_t)j;  // job index until the buffers are laid out
       tasks[s].push_back(t);
@@ -226,7 +226,7 @@ int q4k_plan_commit(q4k_plan* p) {
       t.item_begin = items;
       t.cost_begin = cost;
       items += tiles_of(q.V);
-      cost += tiles_of(q.V) * (q.N / Q4K_QK);
+      cost += tiles_of(q.V) * item_cost(q.N, kTaskSelect);
       t.item_end = items;
       t.aux = (uint32_t)j;
       tasks[s].push_back(t);
