@@ -291,6 +291,25 @@ def run_ours(args) -> None:
                    "rows_per_rank": head.rows, "frac_of_peak": None,
                    "collective": "all_gather 2 KB/rank (NCCL) + on-device merge",
                    "matches_unsharded": same}
+        # the same head with the exchange fused into the launch (peer stores
+        # over NVLink into every rank's mailbox, bounded wait, merge)
+        fhead = ShardedLMHead(262144, 1536, 30.0, ctx=ctx, fused=True)
+        for _ in range(args.warmup):
+            fmerged = fhead(w_shard, x0)
+        torch.cuda.synchronize()
+        fsame = bool(torch.equal(fmerged.cand_idx, step.sel.cand_idx) and torch.equal(fmerged.argmax, step.sel.argmax))
+        barrier(world)
+        a.record()
+        for _ in range(reps):
+            fhead(w_shard, x0)
+        b.record()
+        torch.cuda.synchronize()
+        fs_ms = max_over_ranks(a.elapsed_time(b) / reps, world, dev)
+        fsame = max_over_ranks(0.0 if fsame else 1.0, world, dev) == 0.0
+        barrier(world)
+        fhead.close()
+        sharded["fused_exchange"] = {"ms": round(fs_ms, 4), "GB/s": round(lm_bytes / (fs_ms / 1e3) / 1e9, 1),
+                                     "launches_per_call": 1, "matches_unsharded": fsame}
 
     # end to end through the public API: pinned host inputs in, results out
     x_host = [torch.empty_like(step.x_h, device="cpu").pin_memory(),

@@ -773,12 +773,72 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     float v;
     uint32_t i;
     sel_unkey(key, v, i);
-    S.cand_val[r] = v;
-    S.cand_idx[r] = i;
+    if (tl.xc.world == 0) {
+      S.cand_val[r] = v;
+      S.cand_idx[r] = i;
+    }
     f_v[r] = v;
     f_i[r] = i;
   }
   __syncthreads();
+  if (tl.xc.world > 0) {
+    // Sharded head: push this rank's candidates to every rank's mailbox,
+    // wait for every rank's, merge (per residue: larger value, then lower
+    // index) into the outputs; the argmax tree below runs on the merge.
+    const Exchange& X = tl.xc;
+    __shared__ uint32_t s_epoch;
+    if (threadIdx.x == 0) {
+      s_epoch = *X.epoch + 1u;
+      *X.epoch = s_epoch;
+    }
+    __syncthreads();
+    const uint32_t ep = s_epoch;
+    for (uint32_t p = 0; p < X.world; ++p) {
+      uint32_t* slot = X.peer[p] + X.rank * kSlotWords;
+      if (threadIdx.x < 256) {
+        slot[threadIdx.x] = __float_as_uint(f_v[threadIdx.x]);
+        slot[256 + threadIdx.x] = f_i[threadIdx.x];
+      }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < X.world)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.peer[threadIdx.x] + X.rank * kSlotWords + kSlotFlag),
+                   "r"(ep)
+                   : "memory");
+    // every rank's slot in this rank's mailbox (bounded wait)
+    if (threadIdx.x < X.world) {
+      const uint32_t* flag = X.peer[X.rank] + threadIdx.x * kSlotWords + kSlotFlag;
+      bool ok = false;
+      for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        ok = (v == ep);
+      }
+      if (!ok) atomicOr(sel.status, 1u);
+      __threadfence_system();
+    }
+    __syncthreads();
+    if (threadIdx.x < 256) {
+      const uint32_t r = threadIdx.x;
+      const uint32_t* mb = X.peer[X.rank];
+      float bv = __uint_as_float(__ldcv(mb + r));
+      uint32_t bi = __ldcv(mb + 256 + r);
+      for (uint32_t q = 1; q < X.world; ++q) {
+        const float v = __uint_as_float(__ldcv(mb + q * kSlotWords + r));
+        const uint32_t i = __ldcv(mb + q * kSlotWords + 256 + r);
+        if (better(v, i, bv, bi)) {
+          bv = v;
+          bi = i;
+        }
+      }
+      S.cand_val[r] = bv;
+      S.cand_idx[r] = bi;
+      f_v[r] = bv;
+      f_i[r] = bi;
+    }
+    __syncthreads();
+  }
   // the reference's argmax tree (shaders/argmax.wgsl:21-27): the partner wins
   // only when strictly greater
   for (uint32_t st = 128; st > 0; st >>= 1) {

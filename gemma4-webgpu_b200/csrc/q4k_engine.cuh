@@ -80,6 +80,22 @@ struct XJob {
 
 // Tasks / jobs either live in device memory (plans) or are passed inline as
 // kernel parameters (single calls).
+// Candidate exchange of a vocabulary-sharded LM head (q4k_exchange): every
+// rank owns a mailbox of kMaxRanks slots in its own device memory; the last
+// CTA of a rank's LM-head launch writes its 256 candidates into slot `rank`
+// of every rank's mailbox (peer stores over NVLink), raises the slot's flag
+// to this call's epoch, waits (bounded) until all `world` slots of its own
+// mailbox carry the epoch, and merges them.
+constexpr uint32_t kMaxRanks = 8;
+constexpr uint32_t kSlotWords = 576;      // 256 values, 256 indices, flag at word 512; 2304 bytes
+constexpr uint32_t kSlotFlag = 512;
+
+struct Exchange {
+  uint32_t* peer[kMaxRanks];  // mailbox of each rank as mapped on this device (peer[rank] = own)
+  uint32_t* epoch;            // this rank's call counter (own device memory)
+  uint32_t rank, world;       // world = 0: no exchange
+};
+
 // prep != 0: every CTA prepares the activations of its task range itself,
 // straight into its shared-memory cache (from `jobs`, or `inl_job` for an
 // inline task), so no preparation launch precedes the engine; the host
@@ -98,6 +114,7 @@ struct TaskList {
   uint32_t select_task; // index of the kTaskSelect task, if the launch has one
   uint32_t ksplit;      // > 1: KS warps share each tile, one K slice each (plain tasks, batch <= 4,
                         // every task's N/256 a multiple of KS)
+  Exchange xc;          // LM-head candidate exchange across ranks (xc.world > 0)
 };
 
 struct JobList {

@@ -38,6 +38,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_lmhead_select": ([_P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_merge_candidates": ([_P, _P, _P, _U32, _P, _P, _P, _P], _I),
     "q4k_lmhead_select_static": ([_P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
+    "q4k_exchange_create": ([_P, _U32, _U32, ctypes.POINTER(_P), _P], _I),
+    "q4k_exchange_open": ([_P, _U32, _P], _I),
+    "q4k_exchange_destroy": ([_P], None),
+    "q4k_lmhead_select_sharded": ([_P, _P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P], _I),
     "q4k_plan_create": ([_P, _U32, ctypes.POINTER(_P)], _I),
     "q4k_plan_destroy": ([_P], None),
     "q4k_plan_gemv": ([_P, _U32, _P, _P, _P, _U32, _U32], _I),

@@ -220,6 +220,34 @@ class Context:
             _ptr(out.cand_idx), _ptr(out.argmax), _stream(stream)))
         return out
 
+    def exchange(self, rank: int, world: int) -> "Exchange":
+        """A mailbox for the fused sharded LM head (see Exchange)."""
+        return Exchange(self, rank, world)
+
+    def lmhead_select_sharded(self, ex: "Exchange", weight: torch.Tensor, x: torch.Tensor, V: int, N: int,
+                              cap: float = 30.0, row_offset: int = 0, out: Selection | None = None,
+                              stream: torch.cuda.Stream | None = None) -> Selection:
+        """This rank's rows [row_offset, row_offset+V) of a vocabulary-sharded
+        LM head, the candidate exchange with every rank over NVLink and the
+        merge, in one launch: the whole head's candidates and argmax."""
+        _need(weight, torch.uint8, "weight", self.device)
+        _need(x, torch.float32, "x", self.device)
+        if x.numel() != N:
+            raise ValueError(f"x has {x.numel()} elements, expected N={N}")
+        if weight.numel() < V * (N // QK_K) * BLOCK_BYTES:
+            raise ValueError("weight buffer smaller than V*N/256*144 bytes")
+        if out is None:
+            out = Selection(
+                cand_val=torch.empty(256, dtype=torch.float32, device=self.device),
+                cand_idx=torch.empty(256, dtype=torch.int32, device=self.device),
+                argmax=torch.empty(1, dtype=torch.int32, device=self.device),
+                logits=None,
+            )
+        self._check(self._L.q4k_lmhead_select_sharded(
+            self._h, ex._h, _ptr(weight), _ptr(x), V, N, cap, row_offset, _ptr(out.cand_val), _ptr(out.cand_idx),
+            _ptr(out.argmax), _stream(stream)))
+        return out
+
     def merge_candidates(self, vals: torch.Tensor, idx: torch.Tensor, out: Selection | None = None,
                          stream: torch.cuda.Stream | None = None) -> Selection:
         """[G, 256] gathered shard candidates -> one Selection (no logits)."""
@@ -238,6 +266,41 @@ class Context:
         self._check(self._L.q4k_merge_candidates(self._h, _ptr(vals), _ptr(idx), G, _ptr(out.cand_val),
                                                  _ptr(out.cand_idx), _ptr(out.argmax), _stream(stream)))
         return out
+
+
+class Exchange:
+    """This rank's mailbox for the fused sharded LM head (q4k_exchange_*):
+    create on every rank, share `handle` with the other ranks out of band,
+    then `open(peer, handle)` every peer."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, ctx: "Context", rank: int, world: int):
+        self._ctx = ctx
+        self._L = ctx._L
+        self.rank, self.world = rank, world
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(self.HANDLE_BYTES)
+        ctx._check(self._L.q4k_exchange_create(ctx._h, rank, world, ctypes.byref(h), buf))
+        self._h = h
+        self.handle = bytes(buf.raw)
+
+    def open(self, peer: int, handle: bytes) -> None:
+        if len(handle) != self.HANDLE_BYTES:
+            raise ValueError("bad exchange handle")
+        buf = ctypes.create_string_buffer(handle, self.HANDLE_BYTES)
+        self._ctx._check(self._L.q4k_exchange_open(self._h, peer, buf))
+
+    def close(self) -> None:
+        if self._h:
+            self._L.q4k_exchange_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Plan:

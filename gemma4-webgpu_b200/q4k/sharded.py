@@ -15,6 +15,12 @@ Rows are independent and the selection reduces per residue class (index mod
     over the merged set, which equal the unsharded head's outputs.
 
 The only collective is that 2 KB-per-rank all-gather; the weights never move.
+
+With `fused=True` there is no collective call at all: each rank's LM-head
+launch writes its candidates straight into every rank's mailbox over NVLink,
+waits (bounded) for the other ranks' and merges them (q4k_exchange_* and
+q4k_lmhead_select_sharded); the process group only carries the one-time
+exchange of the mailboxes' IPC handles.
 """
 from __future__ import annotations
 
@@ -51,7 +57,7 @@ class ShardedLMHead:
 
     def __init__(self, V: int, N: int, cap: float = 30.0, ctx: Context | None = None,
                  group: dist.ProcessGroup | None = None, select: SelectFn | None = None,
-                 merge: MergeFn | None = None, device: torch.device | None = None):
+                 merge: MergeFn | None = None, device: torch.device | None = None, fused: bool = False):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -68,6 +74,19 @@ class ShardedLMHead:
         self.recv = torch.empty(self.world * 512, dtype=torch.float32, device=self.device)
         self._argmax = torch.empty(1, dtype=torch.int32, device=self.device)
         self._use_into_tensor = dist.get_backend(group) == "nccl"
+        self.fused = fused
+        self.ex = None
+        if fused:
+            if ctx is None:
+                raise ValueError("the fused exchange needs a Context")
+            self.ex = ctx.exchange(self.rank, self.world)
+            h = torch.tensor(list(self.ex.handle), dtype=torch.uint8,
+                             device=self.device if self._use_into_tensor else torch.device("cpu"))
+            got = [torch.empty_like(h) for _ in range(self.world)]
+            dist.all_gather(got, h, group=group)
+            for p, t in enumerate(got):
+                self.ex.open(p, bytes(t.cpu().tolist()))
+            dist.barrier(group=group)  # every mailbox is mapped everywhere before the first call
 
     # the shard's candidates land in the send buffer
     def _gpu_select(self, w_shard: torch.Tensor, x: torch.Tensor, send: torch.Tensor) -> None:
@@ -79,6 +98,9 @@ class ShardedLMHead:
         return self.ctx.merge_candidates(vals, idx)
 
     def __call__(self, w_shard: torch.Tensor, x: torch.Tensor) -> Selection:
+        if self.fused:
+            return self.ctx.lmhead_select_sharded(self.ex, w_shard, x, self.rows, self.N, self.cap,
+                                                  row_offset=self.row0)
         self._select(w_shard, x, self.send)
         if self._use_into_tensor:
             dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
@@ -88,3 +110,8 @@ class ShardedLMHead:
         vals = g[:, 0].contiguous()
         idx = g[:, 1].contiguous().view(torch.int32)
         return self._merge(vals, idx)
+
+    def close(self) -> None:
+        if self.ex is not None:
+            self.ex.close()
+            self.ex = None

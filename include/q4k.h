@@ -165,6 +165,33 @@ Q4K_API int q4k_lmhead_select_static(const void* w, const float* x, uint32_t V, 
                                      uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
                                      uint32_t* argmax, void* stream);
 
+/* ---- vocabulary-sharded LM head, exchange fused into the launch -------
+ * The reference's LM head runs on one device (sampleNextTokenSubmit,
+ * src/engine.ts:1686-1741).  Split over G ranks (one process per GPU, rank r
+ * owning rows [r*V/G, (r+1)*V/G), V/G a multiple of 256), each rank's launch
+ * computes its shard, writes its 256 candidates straight into every rank's
+ * mailbox over NVLink (peer stores, no collective library), waits for all
+ * ranks' candidates (bounded) and merges them: the outputs on every rank
+ * equal the unsharded head's.  Set-up: every rank creates its mailbox
+ * (q4k_exchange_create returns a Q4K_EXCHANGE_HANDLE_BYTES handle), the
+ * handles are exchanged out of band (e.g. a torch.distributed all-gather),
+ * and every rank opens every peer's (q4k_exchange_open).  Calls must be made
+ * by all ranks in the same order; a rank that never arrives makes the others
+ * give up their bounded wait (Q4K_ERR_TIMEOUT from q4k_check). */
+#define Q4K_EXCHANGE_HANDLE_BYTES 64
+typedef struct q4k_exchange q4k_exchange;
+
+Q4K_API int q4k_exchange_create(q4k_ctx* ctx, uint32_t rank, uint32_t world, q4k_exchange** out, void* handle_out);
+Q4K_API int q4k_exchange_open(q4k_exchange* ex, uint32_t peer, const void* handle);
+Q4K_API void q4k_exchange_destroy(q4k_exchange* ex);
+
+/* This rank's shard of the head (rows of `w` are global indices row_offset +
+ * i, i < V) + the exchange + the merge, in one launch.  Outputs as
+ * q4k_lmhead_select (without logits), for the whole vocabulary. */
+Q4K_API int q4k_lmhead_select_sharded(q4k_ctx* ctx, q4k_exchange* ex, const void* w, const float* x, uint32_t V,
+                                      uint32_t N, float cap, uint32_t row_offset, float* cand_val,
+                                      uint32_t* cand_idx, uint32_t* argmax, void* stream);
+
 /* ---- plans ------------------------------------------------------------
  * A plan records a decode step's matmul-path operations once and replays
  * them with two launches per stage, the way the engine records a token's

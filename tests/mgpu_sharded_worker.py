@@ -34,14 +34,19 @@ def main() -> None:
         ctx = Context(local)
         w = torch.from_numpy(synth.q4k_matrix(V, N, 777)).cuda()
         x = torch.from_numpy(synth.activations(1, N, 778)[0]).cuda()
-        head = ShardedLMHead(V, N, 30.0, ctx=ctx)
-        for _ in range(2):  # twice: the context scratch resets between calls
-            merged = head(w[head.row0:head.row0 + head.rows], x)
         ref = ctx.lmhead_select(w, x, V, N, 30.0)
-        torch.cuda.synchronize()
-        assert torch.equal(merged.cand_idx, ref.cand_idx), "candidate indices differ"
-        assert torch.equal(merged.cand_val.view(torch.int32), ref.cand_val.view(torch.int32)), "values differ"
-        assert torch.equal(merged.argmax, ref.argmax), "argmax differs"
+        for fused in (False, True):
+            head = ShardedLMHead(V, N, 30.0, ctx=ctx, fused=fused)
+            for _ in range(3):  # repeated calls: scratch and mailboxes reset between calls
+                merged = head(w[head.row0:head.row0 + head.rows], x)
+                torch.cuda.synchronize()
+                assert torch.equal(merged.cand_idx, ref.cand_idx), f"candidate indices differ (fused={fused})"
+                assert torch.equal(merged.cand_val.view(torch.int32), ref.cand_val.view(torch.int32)), \
+                    f"values differ (fused={fused})"
+                assert torch.equal(merged.argmax, ref.argmax), f"argmax differs (fused={fused})"
+            ctx.check()
+            dist.barrier()
+            head.close()
         print(f"rank {rank} ok", flush=True)
         ctx.close()
     finally:

@@ -200,6 +200,27 @@ def test_sharded_lmhead_merge_equals_unsharded(ctx, oracle, G):
     assert torch.equal(m.argmax, full.argmax)
 
 
+def test_fused_exchange_one_rank_equals_unsharded(ctx):
+    # the fused sharded head with a world of 1: the launch writes its
+    # candidates into its own mailbox, waits for them and merges; repeated
+    # calls advance the mailbox epoch
+    V, N = 32768, 1536
+    w = to_dev(synth.q4k_matrix(V, N, 71))
+    ex = ctx.exchange(0, 1)
+    try:
+        for seed in (72, 73, 74):
+            x = to_dev(synth.activations(1, N, seed)[0])
+            ref = ctx.lmhead_select(w, x, V, N, 30.0)
+            got = ctx.lmhead_select_sharded(ex, w, x, V, N, 30.0)
+            torch.cuda.synchronize()
+            assert torch.equal(got.cand_idx, ref.cand_idx)
+            assert torch.equal(got.cand_val.view(torch.int32), ref.cand_val.view(torch.int32))
+            assert torch.equal(got.argmax, ref.argmax)
+        ctx.check()
+    finally:
+        ex.close()
+
+
 def test_lmhead_repeat_calls_reset_scratch(ctx):
     V, N = 4096, 256
     w = to_dev(synth.q4k_matrix(V, N, 5))
