@@ -13,6 +13,11 @@ Q4_K layout that src/gguf.ts:157-210 decodes:
                             (src/gguf.ts:175-182)
     offset 16  128 bytes    256 nibbles, uniform in [0, 15]
 
+Q6_K super-blocks (src/gguf.ts:316-368 layout, 210 bytes) for the Q6_K
+GEMV: ql[128] and qh[64] uniform random bytes (6-bit quants uniform in
+[0, 63]), 16 int8 scales uniform in [-128, 127], f16 d = f16(|N(0, 2e-5)|)
+(weights of the same magnitude as the Q4_K ones).
+
 Random numbers come from numpy Generator(PCG64(seed)) with
 seed = 20261201 + 1000 * config + matrix_id.
 """
@@ -95,3 +100,28 @@ def activations(batch: int, n: int, seed: int) -> np.ndarray:
 def q4k_bytes(rows: int, cols: int) -> int:
     """Size rule of tensorByteSize for type 12 (src/gguf.ts:390)."""
     return rows * cols // QK_K * BLOCK_BYTES
+
+
+Q6K_BLOCK_BYTES = 210
+
+
+def make_q6k_blocks(n_blocks: int, rng: np.random.Generator, d_sigma: float = 2e-5) -> np.ndarray:
+    """n_blocks seeded Q6_K super-blocks as uint8 [n_blocks, 210] (GGUF layout)."""
+    out = np.frombuffer(rng.bytes(n_blocks * Q6K_BLOCK_BYTES), dtype=np.uint8).reshape(n_blocks, -1).copy()
+    d = np.abs(rng.normal(0.0, d_sigma, n_blocks)).astype(np.float16)
+    out[:, 208:210] = d.view(np.uint8).reshape(n_blocks, 2)
+    return out
+
+
+def q6k_matrix(rows: int, cols: int, seed: int) -> np.ndarray:
+    """A [rows, cols] Q6_K weight as uint8 [rows, cols/256*210], GGUF row-major."""
+    if cols % QK_K:
+        raise ValueError(f"cols={cols} is not a multiple of {QK_K}")
+    nb = cols // QK_K
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return make_q6k_blocks(rows * nb, rng).reshape(rows, nb * Q6K_BLOCK_BYTES)
+
+
+def q6k_bytes(rows: int, cols: int) -> int:
+    """Size rule of tensorByteSize for type 14 (src/gguf.ts:392)."""
+    return rows * cols // QK_K * Q6K_BLOCK_BYTES

@@ -53,6 +53,10 @@ def lib() -> ctypes.CDLL:
     L.orc_matmul_quant_f16.argtypes = [P, P, P, I64, I64, I64, I]
     L.orc_q4k_gemv.argtypes = [P, P, P, I64, I64, I64, I]
     L.orc_q4k_gemv_f64.argtypes = [P, P, P, P, I64, I64, I64, I]
+    L.orc_q6k_dequant_f32.argtypes = [P, I64, P]
+    L.orc_q6k_dequant_f16.argtypes = [P, I64, P]
+    L.orc_q6k_gemv.argtypes = [P, P, P, I64, I64, I64, I]
+    L.orc_q6k_gemv_f64.argtypes = [P, P, P, P, I64, I64, I64, I]
     L.orc_logit_softcap.argtypes = [P, I64, ctypes.c_float]
     L.orc_argmax.argtypes = [P, I64]
     L.orc_argmax.restype = ctypes.c_uint32
@@ -131,6 +135,43 @@ def q4k_gemv_f64(w: np.ndarray, x: np.ndarray, M: int, N: int, threads: int = 0)
     y = np.empty((batch, M), dtype=np.float64)
     wn = np.empty(M, dtype=np.float64)
     lib().orc_q4k_gemv_f64(_p(wb), _p(xx), _p(y), _p(wn), M, N, batch, threads)
+    return y, wn
+
+
+def q6k_dequant_f32(blocks: np.ndarray) -> np.ndarray:
+    """Q6_K super-blocks (GGUF layout, 210 bytes each) -> f32 (src/gguf.ts:316-368)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)
+    nb = b.size // 210
+    out = np.empty(nb * 256, dtype=np.float32)
+    lib().orc_q6k_dequant_f32(_p(b), nb, _p(out))
+    return out
+
+
+def q6k_dequant_f16(blocks: np.ndarray) -> np.ndarray:
+    """f16 bit patterns (uint16) of the decoded Q6_K weights (RNE)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)
+    nb = b.size // 210
+    out = np.empty(nb * 256, dtype=np.uint16)
+    lib().orc_q6k_dequant_f16(_p(b), nb, _p(out))
+    return out
+
+
+def q6k_gemv(w: np.ndarray, x: np.ndarray, M: int, N: int, threads: int = 0) -> np.ndarray:
+    """y[b, m] for a Q6_K matrix (GGUF bytes [M, N/256*210]), reference semantics."""
+    wb = np.ascontiguousarray(w, dtype=np.uint8)
+    xx = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, N)
+    y = np.empty((xx.shape[0], M), dtype=np.float32)
+    lib().orc_q6k_gemv(_p(wb), _p(xx), _p(y), M, N, xx.shape[0], threads)
+    return y
+
+
+def q6k_gemv_f64(w: np.ndarray, x: np.ndarray, M: int, N: int, threads: int = 0):
+    """(y_f64 [batch, M], ||w_row||_2 [M]) on the f16-rounded Q6_K weights."""
+    wb = np.ascontiguousarray(w, dtype=np.uint8)
+    xx = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, N)
+    y = np.empty((xx.shape[0], M), dtype=np.float64)
+    wn = np.empty(M, dtype=np.float64)
+    lib().orc_q6k_gemv_f64(_p(wb), _p(xx), _p(y), _p(wn), M, N, xx.shape[0], threads)
     return y, wn
 
 

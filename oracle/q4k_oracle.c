@@ -24,6 +24,7 @@
  *   Q4_K decode         src/gguf.ts:157-210   (dequantizeQ4_K, getScaleMin :175-182)
  *   f32 -> f16          src/gguf.ts:425-473   (f32ToF16Array: Float16Array RNE at
  *                                              :432-436, truncating fallback :443-471)
+ *   Q6_K decode         src/gguf.ts:316-368   (dequantizeQ6_K)
  *   GEMV                shaders/matmul_quant.wgsl:21-54
  *   4-row GEMV          shaders/matmul_quant_mr4.wgsl:33-88 (same per-row order)
  *   softcap             shaders/logit_softcap.wgsl:9-16
@@ -43,7 +44,7 @@
 
 #define ORC_API __attribute__((visibility("default")))
 
-enum { QK_K = 256, Q4K_BLOCK_BYTES = 144 };
+enum { QK_K = 256, Q4K_BLOCK_BYTES = 144, Q6K_BLOCK_BYTES = 210 };
 
 /* ---- f16 <-> f32 ------------------------------------------------------- */
 
@@ -159,6 +160,50 @@ ORC_API void orc_q4k_dequant_f16(const uint8_t* blocks, int64_t n_blocks, uint16
   }
 }
 
+/* ---- Q6_K super-block decode ------------------------------------------- */
+
+/* One Q6_K super-block (210 bytes: ql[128], qh[64], int8 scales[16], f16 d)
+ * -> 256 f32, as src/gguf.ts:329-364 evaluates it: per half, element l of
+ * the four 32-wide quarters is (4 bits of ql, 2 bits of qh) - 32, times the
+ * quarter's int8 scale of sub-block l/16 and d, in f64, one rounding to f32
+ * at the Float32Array store. */
+static void dequant_q6k_block_f32(const uint8_t* blk, float* out) {
+  const uint8_t* ql = blk;
+  const uint8_t* qh = blk + 128;
+  const int8_t* sc = (const int8_t*)(blk + 192);
+  const double d = f16_to_f64((uint16_t)(blk[208] | (blk[209] << 8)));
+  for (int half = 0; half < 2; ++half) {
+    const uint8_t* l0 = ql + 64 * half;
+    const uint8_t* h0 = qh + 32 * half;
+    const int8_t* s0 = sc + 8 * half;
+    float* o = out + 128 * half;
+    for (int l = 0; l < 32; ++l) {
+      const int is = l >> 4;
+      const int q1 = ((l0[l] & 0x0f) | (((h0[l] >> 0) & 3) << 4)) - 32;
+      const int q2 = ((l0[l + 32] & 0x0f) | (((h0[l] >> 2) & 3) << 4)) - 32;
+      const int q3 = ((l0[l] >> 4) | (((h0[l] >> 4) & 3) << 4)) - 32;
+      const int q4 = ((l0[l + 32] >> 4) | (((h0[l] >> 6) & 3) << 4)) - 32;
+      o[l] = (float)(d * s0[is + 0] * q1);
+      o[l + 32] = (float)(d * s0[is + 2] * q2);
+      o[l + 64] = (float)(d * s0[is + 4] * q3);
+      o[l + 96] = (float)(d * s0[is + 6] * q4);
+    }
+  }
+}
+
+ORC_API void orc_q6k_dequant_f32(const uint8_t* blocks, int64_t n_blocks, float* out) {
+  for (int64_t b = 0; b < n_blocks; ++b) dequant_q6k_block_f32(blocks + b * Q6K_BLOCK_BYTES, out + b * QK_K);
+}
+
+/* Q6_K -> f16 bit patterns (dequantizeQ6_K then f32ToF16Array, RNE). */
+ORC_API void orc_q6k_dequant_f16(const uint8_t* blocks, int64_t n_blocks, uint16_t* out) {
+  float tmp[QK_K];
+  for (int64_t b = 0; b < n_blocks; ++b) {
+    dequant_q6k_block_f32(blocks + b * Q6K_BLOCK_BYTES, tmp);
+    for (int i = 0; i < QK_K; ++i) out[b * QK_K + i] = orc_f32_to_f16_rne(tmp[i]);
+  }
+}
+
 /* ---- matmul_quant ------------------------------------------------------ */
 
 /* One output row in the order of shaders/matmul_quant.wgsl:31-53: thread t of
@@ -228,6 +273,7 @@ typedef struct {
   void* y;
   double* wnorm;
   int64_t M, N, batch;
+  int fmt; /* weight format of `w` for the fused GEMVs: 0 = Q4_K, 1 = Q6_K */
 } gemv_args;
 
 static void rows_matmul_f16(void* p, int64_t m0, int64_t m1) {
@@ -248,7 +294,7 @@ static void rows_matmul_f16(void* p, int64_t m0, int64_t m1) {
  * activation row). */
 ORC_API void orc_matmul_quant_f16(const uint16_t* w16, const float* x, float* y, int64_t M, int64_t N,
                                   int64_t batch, int n_threads) {
-  gemv_args a = {w16, x, y, NULL, M, N, batch};
+  gemv_args a = {w16, x, y, NULL, M, N, batch, 0};
   parallel_rows(rows_matmul_f16, &a, M, n_threads);
 }
 
@@ -265,19 +311,28 @@ static inline float round_f16(float v) {
 
 /* Decode one row of Q4_K into f16-rounded f32 weights (the values the
  * reference GPU multiplies). */
-static void decode_row_f16r(const uint8_t* row, int64_t N, float* w) {
+static void decode_row_f16r(const uint8_t* row, int64_t N, int fmt, float* w) {
   const int64_t nb = N / QK_K;
-  for (int64_t b = 0; b < nb; ++b) dequant_block_f32(row + b * Q4K_BLOCK_BYTES, w + b * QK_K);
+  for (int64_t b = 0; b < nb; ++b) {
+    if (fmt == 1)
+      dequant_q6k_block_f32(row + b * Q6K_BLOCK_BYTES, w + b * QK_K);
+    else
+      dequant_block_f32(row + b * Q4K_BLOCK_BYTES, w + b * QK_K);
+  }
   for (int64_t k = 0; k < N; ++k) w[k] = round_f16(w[k]);
+}
+
+static int64_t row_bytes_of(int64_t N, int fmt) {
+  return N / QK_K * (fmt == 1 ? Q6K_BLOCK_BYTES : Q4K_BLOCK_BYTES);
 }
 
 static void rows_q4k_gemv(void* p, int64_t m0, int64_t m1) {
   const gemv_args* a = (const gemv_args*)p;
-  const int64_t row_bytes = a->N / QK_K * Q4K_BLOCK_BYTES;
+  const int64_t row_bytes = row_bytes_of(a->N, a->fmt);
   float* y = (float*)a->y;
   float* w = (float*)malloc(sizeof(float) * (size_t)a->N);
   for (int64_t m = m0; m < m1; ++m) {
-    decode_row_f16r((const uint8_t*)a->w + m * row_bytes, a->N, w);
+    decode_row_f16r((const uint8_t*)a->w + m * row_bytes, a->N, a->fmt, w);
     for (int64_t b = 0; b < a->batch; ++b) y[b * a->M + m] = row_dot_wgsl(w, a->x + b * a->N, a->N);
   }
   free(w);
@@ -288,17 +343,25 @@ static void rows_q4k_gemv(void* p, int64_t m0, int64_t m1) {
  * Also the timed CPU baseline ("port"). */
 ORC_API void orc_q4k_gemv(const uint8_t* w_q4k, const float* x, float* y, int64_t M, int64_t N, int64_t batch,
                           int n_threads) {
-  gemv_args a = {w_q4k, x, y, NULL, M, N, batch};
+  gemv_args a = {w_q4k, x, y, NULL, M, N, batch, 0};
+  parallel_rows(rows_q4k_gemv, &a, M, n_threads);
+}
+
+/* The same for Q6_K bytes (GGUF layout, 210-byte super-blocks): decode
+ * (dequantizeQ6_K) -> RNE f16 -> the WGSL dot. */
+ORC_API void orc_q6k_gemv(const uint8_t* w_q6k, const float* x, float* y, int64_t M, int64_t N, int64_t batch,
+                          int n_threads) {
+  gemv_args a = {w_q6k, x, y, NULL, M, N, batch, 1};
   parallel_rows(rows_q4k_gemv, &a, M, n_threads);
 }
 
 static void rows_q4k_gemv_f64(void* p, int64_t m0, int64_t m1) {
   const gemv_args* a = (const gemv_args*)p;
-  const int64_t row_bytes = a->N / QK_K * Q4K_BLOCK_BYTES;
+  const int64_t row_bytes = row_bytes_of(a->N, a->fmt);
   double* y = (double*)a->y;
   float* w = (float*)malloc(sizeof(float) * (size_t)a->N);
   for (int64_t m = m0; m < m1; ++m) {
-    decode_row_f16r((const uint8_t*)a->w + m * row_bytes, a->N, w);
+    decode_row_f16r((const uint8_t*)a->w + m * row_bytes, a->N, a->fmt, w);
     if (a->wnorm) {
       double nrm = 0.0;
       for (int64_t k = 0; k < a->N; ++k) nrm += (double)w[k] * (double)w[k];
@@ -318,7 +381,13 @@ static void rows_q4k_gemv_f64(void* p, int64_t m0, int64_t m1) {
  * Also returns ||w_row||_2 per row (for the per-output tolerance term). */
 ORC_API void orc_q4k_gemv_f64(const uint8_t* w_q4k, const float* x, double* y, double* wnorm, int64_t M,
                               int64_t N, int64_t batch, int n_threads) {
-  gemv_args a = {w_q4k, x, y, wnorm, M, N, batch};
+  gemv_args a = {w_q4k, x, y, wnorm, M, N, batch, 0};
+  parallel_rows(rows_q4k_gemv_f64, &a, M, n_threads);
+}
+
+ORC_API void orc_q6k_gemv_f64(const uint8_t* w_q6k, const float* x, double* y, double* wnorm, int64_t M,
+                              int64_t N, int64_t batch, int n_threads) {
+  gemv_args a = {w_q6k, x, y, wnorm, M, N, batch, 1};
   parallel_rows(rows_q4k_gemv_f64, &a, M, n_threads);
 }
 

@@ -15,6 +15,11 @@ implementations of the algorithms it cites:
 * gemv_c0.npz -- config 0 (2048 x 1536, M=1): y computed in float64 from the
   gguf-py weights rounded to f16, plus a digest of the synthetic bytes so a
   generator change is caught.
+* q6k_blocks.npz -- Q6_K super-blocks (seeded random plus hand-built edge
+  cases: extreme int8 scales, every 6-bit quant, subnormal / huge / NaN d)
+  decoded by gguf-py's Q6_K.dequantize_blocks (llama.cpp's
+  dequantize_row_q6_K, the layout src/gguf.ts:316-368 decodes) and the RNE
+  f16 bit patterns of those values.
 * select.npz -- small logit vectors with planted ties, NaN and -1e30 entries,
   with argmax / per-residue max computed by a numpy restatement of
   shaders/argmax.wgsl and shaders/topk256.wgsl.
@@ -96,6 +101,51 @@ def make_blocks_fixture() -> None:
     np.savez_compressed(OUT / "q4k_blocks.npz", blocks=blocks, f32=f32, f16=f16)
 
 
+def q6k_edge_blocks() -> np.ndarray:
+    """Hand-built Q6_K super-blocks: ql | qh | int8 scales | f16 d."""
+    def blk(d, scales, ql, qh):
+        b = np.zeros(210, dtype=np.uint8)
+        b[0:128] = ql
+        b[128:192] = qh
+        b[192:208] = np.array(scales, dtype=np.int8).view(np.uint8)
+        b[208:210] = np.array([d], dtype=np.float16).view(np.uint8)
+        return b
+
+    rng = np.random.Generator(np.random.PCG64(17))
+    ramp_ql = np.arange(128, dtype=np.uint8) * 3
+    ramp_qh = np.arange(64, dtype=np.uint8) * 5
+    out = [np.zeros(210, dtype=np.uint8)]
+    out.append(blk(1.0, [1] * 16, ramp_ql, ramp_qh))                       # w = q - 32
+    out.append(blk(1.0, [-128] * 16, np.full(128, 0xFF, np.uint8), np.full(64, 0xFF, np.uint8)))  # q = 31
+    out.append(blk(1.0, [-128] * 16, np.zeros(128, np.uint8), np.zeros(64, np.uint8)))  # q = -32: 4096
+    out.append(blk(1.0, [127] * 16, ramp_ql, ramp_qh))                     # |sc*q| > 2048, odd products
+    out.append(blk(2.0 ** -10, list(range(-128, 128, 16)), ramp_ql, ramp_qh))
+    out.append(blk(6.0e-8, [127, -128] * 8, ramp_ql, ramp_qh))            # subnormal d
+    out.append(blk(3.0, [127] * 16, ramp_ql, ramp_qh))                     # results past f16 max -> inf
+    out.append(blk(1.0e-3, [-77, 91, 33, -5, 101, -128, 127, 1] * 2, rng.integers(0, 256, 128, dtype=np.uint8),
+                   rng.integers(0, 256, 64, dtype=np.uint8)))
+    b = blk(1.0, [1] * 16, ramp_ql, ramp_qh)                               # NaN d
+    b[208:210] = np.array([0x7E00], dtype=np.uint16).view(np.uint8)
+    out.append(b)
+    b = blk(1.0, [0] * 16, ramp_ql, ramp_qh)                               # inf d, sc = 0 -> NaN
+    b[208:210] = np.array([0x7C00], dtype=np.uint16).view(np.uint8)
+    out.append(b)
+    return np.stack(out)
+
+
+def make_q6k_fixture() -> None:
+    from gguf import quants
+    from gguf.constants import GGMLQuantizationType
+
+    rand = synth.make_q6k_blocks(64, np.random.Generator(np.random.PCG64(synth.seed_for(0, 998))))
+    wide = synth.make_q6k_blocks(32, np.random.Generator(np.random.PCG64(12)), d_sigma=0.05)
+    blocks = np.concatenate([q6k_edge_blocks(), rand, wide]).astype(np.uint8)
+    with np.errstate(all="ignore"):
+        f32 = quants.dequantize(blocks.reshape(-1), GGMLQuantizationType.Q6_K).astype(np.float32).reshape(-1)
+        f16 = f32.astype(np.float16).view(np.uint16)
+    np.savez_compressed(OUT / "q6k_blocks.npz", blocks=blocks, f32=f32, f16=f16)
+
+
 def make_gemv_fixture() -> None:
     M, N = 2048, 1536
     w = synth.q4k_matrix(M, N, synth.seed_for(0, 0))
@@ -165,6 +215,7 @@ def make_select_fixture() -> None:
 
 if __name__ == "__main__":
     make_blocks_fixture()
+    make_q6k_fixture()
     make_gemv_fixture()
     make_select_fixture()
     for f in sorted(OUT.glob("*.npz")):

@@ -153,3 +153,62 @@ def test_softcap_and_gelu(oracle):
     gd = g.astype(np.float64)
     ref = 0.5 * gd * (1 + np.tanh(np.clip(0.7978845608028654 * gd * (1 + 0.044715 * gd * gd), -15, 15))) * u
     assert np.max(np.abs(oracle.gelu_mul(g, u) - ref)) < 1e-5
+
+
+# ---- Q6_K (src/gguf.ts:316-368) ----------------------------------------------
+
+def test_q6k_dequant_f32_matches_gguf_py(oracle, golden_dir):
+    g = np.load(golden_dir / "q6k_blocks.npz")
+    out = oracle.q6k_dequant_f32(g["blocks"])
+    ref = g["f32"]
+    assert np.array_equal(np.isnan(out), np.isnan(ref))
+    m = ~np.isnan(ref)
+    assert np.array_equal(out[m].view(np.uint32), ref[m].view(np.uint32))
+
+
+def test_q6k_dequant_f16_matches_golden(oracle, golden_dir):
+    g = np.load(golden_dir / "q6k_blocks.npz")
+    assert _f16_equal(oracle.q6k_dequant_f16(g["blocks"]), g["f16"])
+
+
+def test_q6k_known_answer_positions(oracle):
+    """d = 1, every scale 1: element 128h + 32s + l is quant s of column l of
+    half h (4 bits of ql, 2 bits of qh) minus 32."""
+    rng = np.random.default_rng(3)
+    b = np.zeros(210, dtype=np.uint8)
+    ql = rng.integers(0, 256, 128, dtype=np.uint8)
+    qh = rng.integers(0, 256, 64, dtype=np.uint8)
+    b[0:128], b[128:192] = ql, qh
+    b[192:208] = 1
+    b[208:210] = np.array([1.0], dtype=np.float16).view(np.uint8)
+    w = oracle.q6k_dequant_f32(b)
+    for h in range(2):
+        for l in range(32):
+            lo0, lo1, hb = int(ql[64 * h + l]), int(ql[64 * h + 32 + l]), int(qh[32 * h + l])
+            q = [(lo0 & 15) | ((hb & 3) << 4), (lo1 & 15) | (((hb >> 2) & 3) << 4),
+                 (lo0 >> 4) | (((hb >> 4) & 3) << 4), (lo1 >> 4) | (((hb >> 6) & 3) << 4)]
+            for s in range(4):
+                assert w[128 * h + 32 * s + l] == q[s] - 32
+
+
+def test_q6k_scales_are_signed_per_16(oracle):
+    b = np.zeros(210, dtype=np.uint8)
+    b[0:192] = 0xFF                      # every quant 63 -> 31
+    sc = np.arange(-8, 8, dtype=np.int8) * 16
+    b[192:208] = sc.view(np.uint8)
+    b[208:210] = np.array([0.5], dtype=np.float16).view(np.uint8)
+    w = oracle.q6k_dequant_f32(b)
+    for j in range(16):
+        assert np.all(w[16 * j:16 * j + 16] == np.float32(0.5 * int(sc[j]) * 31))
+
+
+def test_q6k_gemv_matches_f64(oracle):
+    M, N = 64, 512
+    w = synth.q6k_matrix(M, N, 5)
+    x = synth.activations(2, N, 6)
+    y = oracle.q6k_gemv(w, x, M, N)
+    y64, wn = oracle.q6k_gemv_f64(w, x, M, N)
+    w16 = oracle.q6k_dequant_f16(w).view(np.float16).astype(np.float64).reshape(M, N)
+    assert np.allclose(y64, x.astype(np.float64) @ w16.T, rtol=1e-12, atol=1e-12)
+    assert np.allclose(wn, np.linalg.norm(w16, axis=1))
+    assert np.all(np.abs(y - y64) <= 1e-5 * wn[None, :] * np.linalg.norm(x, axis=1)[:, None])
