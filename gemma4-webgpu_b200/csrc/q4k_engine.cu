@@ -33,6 +33,7 @@
 #include "q4k_device.cuh"
 #include "q4k_engine.cuh"
 #include "q4k_ptx.cuh"
+#include "q6k_dequant.cuh"
 
 namespace q4k {
 namespace {
@@ -272,16 +273,39 @@ __global__ void __launch_bounds__(256) xprep_kernel(const JobList jl, uint32_t b
 
 // ---- the engine kernel ----------------------------------------------------------
 
-constexpr int kStages = 2;        // stages in flight per warp
-constexpr int kBlocksPerStage = 2;  // super-blocks per stage (per tile row)
-
-// A stage holds one weight-map box: 16 tile rows of 2 super-blocks plus 16
-// bytes (the box width; 144 bytes for one-block rows), so the 8 rows a
-// quarter-warp reads land in distinct banks.
+// Per-warp weight pipeline of each format.
+//
+// Q4_K: a stage holds one weight-map box: 16 tile rows of 2 super-blocks
+// plus 16 bytes (the box width; 144 bytes for one-block rows), so the 8 rows
+// a quarter-warp reads land in distinct banks; 2 stages in flight.
+// Q6_K: a stage holds one 208-byte body of each of the 16 rows (rows 52
+// words apart: conflict-free) and the rows' 16 f16 d values behind them; 3
+// stages in flight (about the same bytes as Q4_K's 2 x 2 super-blocks).
 constexpr uint32_t kBoxWords2 = 2 * kBlockBytes / 4 + 4;  // 76 words = 304 bytes
 constexpr uint32_t kBoxWords1 = kBlockBytes / 4;          // 36 words = 144 bytes
-constexpr uint32_t kStageBytes = kTileRows * kBoxWords2 * 4;
-constexpr size_t kWeightSmem = (size_t)kEngineWarps * kStages * kStageBytes;
+
+template <int FMT>
+struct Pipe;
+template <>
+struct Pipe<kFmtQ4K> {
+  static constexpr int kStages = 2;
+  static constexpr uint32_t kBlocks = 2;  // super-blocks per stage (per tile row)
+  static constexpr uint32_t kStageBytes = kTileRows * kBoxWords2 * 4;
+};
+template <>
+struct Pipe<kFmtQ6K> {
+  static constexpr int kStages = 3;
+  static constexpr uint32_t kBlocks = 1;
+  static constexpr uint32_t kDOff = kTileRows * kQ6BodyBytes;  // 3328: the d values (128-byte aligned)
+  static constexpr uint32_t kTxBytes = kDOff + kTileRows * 2;   // bytes the two copies deliver
+  static constexpr uint32_t kStageBytes = (kTxBytes + 127u) & ~127u;  // stages stay 128-byte aligned
+};
+constexpr int kMaxStages = 3;
+
+template <int FMT>
+constexpr size_t weight_smem() {
+  return (size_t)kEngineWarps * Pipe<FMT>::kStages * Pipe<FMT>::kStageBytes;
+}
 constexpr size_t kSelectSmem = (size_t)kEngineWarps * 256 * 8;
 constexpr size_t kTaskSmem = (size_t)kMaxCtaTasks * sizeof(EngineTask);
 constexpr size_t kSmemLimit = 227 * 1024;
@@ -292,7 +316,8 @@ constexpr size_t kStaticSmemHeadroom = 4096;
 struct TaskSrc {
   const EngineTask* table;
   uint32_t t0;
-  const CUtensorMap* pmap;  // the launch's own weight map (inline task)
+  const CUtensorMap* pmap;   // the launch's own weight map (inline task)
+  const CUtensorMap* pdmap;  // and its Q6_K d-plane map
 };
 
 __device__ __forceinline__ EngineTask task_get(const TaskList& tl, const TaskSrc& ts, uint32_t i) {
@@ -303,6 +328,7 @@ __device__ __forceinline__ EngineTask task_get(const TaskList& tl, const TaskSrc
 struct Cursor {
   uint32_t item, b, b_hi, ti;
   const CUtensorMap* map;
+  const CUtensorMap* dmap;  // Q6_K: the d-plane map
   uint32_t tile_bytes, nb, item_begin, item_end;
 };
 
@@ -317,6 +343,7 @@ __device__ __forceinline__ void cursor_range(Cursor& cu, uint32_t q, uint32_t ks
 __device__ __forceinline__ void cursor_task(Cursor& cu, const TaskList& tl, const TaskSrc& ts) {
   const EngineTask T = task_get(tl, ts, cu.ti);
   cu.map = T.tmap ? T.tmap : ts.pmap;
+  cu.dmap = T.tmap ? T.tmap + 1 : ts.pdmap;
   cu.tile_bytes = T.tile_bytes;
   cu.nb = T.N >> 8;
   cu.item_begin = T.item_begin;
@@ -330,18 +357,30 @@ __device__ __forceinline__ void cursor_seek(Cursor& cu, const TaskList& tl, cons
   }
 }
 
-// Super-blocks of the cursor's stage: up to kBlocksPerStage, not past the range.
+// Super-blocks of the cursor's stage: up to the format's per-stage count,
+// not past the range.
+template <int FMT>
 __device__ __forceinline__ uint32_t cursor_blocks(const Cursor& cu) {
-  return min((uint32_t)kBlocksPerStage, cu.b_hi - cu.b);
+  return min(Pipe<FMT>::kBlocks, cu.b_hi - cu.b);
 }
 
-// Lane 0 copies the tile's super-blocks b, b+1 of its 16 rows (one map box,
-// rows tile_bytes apart) into the stage and arms the stage's barrier with the
-// box size; rows past M and words past the row end arrive as zeros.
+// Lane 0 copies the stage's tile data and arms the stage's barrier with its
+// size.  Q4_K: super-blocks b, b+1 of the tile's 16 rows (one map box, rows
+// tile_bytes apart).  Q6_K: body b of the 16 rows (one box) and their 16 d
+// values (one box of the d plane).  Rows past M and words past the row end
+// arrive as zeros.
+template <int FMT>
 __device__ __forceinline__ void issue_stage(const Cursor& cu, uint8_t* stage, uint64_t* bar, uint32_t lane) {
   if (lane == 0) {
-    mbar_arrive_expect_tx(bar, kTileRows * cu.tile_bytes);
-    tma_tile_g2s(stage, cu.map, cu.b * (kBlockBytes / 4), (cu.item - cu.item_begin) * kTileRows, bar);
+    const uint32_t row0 = (cu.item - cu.item_begin) * kTileRows;
+    if constexpr (FMT == kFmtQ6K) {
+      mbar_arrive_expect_tx(bar, Pipe<kFmtQ6K>::kTxBytes);
+      tma_tile_g2s(stage, cu.map, cu.b * kQ6BodyWords, row0, bar);
+      tma_tile_g2s(stage + Pipe<kFmtQ6K>::kDOff, cu.dmap, row0, cu.b, bar);
+    } else {
+      mbar_arrive_expect_tx(bar, kTileRows * cu.tile_bytes);
+      tma_tile_g2s(stage, cu.map, cu.b * (kBlockBytes / 4), row0, bar);
+    }
   }
 }
 
@@ -398,6 +437,64 @@ __device__ __forceinline__ void block_math(float (&acc)[NT][2][4], const BlockRe
   }
 }
 
+// One Q6_K super-block of the lane's two rows in a stage: the rows' bodies,
+// the lane's scale words and the rows' d values (the ql / qh words are read
+// per 16-column half inside the math, so they never all sit in registers).
+struct Q6Rows {
+  const uint8_t* ra;
+  const uint8_t* rb;
+  uint32_t sa, sb;
+  uint16_t da, db;
+};
+
+__device__ __forceinline__ Q6Rows q6_rows(const uint8_t* stg, uint32_t g, uint32_t c) {
+  Q6Rows r;
+  r.ra = stg + g * kQ6BodyBytes;
+  r.rb = stg + (g + 8) * kQ6BodyBytes;
+  r.sa = *reinterpret_cast<const uint32_t*>(r.ra + 192 + 4 * c);
+  r.sb = *reinterpret_cast<const uint32_t*>(r.rb + 192 + 4 * c);
+  const uint16_t* dv = reinterpret_cast<const uint16_t*>(stg + kTileRows * kQ6BodyBytes);
+  r.da = dv[g];
+  r.db = dv[g + 8];
+  return r;
+}
+
+__device__ __forceinline__ uint32_t u4_word(const uint4& a, int w) {
+  return w == 0 ? a.x : (w == 1 ? a.y : (w == 2 ? a.z : a.w));
+}
+
+// The math of one Q6_K super-block: 2 rows x 64 weights per lane, words in
+// the Q4_K order (word w = 4*is + j of the lane's half), same B fragments.
+template <int NT, int COLS, bool SX, bool EXACT>
+__device__ __forceinline__ void q6_block_math(float (&acc)[NT][2][4], const Q6Rows& R, uint32_t c,
+                                              const uint64_t (&base)[NT], const uint32_t (&wstep)[NT]) {
+  const uint32_t sh = (c & 1u) * 4u, h = c >> 1;
+  const float d4a = 4.0f * __half2float(__ushort_as_half(R.da));
+  const float d4b = 4.0f * __half2float(__ushort_as_half(R.db));
+#pragma unroll
+  for (int is = 0; is < 2; ++is) {
+    const uint4 la0 = lds128(R.ra + 64 * h + 16 * is), la1 = lds128(R.ra + 64 * h + 32 + 16 * is);
+    const uint4 ha = lds128(R.ra + 128 + 32 * h + 16 * is);
+    const uint4 lb0 = lds128(R.rb + 64 * h + 16 * is), lb1 = lds128(R.rb + 64 * h + 32 + 16 * is);
+    const uint4 hb = lds128(R.rb + 128 + 32 * h + 16 * is);
+    const Q6Consts ka = q6_consts(R.sa, is, d4a);
+    const Q6Consts kb = q6_consts(R.sb, is, d4b);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int w = 4 * is + j;
+      const WordPairs A = dequant6_word<EXACT>(u4_word(la0, j), u4_word(la1, j), u4_word(ha, j), sh, ka);
+      const WordPairs B = dequant6_word<EXACT>(u4_word(lb0, j), u4_word(lb1, j), u4_word(hb, j), sh, kb);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint32_t ws = COLS > 0 ? (uint32_t)COLS * 64u : wstep[n];
+        const uint4 f = load_frag<SX>(base[n] + (uint64_t)(w * ws));
+        mma_16816(acc[n][0], A.lo02, B.lo02, A.lo13, B.lo13, make_uint2(f.x, f.y));
+        mma_16816(acc[n][1], A.hi02, B.hi02, A.hi13, B.hi13, make_uint2(f.z, f.w));
+      }
+    }
+  }
+}
+
 // The task fields the math loop keeps in registers.
 template <int NT>
 struct Hot {
@@ -434,14 +531,17 @@ __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts,
   return h;
 }
 
-template <int NT, int COLS, int KS>
+template <int NT, int COLS, int KS, int FMT>
 __global__ void __launch_bounds__(kEngineWarps * 32, 1)
-    engine_kernel(const TaskList tl, const __grid_constant__ CUtensorMap wmap, uint32_t batch, int has_select,
-                  SelectScratch sel, uint32_t xcache_cap) {
+    engine_kernel(const TaskList tl, const __grid_constant__ CUtensorMap wmap,
+                  const __grid_constant__ CUtensorMap dmap, uint32_t batch, int has_select, SelectScratch sel,
+                  uint32_t xcache_cap) {
+  constexpr int kSt = Pipe<FMT>::kStages;
+  constexpr uint32_t kSB = Pipe<FMT>::kStageBytes;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // tile copies land on 128-byte boundaries
   uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
-  __shared__ uint64_t s_bar[kEngineWarps][kStages];
+  __shared__ uint64_t s_bar[kEngineWarps][kMaxStages];
   __shared__ uint64_t s_xbar;
   __shared__ CtaSched s_sched;
   __shared__ uint32_t s_next;                    // next unclaimed item of this CTA's range
@@ -454,9 +554,9 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   const uint32_t g = lane >> 2, c = lane & 3u;
   // bytes (2(c&1), 2(c&1)+1) of a packed scale word -> bytes 0 and 2
   const uint32_t bsel = scale_sel(c);
-  uint8_t* wsm = smem + warp * (kStages * kStageBytes);
-  EngineTask* s_tasks = reinterpret_cast<EngineTask*>(smem + kWeightSmem);
-  uint8_t* xsm = smem + kWeightSmem + kTaskSmem;
+  uint8_t* wsm = smem + warp * (kSt * kSB);
+  EngineTask* s_tasks = reinterpret_cast<EngineTask*>(smem + weight_smem<FMT>());
+  uint8_t* xsm = smem + weight_smem<FMT>() + kTaskSmem;
   float* s_bv = reinterpret_cast<float*>(xsm + xcache_cap) + warp * 512;
   uint32_t* s_bi = reinterpret_cast<uint32_t*>(s_bv + 256);
   uint64_t* bars = s_bar[warp];
@@ -466,7 +566,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   // previous kernel wrote: wait for it before anything else
   if (!tl.prep) wait_prior_grids();
   if (lane == 0)
-    for (int st = 0; st < kStages; ++st) mbar_init(&bars[st], 1);
+    for (int st = 0; st < kSt; ++st) mbar_init(&bars[st], 1);
   if (threadIdx.x == 0) mbar_init(&s_xbar, 1);
   // K-split launches (tl.ksplit = KS > 1): the KS warps of a group take the
   // same tiles, each a 1/KS slice of the row's super-blocks, and add their
@@ -524,6 +624,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   ts.table = !tl.dev ? nullptr : (s_sched.nt ? s_tasks : tl.dev);
   ts.t0 = s_sched.nt ? s_sched.t0 : 0u;
   ts.pmap = &wmap;
+  ts.pdmap = &dmap;
   const uint32_t t_first = s_sched.nt ? s_sched.t0 : 0u;
 
   // Items are claimed from the CTA's range by the copy cursor (a shared
@@ -548,9 +649,9 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   cursor_seek(F, tl, ts, c1);
   cursor_range(F, gq, ks_n);
   uint32_t issued = 0;
-  for (int st = 0; st < kStages && F.item < c1; ++st) {
-    issue_stage(F, wsm + st * kStageBytes, &bars[st], lane);
-    F.b += cursor_blocks(F);
+  for (int st = 0; st < kSt && F.item < c1; ++st) {
+    issue_stage<FMT>(F, wsm + st * kSB, &bars[st], lane);
+    F.b += cursor_blocks<FMT>(F);
     if (F.b == F.b_hi) {
       F.item = claim();
       cursor_seek(F, tl, ts, c1);
@@ -604,15 +705,49 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     for (int h = 0; h < 2; ++h) acc[n][h][0] = acc[n][h][1] = acc[n][h][2] = acc[n][h][3] = 0.0f;
 
   while (item < c1 && !timed_out) {
-    const uint32_t slot = k % kStages;
-    if (!mbar_wait(&bars[slot], (k / kStages) & 1u)) {
+    const uint32_t slot = k % kSt;
+    if (!mbar_wait(&bars[slot], (k / kSt) & 1u)) {
       timed_out = true;
       break;
     }
-    const uint32_t nblk = min((uint32_t)kBlocksPerStage, b_hi - b);
-    const uint8_t* stg = wsm + slot * kStageBytes;
-    const uint32_t rs = H.tile_bytes;
+    const uint8_t* stg = wsm + slot * kSB;
     const bool sx = H.xs != 0xffffffffu;
+    if constexpr (FMT == kFmtQ6K) {
+      // one super-block per stage: compute straight from the stage (the
+      // other stages stay in flight meanwhile), then hand it back
+      const Q6Rows R = q6_rows(stg, g, c);
+      uint64_t base[NT];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint32_t off = n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n];
+        base[n] = sx ? (uint64_t)(xs_base + H.xs + off)
+                     : reinterpret_cast<uint64_t>(reinterpret_cast<const uint8_t*>(H.xfrag) + off);
+      }
+      // a non-finite d anywhere in the warp's rows: the exact (slower) form
+      const bool odd_d = ((R.da & 0x7C00u) == 0x7C00u) || ((R.db & 0x7C00u) == 0x7C00u);
+      if (__any_sync(0xffffffffu, odd_d)) {
+        if (sx) q6_block_math<NT, COLS, true, true>(acc, R, c, base, wstep);
+        else q6_block_math<NT, COLS, false, true>(acc, R, c, base, wstep);
+      } else {
+        if (sx) q6_block_math<NT, COLS, true, false>(acc, R, c, base, wstep);
+        else q6_block_math<NT, COLS, false, false>(acc, R, c, base, wstep);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (F.item < c1) {
+        issue_stage<FMT>(F, wsm + slot * kSB, &bars[slot], lane);
+        F.b += cursor_blocks<FMT>(F);
+        if (F.b == F.b_hi) {
+          F.item = claim();
+          cursor_seek(F, tl, ts, c1);
+          cursor_range(F, gq, ks_n);
+        }
+        ++issued;
+      }
+      ++b;
+    } else {
+    const uint32_t nblk = min(Pipe<FMT>::kBlocks, b_hi - b);
+    const uint32_t rs = H.tile_bytes;
 #pragma unroll 1
     for (uint32_t sb = 0; sb < nblk; ++sb, ++b) {
       const BlockRegs R = read_block(stg + g * rs + sb * kBlockBytes, stg + (g + 8) * rs + sb * kBlockBytes, c);
@@ -621,8 +756,8 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (F.item < c1) {
-          issue_stage(F, wsm + slot * kStageBytes, &bars[slot], lane);
-          F.b += cursor_blocks(F);
+          issue_stage<FMT>(F, wsm + slot * kSB, &bars[slot], lane);
+          F.b += cursor_blocks<FMT>(F);
           if (F.b == F.b_hi) {
             F.item = claim();
             cursor_seek(F, tl, ts, c1);
@@ -643,6 +778,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
         block_math<NT, COLS, true>(acc, R, c, bsel, base, wstep);
       else
         block_math<NT, COLS, false>(acc, R, c, bsel, base, wstep);
+    }
     }
     ++k;
     if (b < b_hi) continue;
@@ -732,7 +868,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   if (timed_out) {
     // record the failure, then let every copy still in flight land (bounded)
     if (lane == 0) atomicOr(sel.status, 1u);
-    for (uint32_t j = k; j < issued; ++j) mbar_wait(&bars[j % kStages], (j / kStages) & 1u);
+    for (uint32_t j = k; j < issued; ++j) mbar_wait(&bars[j % kSt], (j / kSt) & 1u);
   }
 
   if (!has_select) return;
@@ -870,20 +1006,23 @@ constexpr size_t kPartSmem = (size_t)2 * kEngineWarps * kTileRows * 4 * sizeof(f
 
 // hs: the launch has an LM head (per-warp candidate tables); else the same
 // space holds K-split partial sums.
+template <int FMT>
 size_t xcache_bytes(int hs) {
-  return kSmemLimit - kStaticSmemHeadroom - kAlignSlack - kWeightSmem - kTaskSmem - (hs ? kSelectSmem : kPartSmem);
+  return kSmemLimit - kStaticSmemHeadroom - kAlignSlack - weight_smem<FMT>() - kTaskSmem -
+         (hs ? kSelectSmem : kPartSmem);
 }
 
-template <int NT, int COLS, int KS = 1>
-cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, int hs,
-                           const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
-  const size_t xcap = xcache_bytes(hs);
-  const size_t smem = kAlignSlack + kWeightSmem + kTaskSmem + xcap + (hs ? kSelectSmem : kPartSmem);
+template <int NT, int COLS, int KS = 1, int FMT = kFmtQ4K>
+cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, const CUtensorMap& dmap, uint32_t batch,
+                           int hs, const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
+  const size_t xcap = xcache_bytes<FMT>(hs);
+  const size_t smem = kAlignSlack + weight_smem<FMT>() + kTaskSmem + xcap + (hs ? kSelectSmem : kPartSmem);
   static int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS, FMT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(kSmemLimit - kStaticSmemHeadroom));
     if (e != cudaSuccess) return e;
     attr_dev = dev;
@@ -898,7 +1037,8 @@ cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, uint32
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, engine_kernel<NT, COLS, KS>, tasks, map, batch, hs, sel, (uint32_t)xcap);
+  return cudaLaunchKernelEx(&cfg, engine_kernel<NT, COLS, KS, FMT>, tasks, map, dmap, batch, hs, sel,
+                            (uint32_t)xcap);
 }
 
 }  // namespace
@@ -919,7 +1059,10 @@ uint32_t engine_grid(uint32_t total_items, int sm_count) {
   return grid == 0 ? 1 : grid;
 }
 
-uint32_t engine_xcache_bytes(bool has_select) { return (uint32_t)xcache_bytes(has_select ? 1 : 0); }
+uint32_t engine_xcache_bytes(bool has_select, uint32_t fmt) {
+  return (uint32_t)(fmt == kFmtQ6K ? xcache_bytes<kFmtQ6K>(has_select ? 1 : 0)
+                                   : xcache_bytes<kFmtQ4K>(has_select ? 1 : 0));
+}
 
 namespace {
 using EncodeTiledFn = decltype(&cuTensorMapEncodeTiled);
@@ -960,6 +1103,35 @@ cudaError_t encode_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint3
     }
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t encode_q6k_maps(CUtensorMap* maps, const void* w, uint32_t M, uint32_t N, uint32_t* tile_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const uint64_t nb = N / kQK;
+  const cuuint32_t estr[2] = {1, 1};
+  {
+    const cuuint64_t dims[2] = {nb * kQ6BodyWords, M};
+    const cuuint64_t strides[1] = {nb * kQ6BodyBytes};
+    const cuuint32_t box[2] = {kQ6BodyWords, (cuuint32_t)kTileRows};
+    if (fn(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    const uint32_t mp = q6k_dpitch(M);
+    void* dp = static_cast<uint8_t*>(const_cast<void*>(w)) + (uint64_t)M * nb * kQ6BodyBytes;
+    const cuuint64_t dims[2] = {mp, nb};
+    const cuuint64_t strides[1] = {(cuuint64_t)mp * 2u};
+    const cuuint32_t box[2] = {(cuuint32_t)kTileRows, 1};
+    if (fn(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, dp, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  *tile_bytes = kQ6BodyBytes;
+  return cudaSuccess;
 }
 
 // First work item whose super-blocks start at or after cost position p.
@@ -1019,31 +1191,43 @@ bool schedule_covers_tasks(const EngineTask* tasks, uint32_t n, const CtaSched* 
   return true;
 }
 
+template <int FMT>
+cudaError_t launch_fmt(const TaskList& tasks, const CUtensorMap& map, const CUtensorMap& dmap, uint32_t batch,
+                       int hs, const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
+  switch (batch) {
+    case 1: return launch_variant<1, 2, 1, FMT>(tasks, map, dmap, batch, hs, sel, grid, s);
+    case 2: return launch_variant<1, 4, 1, FMT>(tasks, map, dmap, batch, hs, sel, grid, s);
+    case 3: return launch_variant<1, 6, 1, FMT>(tasks, map, dmap, batch, hs, sel, grid, s);
+    case 4: return launch_variant<1, 8, 1, FMT>(tasks, map, dmap, batch, hs, sel, grid, s);
+    default:
+      switch ((batch + 3) / 4) {
+        case 2: return launch_variant<2, 0, 1, FMT>(tasks, map, dmap, batch, hs, sel, grid, s);
+        case 3: return launch_variant<3, 0, 1, FMT>(tasks, map, dmap, batch, hs, sel, grid, s);
+        default: return launch_variant<4, 0, 1, FMT>(tasks, map, dmap, batch, hs, sel, grid, s);
+      }
+  }
+}
+
 cudaError_t launch_engine(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, bool has_select,
-                          const SelectScratch& sel, int sm_count, cudaStream_t s) {
+                          const SelectScratch& sel, int sm_count, cudaStream_t s, const CUtensorMap* dmap) {
   const uint32_t grid = tasks.sched ? tasks.grid : engine_grid(tasks.total_items, sm_count);
   const int hs = has_select ? 1 : 0;
+  const CUtensorMap& dm = dmap ? *dmap : map;
+  if (tasks.fmt == kFmtQ6K) {
+    if (tasks.ksplit > 1) return cudaErrorInvalidValue;
+    return launch_fmt<kFmtQ6K>(tasks, map, dm, batch, hs, sel, grid, s);
+  }
+  if (tasks.fmt != kFmtQ4K) return cudaErrorInvalidValue;
   if (tasks.ksplit == 4) {
     switch (batch) {
-      case 1: return launch_variant<1, 2, 4>(tasks, map, batch, hs, sel, grid, s);
-      case 2: return launch_variant<1, 4, 4>(tasks, map, batch, hs, sel, grid, s);
-      case 3: return launch_variant<1, 6, 4>(tasks, map, batch, hs, sel, grid, s);
-      case 4: return launch_variant<1, 8, 4>(tasks, map, batch, hs, sel, grid, s);
+      case 1: return launch_variant<1, 2, 4>(tasks, map, dm, batch, hs, sel, grid, s);
+      case 2: return launch_variant<1, 4, 4>(tasks, map, dm, batch, hs, sel, grid, s);
+      case 3: return launch_variant<1, 6, 4>(tasks, map, dm, batch, hs, sel, grid, s);
+      case 4: return launch_variant<1, 8, 4>(tasks, map, dm, batch, hs, sel, grid, s);
       default: return cudaErrorInvalidValue;
     }
   }
-  switch (batch) {
-    case 1: return launch_variant<1, 2>(tasks, map, batch, hs, sel, grid, s);
-    case 2: return launch_variant<1, 4>(tasks, map, batch, hs, sel, grid, s);
-    case 3: return launch_variant<1, 6>(tasks, map, batch, hs, sel, grid, s);
-    case 4: return launch_variant<1, 8>(tasks, map, batch, hs, sel, grid, s);
-    default:
-      switch ((batch + 3) / 4) {
-        case 2: return launch_variant<2, 0>(tasks, map, batch, hs, sel, grid, s);
-        case 3: return launch_variant<3, 0>(tasks, map, batch, hs, sel, grid, s);
-        default: return launch_variant<4, 0>(tasks, map, batch, hs, sel, grid, s);
-      }
-  }
+  return launch_fmt<kFmtQ4K>(tasks, map, dm, batch, hs, sel, grid, s);
 }
 
 }  // namespace q4k

@@ -26,6 +26,10 @@ __host__ __device__ inline size_t xfrag_bytes(uint32_t N, uint32_t batch) { retu
 
 enum TaskKind : uint32_t { kTaskPlain = 0, kTaskSelect = 1 };
 
+// Weight format of every task of an engine launch: Q4_K as GGUF stores it,
+// or Q6_K in the device layout of q6k_dequant.cuh.
+enum WeightFormat : uint32_t { kFmtQ4K = 0, kFmtQ6K = 1 };
+
 // One GEMV of an engine launch: y[t*M + m] = sum_k w16[m,k] * x[t,k].
 struct alignas(16) EngineTask {
   const uint8_t* w;         // Q4_K [M][N/256*144]
@@ -42,7 +46,8 @@ struct alignas(16) EngineTask {
   uint32_t kind;
   uint32_t row_offset;      // kTaskSelect: global index of row 0
   float cap;                // kTaskSelect: softcap (<= 0: none)
-  const CUtensorMap* tmap;  // TMA map of w (device memory); null: the launch's own map
+  const CUtensorMap* tmap;  // TMA map of w (device memory; Q6_K: the body map, the d-plane map
+                            // follows it); null: the launch's own map(s)
   uint32_t tile_bytes;      // bytes per tile row in a weight stage (the map's box width)
   uint32_t aux;             // host-side bookkeeping while a plan is laid out
 };
@@ -113,7 +118,8 @@ struct TaskList {
   uint32_t grid;        // CTAs the schedule was made for
   uint32_t select_task; // index of the kTaskSelect task, if the launch has one
   uint32_t ksplit;      // > 1: KS warps share each tile, one K slice each (plain tasks, batch <= 4,
-                        // every task's N/256 a multiple of KS)
+                        // every task's N/256 a multiple of KS; Q4_K only)
+  uint32_t fmt;         // WeightFormat of every task
   Exchange xc;          // LM-head candidate exchange across ranks (xc.world > 0)
 };
 
@@ -130,6 +136,12 @@ struct JobList {
 // read as zeros.  *tile_bytes = the box width in bytes.
 cudaError_t encode_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N, uint32_t* tile_bytes);
 
+// A Q6_K matrix in the device layout as two TMA tensors: maps[0] the bodies
+// as 32-bit words [M rows][N/256*52 words], read in boxes of 16 rows x one
+// 208-byte body; maps[1] the d plane as f16 [N/256][Mp], read in boxes of
+// 16 rows of one super-block column.  *tile_bytes = 208.
+cudaError_t encode_q6k_maps(CUtensorMap* maps, const void* w, uint32_t M, uint32_t N, uint32_t* tile_bytes);
+
 // Schedule cost of one work item (16 rows) of a task: its super-blocks per
 // row, in units of 1/20; LM-head items (softcap + per-residue selection in
 // the epilogue) count 5 % more.
@@ -140,7 +152,7 @@ __host__ __device__ inline uint32_t item_cost(uint32_t N, uint32_t kind) {
 // Engine launch geometry: CTAs for a work list, and the shared-memory
 // activation cache each CTA has (depends on whether an LM head is present).
 uint32_t engine_grid(uint32_t total_items, int sm_count);
-uint32_t engine_xcache_bytes(bool has_select);
+uint32_t engine_xcache_bytes(bool has_select, uint32_t fmt = kFmtQ4K);
 
 // Host-side schedule of a device task list (tasks sorted by item_begin):
 // equal shares of super-blocks per CTA, and what each CTA stages.
@@ -152,9 +164,10 @@ void engine_schedule(const EngineTask* tasks, uint32_t n, uint32_t total_cost, u
 bool schedule_covers_tasks(const EngineTask* tasks, uint32_t n, const CtaSched* sched, uint32_t grid);
 
 cudaError_t launch_xprep(const JobList& jobs, uint32_t batch, cudaStream_t s);
-// `map`: the weight map of an inline task (tasks.dev == null); ignored for
-// device task lists, whose tasks carry their own maps.
+// `map` (and for Q6_K `dmap`, the d-plane map): the weight maps of an inline
+// task (tasks.dev == null); ignored for device task lists, whose tasks carry
+// their own maps.
 cudaError_t launch_engine(const TaskList& tasks, const CUtensorMap& map, uint32_t batch, bool has_select,
-                          const SelectScratch& sel, int sm_count, cudaStream_t s);
+                          const SelectScratch& sel, int sm_count, cudaStream_t s, const CUtensorMap* dmap = nullptr);
 
 }  // namespace q4k

@@ -42,6 +42,11 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_exchange_open": ([_P, _U32, _P], _I),
     "q4k_exchange_destroy": ([_P], None),
     "q4k_lmhead_select_sharded": ([_P, _P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P], _I),
+    "q4k_q6k_device_bytes": ([_U32, _U32], _U64),
+    "q4k_q6k_repack": ([_P, _P, _P, _U32, _U32, _P], _I),
+    "q4k_q6k_dequant_f16": ([_P, _P, _U32, _U32, _P, _P], _I),
+    "q4k_q6k_gemv": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
+    "q4k_q6k_lmhead_select": ([_P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_plan_create": ([_P, _U32, ctypes.POINTER(_P)], _I),
     "q4k_plan_destroy": ([_P], None),
     "q4k_plan_gemv": ([_P, _U32, _P, _P, _P, _U32, _U32], _I),

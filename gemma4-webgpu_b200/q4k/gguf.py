@@ -103,6 +103,16 @@ class GGUFFile:
             raise GGUFError(f"{t.name}: data [{start}, {end}) past the end of the file ({len(self._buf)} bytes)")
         return np.frombuffer(self._buf, dtype=np.uint8, count=t.nbytes, offset=start)
 
+    def q6k_matrix(self, name: str) -> tuple[np.ndarray, int, int]:
+        """A Q6_K matrix's GGUF bytes: (bytes [M, N/256*210], M, N)."""
+        t = self.by_name[name]
+        if t.type != TYPE_Q6_K:
+            raise GGUFError(f"{name} is {TYPE_NAMES.get(t.type, t.type)}, not Q6_K")
+        M, N = t.matrix_shape
+        if N % 256:
+            raise GGUFError(f"{name}: N={N} is not a multiple of 256")
+        return self.tensor_bytes(t).reshape(M, N // 256 * 210), M, N
+
     def q4k_matrix(self, name: str) -> tuple[np.ndarray, int, int]:
         """A Q4_K matrix as libq4k takes it: (bytes [M, N/256*144], M, N)."""
         t = self.by_name[name]
@@ -189,3 +199,13 @@ def upload_q4k(f: GGUFFile, name: str, device) -> tuple["torch.Tensor", int, int
 
     raw, M, N = f.q4k_matrix(name)
     return torch.from_numpy(np.array(raw)).to(device), M, N
+
+
+def upload_q6k(f: GGUFFile, name: str, ctx) -> tuple["torch.Tensor", int, int]:  # noqa: F821
+    """A Q6_K matrix into the device layout on ctx's device (copy the GGUF
+    bytes, then q4k_q6k_repack): (tensor, M, N)."""
+    import torch
+
+    raw, M, N = f.q6k_matrix(name)
+    src = torch.from_numpy(np.array(raw)).to(ctx.device)
+    return ctx.q6k_repack(src, M, N), M, N

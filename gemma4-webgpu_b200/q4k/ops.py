@@ -22,6 +22,7 @@ from ._lib import Q4KError
 
 QK_K = 256
 BLOCK_BYTES = 144
+Q6K_BLOCK_BYTES = 210
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -159,6 +160,81 @@ class Context:
         nb = weight.numel() // BLOCK_BYTES
         out = torch.empty(nb * QK_K, dtype=torch.int16, device=self.device)
         self._check(self._L.q4k_dequant_f16(self._h, _ptr(weight), _ptr(out), nb, _stream(stream)))
+        return out
+
+    # ---- Q6_K matrices (device layout; see include/q4k.h) ---------------------
+
+    def q6k_device_bytes(self, M: int, N: int) -> int:
+        """Bytes of the device layout of an M x N Q6_K matrix."""
+        if N % QK_K:
+            raise ValueError(f"N={N} is not a multiple of {QK_K}")
+        return int(self._L.q4k_q6k_device_bytes(M, N))
+
+    def q6k_repack(self, w_gguf: torch.Tensor, M: int, N: int, out: torch.Tensor | None = None,
+                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """GGUF Q6_K bytes (uint8, M*N/256*210, on the device) -> the device
+        layout the Q6_K calls read: the load-time step that replaces the
+        reference's dequantizeQ6_K + f32ToF16Array upload."""
+        _need(w_gguf, torch.uint8, "w_gguf", self.device)
+        if w_gguf.numel() < M * (N // QK_K) * Q6K_BLOCK_BYTES:
+            raise ValueError("w_gguf smaller than M*N/256*210 bytes")
+        nbytes = self.q6k_device_bytes(M, N)
+        if out is None:
+            out = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        _need(out, torch.uint8, "out", self.device)
+        if out.numel() < nbytes:
+            raise ValueError(f"out smaller than {nbytes} bytes")
+        self._check(self._L.q4k_q6k_repack(self._h, _ptr(w_gguf), _ptr(out), M, N, _stream(stream)))
+        return out
+
+    def _need_q6(self, w_dev: torch.Tensor, M: int, N: int) -> None:
+        _need(w_dev, torch.uint8, "w_dev", self.device)
+        if w_dev.numel() < self.q6k_device_bytes(M, N):
+            raise ValueError("w_dev smaller than q6k_device_bytes(M, N)")
+
+    def q6k_dequant_f16(self, w_dev: torch.Tensor, M: int, N: int,
+                        stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """The f16 weights (int16 bit patterns, [M, N]) the Q6_K GEMV multiplies."""
+        self._need_q6(w_dev, M, N)
+        out = torch.empty((M, N), dtype=torch.int16, device=self.device)
+        self._check(self._L.q4k_q6k_dequant_f16(self._h, _ptr(w_dev), M, N, _ptr(out), _stream(stream)))
+        return out
+
+    def q6k_gemv(self, w_dev: torch.Tensor, x: torch.Tensor, M: int, N: int, out: torch.Tensor | None = None,
+                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """y[b, m] for a Q6_K matrix in the device layout, x [batch, N] (or [N])."""
+        self._need_q6(w_dev, M, N)
+        _need(x, torch.float32, "x", self.device)
+        if x.numel() % N:
+            raise ValueError(f"x has {x.numel()} elements, not a multiple of N={N}")
+        batch = x.numel() // N
+        if out is None:
+            out = torch.empty((batch, M), dtype=torch.float32, device=self.device)
+        _need(out, torch.float32, "out", self.device)
+        if out.numel() < batch * M:
+            raise ValueError("out smaller than batch*M")
+        self._check(self._L.q4k_q6k_gemv(self._h, _ptr(w_dev), _ptr(x), _ptr(out), M, N, batch, _stream(stream)))
+        return out
+
+    def q6k_lmhead_select(self, w_dev: torch.Tensor, x: torch.Tensor, V: int, N: int, cap: float = 30.0,
+                          row_offset: int = 0, return_logits: bool = False, out: Selection | None = None,
+                          stream: torch.cuda.Stream | None = None) -> Selection:
+        """The fused LM head (lmHead matmul + logitSoftcap + argmax/topk256) of
+        a Q6_K head in the device layout."""
+        self._need_q6(w_dev, V, N)
+        _need(x, torch.float32, "x", self.device)
+        if x.numel() != N:
+            raise ValueError(f"x has {x.numel()} elements, expected N={N}")
+        if out is None:
+            out = Selection(
+                cand_val=torch.empty(256, dtype=torch.float32, device=self.device),
+                cand_idx=torch.empty(256, dtype=torch.int32, device=self.device),
+                argmax=torch.empty(1, dtype=torch.int32, device=self.device),
+                logits=torch.empty(V, dtype=torch.float32, device=self.device) if return_logits else None,
+            )
+        self._check(self._L.q4k_q6k_lmhead_select(
+            self._h, _ptr(w_dev), _ptr(x), V, N, cap, row_offset, _ptr(out.logits), _ptr(out.cand_val),
+            _ptr(out.cand_idx), _ptr(out.argmax), _stream(stream)))
         return out
 
     # ---- LM-head consumers ------------------------------------------------

@@ -192,6 +192,49 @@ Q4K_API int q4k_lmhead_select_sharded(q4k_ctx* ctx, q4k_exchange* ex, const void
                                       uint32_t N, float cap, uint32_t row_offset, float* cand_val,
                                       uint32_t* cand_idx, uint32_t* argmax, void* stream);
 
+/* ---- Q6_K matrices -----------------------------------------------------
+ * Q4_K_M files store some matmul weights as Q6_K (docs/findings/why-q4km.md:33;
+ * 210-byte super-blocks: ql[128], qh[64], int8 scales[16], f16 d).  The
+ * reference decodes them on the CPU at load (dequantizeQ6_K,
+ * src/gguf.ts:316-368, then f32ToF16Array + upload via tensorToF16,
+ * src/engine.ts:570-578) and multiplies them with the same matmul_quant
+ * pipelines.  Here they stay 6.56 bits per weight on the device: once at
+ * load, q4k_q6k_repack rewrites the GGUF bytes into the "Q6_K device
+ * layout" (every 208-byte body ql|qh|scales 16-byte aligned, row-major
+ * [M][N/256]; then the f16 d values as a plane [N/256][M rounded up to 8]),
+ * q4k_q6k_device_bytes(M, N) bytes, and the calls below read that layout.
+ * Weights seen by each output: f16_rne(f32(d*sc*(q-32))), the reference's. */
+
+/* Bytes of the device layout of an M x N Q6_K matrix (0 if N % 256 != 0). */
+Q4K_API uint64_t q4k_q6k_device_bytes(uint32_t M, uint32_t N);
+
+/* Load-time repack: GGUF Q6_K bytes (w_gguf: M rows of N/256 super-blocks,
+ * 2-byte aligned) -> device layout (w_dev, 16-byte aligned,
+ * q4k_q6k_device_bytes(M, N) bytes).  Replaces the reference's per-tensor
+ * dequantizeQ6_K + f32ToF16Array + writeBuffer (src/engine.ts:570-578). */
+Q4K_API int q4k_q6k_repack(q4k_ctx* ctx, const void* w_gguf, void* w_dev, uint32_t M, uint32_t N, void* stream);
+
+/* Weight probe: out[M*N] = the f16 bit patterns the GEMV multiplies, in
+ * row-major order -- the reference's uploaded f16 weight buffer, for the
+ * weight-probe comparison (src/diagnostics/weight-probe.ts:60-162). */
+Q4K_API int q4k_q6k_dequant_f16(q4k_ctx* ctx, const void* w_dev, uint32_t M, uint32_t N, uint16_t* out,
+                                void* stream);
+
+/* y[t*M + m] = sum_k w16[m,k] * x[t*N + k] for a Q6_K matrix in the device
+ * layout: the matmul_quant dispatch (shaders/matmul_quant.wgsl:21-54) of a
+ * Q6_K-sourced weight (src/engine.ts:1547-1605 call sites).  Same tolerance
+ * and conventions as q4k_gemv; batch > 16 runs in chunks of 16 rows. */
+Q4K_API int q4k_q6k_gemv(q4k_ctx* ctx, const void* w_dev, const float* x, float* y, uint32_t M, uint32_t N,
+                         uint32_t batch, void* stream);
+
+/* q4k_lmhead_select for a Q6_K LM head in the device layout (Q4_K_M files
+ * commonly store the tied token_embd / output matrix as Q6_K): lmHead matmul
+ * + logitSoftcap + argmax/topk256 candidates in one launch
+ * (src/engine.ts:1686-1741). */
+Q4K_API int q4k_q6k_lmhead_select(q4k_ctx* ctx, const void* w_dev, const float* x, uint32_t V, uint32_t N,
+                                  float cap, uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
+                                  uint32_t* argmax, void* stream);
+
 /* ---- plans ------------------------------------------------------------
  * A plan records a decode step's matmul-path operations once and replays
  * them with two launches per stage, the way the engine records a token's
