@@ -8,6 +8,8 @@
 // evaluates gelu_mul ops whose output feeds a GEMV of the same stage), then
 // one engine launch runs every GEMV and the LM-head selection of the stage
 // over one shared work list.  Stage s+1 starts after stage s has finished.
+// A stage that mixes weight formats (Q4_K and Q6_K matrices) runs as one
+// engine launch per format, back to back.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -24,6 +26,7 @@ struct PlanGemv {
   const float* x;
   float* y;
   uint32_t M, N;
+  uint32_t fmt;  // WeightFormat of w
 };
 
 struct PlanGelu {
@@ -43,6 +46,7 @@ struct PlanSelect {
   float* cand_val;
   uint32_t* cand_idx;
   uint32_t* argmax;
+  uint32_t fmt;
 };
 
 struct Stage {
@@ -57,7 +61,34 @@ struct Stage {
   uint32_t n_tasks = 0, n_jobs = 0, total_items = 0, total_cost = 0, grid = 0, select_task = 0;
   bool prep = false;  // activations prepared inside the engine launch (no preparation launch)
   uint32_t ksplit = 0;  // warps sharing each tile (long rows only; see TaskList::ksplit)
+  uint32_t fmt = kFmtQ4K;  // after commit: the weight format of every task of this launch unit
 };
+
+// Commit splits each recorded stage into launch units of one weight format
+// (Q4_K first); a gelu_mul goes with every unit that reads its output (the
+// Q4_K unit if none does).
+std::vector<Stage> split_by_format(const std::vector<Stage>& stages) {
+  std::vector<Stage> units;
+  for (const Stage& st : stages) {
+    Stage u[2];
+    u[1].fmt = kFmtQ6K;
+    for (const PlanGemv& g : st.gemvs) u[g.fmt == kFmtQ6K].gemvs.push_back(g);
+    for (const PlanSelect& q : st.selects) u[q.fmt == kFmtQ6K].selects.push_back(q);
+    for (const PlanGelu& gl : st.gelus) {
+      bool used[2] = {false, false};
+      for (int f = 0; f < 2; ++f) {
+        for (const PlanGemv& g : u[f].gemvs) used[f] |= (g.x == gl.act);
+        for (const PlanSelect& q : u[f].selects) used[f] |= (q.x == gl.act);
+      }
+      if (!used[0] && !used[1]) used[0] = true;
+      for (int f = 0; f < 2; ++f)
+        if (used[f]) u[f].gelus.push_back(gl);
+    }
+    for (int f = 0; f < 2; ++f)
+      if (!u[f].gemvs.empty() || !u[f].selects.empty() || !u[f].gelus.empty()) units.push_back(u[f]);
+  }
+  return units;
+}
 
 }  // namespace
 
@@ -111,7 +142,8 @@ void q4k_plan_destroy(q4k_plan* p) {
   delete p;
 }
 
-int q4k_plan_gemv(q4k_plan* p, uint32_t stage, const void* w, const float* x, float* y, uint32_t M, uint32_t N) {
+static int plan_gemv(q4k_plan* p, uint32_t stage, const void* w, const float* x, float* y, uint32_t M, uint32_t N,
+              uint32_t fmt) {
   int rc = check_plan(p);
   if (rc != Q4K_OK) return rc;
   q4k_ctx* ctx = p->ctx;
@@ -122,8 +154,17 @@ int q4k_plan_gemv(q4k_plan* p, uint32_t stage, const void* w, const float* x, fl
     return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
   Stage* st = stage_of(p, stage);
   if (!st) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "stage %u out of range", stage);
-  st->gemvs.push_back({static_cast<const uint8_t*>(w), x, y, M, N});
+  st->gemvs.push_back({static_cast<const uint8_t*>(w), x, y, M, N, fmt});
   return Q4K_OK;
+}
+
+int q4k_plan_gemv(q4k_plan* p, uint32_t stage, const void* w, const float* x, float* y, uint32_t M, uint32_t N) {
+  return plan_gemv(p, stage, w, x, y, M, N, kFmtQ4K);
+}
+
+int q4k_plan_gemv_q6k(q4k_plan* p, uint32_t stage, const void* w_dev, const float* x, float* y, uint32_t M,
+                      uint32_t N) {
+  return plan_gemv(p, stage, w_dev, x, y, M, N, kFmtQ6K);
 }
 
 int q4k_plan_gelu_mul(q4k_plan* p, uint32_t stage, const float* gate, const float* up, float* act, uint32_t n) {
@@ -141,8 +182,9 @@ int q4k_plan_gelu_mul(q4k_plan* p, uint32_t stage, const float* gate, const floa
   return Q4K_OK;
 }
 
-int q4k_plan_lmhead(q4k_plan* p, uint32_t stage, const void* w, const float* x, uint32_t V, uint32_t N, float cap,
-                    uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx, uint32_t* argmax) {
+static int plan_lmhead(q4k_plan* p, uint32_t stage, const void* w, const float* x, uint32_t V, uint32_t N, float cap,
+                uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx, uint32_t* argmax,
+                uint32_t fmt) {
   int rc = check_plan(p);
   if (rc != Q4K_OK) return rc;
   q4k_ctx* ctx = p->ctx;
@@ -157,8 +199,19 @@ int q4k_plan_lmhead(q4k_plan* p, uint32_t stage, const void* w, const float* x, 
   if (!st) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "stage %u out of range", stage);
   if (!st->selects.empty()) return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "one LM head per plan stage");
   st->selects.push_back({static_cast<const uint8_t*>(w), x, V, N, cap, row_offset, logits, cand_val, cand_idx,
-                         argmax});
+                         argmax, fmt});
   return Q4K_OK;
+}
+
+int q4k_plan_lmhead(q4k_plan* p, uint32_t stage, const void* w, const float* x, uint32_t V, uint32_t N, float cap,
+                    uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx, uint32_t* argmax) {
+  return plan_lmhead(p, stage, w, x, V, N, cap, row_offset, logits, cand_val, cand_idx, argmax, kFmtQ4K);
+}
+
+int q4k_plan_lmhead_q6k(q4k_plan* p, uint32_t stage, const void* w_dev, const float* x, uint32_t V, uint32_t N,
+                        float cap, uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
+                        uint32_t* argmax) {
+  return plan_lmhead(p, stage, w_dev, x, V, N, cap, row_offset, logits, cand_val, cand_idx, argmax, kFmtQ6K);
 }
 
 int q4k_plan_commit(q4k_plan* p) {
@@ -166,6 +219,7 @@ int q4k_plan_commit(q4k_plan* p) {
   if (rc != Q4K_OK) return rc;
   q4k_ctx* ctx = p->ctx;
   const uint32_t B = p->batch;
+  p->stages = split_by_format(p->stages);
   // Per stage: one preparation job per distinct (input, N); a gelu_mul's
   // output is a GEMV input of its stage.
   struct JobKey {
@@ -243,7 +297,7 @@ int q4k_plan_commit(q4k_plan* p) {
     // items: a stage of only such GEMVs shares each tile across 4 warps,
     // each taking a quarter of the row, so the items balance over the warps.
     {
-      bool long_rows = B <= 4 && st.selects.empty() && !tasks[s].empty();
+      bool long_rows = B <= 4 && st.selects.empty() && !tasks[s].empty() && st.fmt == kFmtQ4K;
       for (const EngineTask& t : tasks[s]) {
         const uint32_t nb = t.N / Q4K_QK;
         long_rows = long_rows && nb >= 16 && nb % 4 == 0;
@@ -254,7 +308,7 @@ int q4k_plan_commit(q4k_plan* p) {
     st.n_jobs = (uint32_t)keys[s].size();
     st.grid = items ? engine_grid(items, ctx->sm_count) : 0;
     for (const JobKey& k : keys[s]) xbytes += align_up(xfrag_bytes(k.N, B), 256) + 256;
-    desc_bytes += align_up(sizeof(EngineTask) * st.n_tasks, 256) + align_up(sizeof(CUtensorMap) * st.n_tasks, 256) +
+    desc_bytes += align_up(sizeof(EngineTask) * st.n_tasks, 256) + align_up(sizeof(CUtensorMap) * 2 * st.n_tasks, 256) +
                   align_up(sizeof(XJob) * st.n_jobs, 256) + align_up(sizeof(CtaSched) * st.grid, 256);
   }
   p->bytes = desc_bytes + xbytes;
@@ -294,18 +348,20 @@ int q4k_plan_commit(q4k_plan* p) {
       t.xfrag = J.xfrag;
       t.inv_scale = J.inv_scale;  // t.aux keeps the job index (the CTA schedules name jobs by it)
     }
-    // one weight tensor map per task, in the plan's memory
+    // the weight tensor maps of each task (Q6_K: body map, then d-plane map), in the plan's memory
+    const uint32_t mpt = st.fmt == kFmtQ6K ? 2u : 1u;
     st.maps_dev = reinterpret_cast<CUtensorMap*>(cur);
-    cur += align_up(sizeof(CUtensorMap) * st.n_tasks, 256);
-    std::vector<CUtensorMap> maps(st.n_tasks);
+    cur += align_up(sizeof(CUtensorMap) * 2 * st.n_tasks, 256);
+    std::vector<CUtensorMap> maps(mpt * st.n_tasks);
     for (uint32_t i = 0; i < st.n_tasks; ++i) {
       EngineTask& t = tasks[s][i];
-      e = encode_weight_map(&maps[i], t.w, t.M, t.N, &t.tile_bytes);
+      e = st.fmt == kFmtQ6K ? encode_q6k_maps(&maps[mpt * i], t.w, t.M, t.N, &t.tile_bytes)
+                            : encode_weight_map(&maps[i], t.w, t.M, t.N, &t.tile_bytes);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit weight tensor map");
-      t.tmap = st.maps_dev + i;
+      t.tmap = st.maps_dev + mpt * i;
     }
     if (st.n_tasks) {
-      e = cudaMemcpy(st.maps_dev, maps.data(), sizeof(CUtensorMap) * st.n_tasks, cudaMemcpyHostToDevice);
+      e = cudaMemcpy(st.maps_dev, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
     }
     st.tasks_dev = reinterpret_cast<EngineTask*>(cur);
@@ -317,7 +373,7 @@ int q4k_plan_commit(q4k_plan* p) {
     if (st.grid) {
       std::vector<CtaSched> sched(st.grid);
       engine_schedule(tasks[s].data(), st.n_tasks, st.total_cost, st.total_items, B, st.grid,
-                      engine_xcache_bytes(!st.selects.empty()), sched.data());
+                      engine_xcache_bytes(!st.selects.empty(), st.fmt), sched.data());
       // Prepare activations inside the engine when every CTA caches every
       // activation it uses and each stored gelu_mul output has a CTA that
       // prepares it (the first such CTA stores it).
@@ -376,6 +432,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
       tl.jobs = st.jobs_dev;
       tl.prep = st.prep ? 1u : 0u;
       tl.ksplit = st.ksplit;
+      tl.fmt = st.fmt;
       cudaError_t e = launch_engine(tl, kNoMap, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
     }

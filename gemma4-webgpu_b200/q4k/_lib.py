@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_plan_gemv": ([_P, _U32, _P, _P, _P, _U32, _U32], _I),
     "q4k_plan_gelu_mul": ([_P, _U32, _P, _P, _P, _U32], _I),
     "q4k_plan_lmhead": ([_P, _U32, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P], _I),
+    "q4k_plan_gemv_q6k": ([_P, _U32, _P, _P, _P, _U32, _U32], _I),
+    "q4k_plan_lmhead_q6k": ([_P, _U32, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P], _I),
     "q4k_plan_commit": ([_P], _I),
     "q4k_plan_run": ([_P, _P], _I),
     "q4k_plan_launches": ([_P], _I),

@@ -414,6 +414,17 @@ class Plan:
         self.ctx._check(self._L.q4k_plan_gemv(self._h, stage, _ptr(weight), _ptr(x), _ptr(y), M, N))
         self._bind(weight, x, y)
 
+    def gemv_q6k(self, stage: int, w_dev: torch.Tensor, x: torch.Tensor, y: torch.Tensor, M: int, N: int) -> None:
+        """A Q6_K GEMV (weights in the device layout, Context.q6k_repack)."""
+        dev = self.ctx.device
+        self.ctx._need_q6(w_dev, M, N)
+        _need(x, torch.float32, "x", dev)
+        _need(y, torch.float32, "y", dev)
+        if x.numel() < self.batch * N or y.numel() < self.batch * M:
+            raise ValueError("x / y smaller than batch x N / batch x M")
+        self.ctx._check(self._L.q4k_plan_gemv_q6k(self._h, stage, _ptr(w_dev), _ptr(x), _ptr(y), M, N))
+        self._bind(w_dev, x, y)
+
     def gelu_mul(self, stage: int, gate: torch.Tensor, up: torch.Tensor, act: torch.Tensor) -> None:
         dev = self.ctx.device
         for t, n in ((gate, "gate"), (up, "up"), (act, "act")):
@@ -431,6 +442,17 @@ class Plan:
             self._h, stage, _ptr(weight), _ptr(x), V, N, cap, row_offset, _ptr(out.logits), _ptr(out.cand_val),
             _ptr(out.cand_idx), _ptr(out.argmax)))
         self._bind(weight, x, out.logits, out.cand_val, out.cand_idx, out.argmax)
+
+    def lmhead_q6k(self, stage: int, w_dev: torch.Tensor, x: torch.Tensor, V: int, N: int, cap: float,
+                   out: Selection, row_offset: int = 0) -> None:
+        """The fused LM head of a Q6_K head in the device layout."""
+        dev = self.ctx.device
+        self.ctx._need_q6(w_dev, V, N)
+        _need(x, torch.float32, "x", dev)
+        self.ctx._check(self._L.q4k_plan_lmhead_q6k(
+            self._h, stage, _ptr(w_dev), _ptr(x), V, N, cap, row_offset, _ptr(out.logits), _ptr(out.cand_val),
+            _ptr(out.cand_idx), _ptr(out.argmax)))
+        self._bind(w_dev, x, out.logits, out.cand_val, out.cand_idx, out.argmax)
 
     def commit(self) -> "Plan":
         self.ctx._check(self._L.q4k_plan_commit(self._h))

@@ -267,6 +267,15 @@ Q4K_API int q4k_plan_lmhead(q4k_plan* plan, uint32_t stage, const void* w, const
                             float cap, uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
                             uint32_t* argmax);
 
+/* Q6_K variants of q4k_plan_gemv / q4k_plan_lmhead: the weight is a Q6_K
+ * matrix in the device layout (q4k_q6k_repack).  A stage that mixes Q4_K and
+ * Q6_K matrices runs as one engine launch per format. */
+Q4K_API int q4k_plan_gemv_q6k(q4k_plan* plan, uint32_t stage, const void* w_dev, const float* x, float* y,
+                              uint32_t M, uint32_t N);
+Q4K_API int q4k_plan_lmhead_q6k(q4k_plan* plan, uint32_t stage, const void* w_dev, const float* x, uint32_t V,
+                                uint32_t N, float cap, uint32_t row_offset, float* logits, float* cand_val,
+                                uint32_t* cand_idx, uint32_t* argmax);
+
 /* Finish recording: lay out and upload the launch descriptors. */
 Q4K_API int q4k_plan_commit(q4k_plan* plan);
 

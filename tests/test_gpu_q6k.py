@@ -165,5 +165,51 @@ def test_q6k_rejects_bad_arguments(ctx):
         ctx.q6k_gemv(w, x, 16, 100)
     with pytest.raises(Q4KError):
         ctx.q6k_gemv(w[1:], x, 16, 256)  # misaligned weights
+    g = torch.zeros(2 * 210 * 16 + 2, dtype=torch.uint8, device=DEV)
     with pytest.raises(Q4KError):
-        ctx.q6k_repack(w[1:2 * 210 * 16 + 1], 16, 256 * 2)  # odd GGUF pointer
+        ctx.q6k_repack(g[1:1 + 2 * 210 * 16], 16, 256 * 2)  # odd GGUF pointer
+
+
+def test_plan_mixed_formats_match_single_calls(ctx):
+    """A stage mixing Q4_K and Q6_K GEMVs (sharing an input) and a Q6_K LM
+    head, then a gelu_mul feeding a Q6_K down projection: the plan's outputs
+    equal the single calls' (same kernels, same per-output arithmetic)."""
+    from q4k import Plan
+
+    N, M, I, V = 1536, 2048, 6144, 16384
+    wq = to_dev(synth.q4k_matrix(M, N, 1))
+    wv = ctx.q6k_repack(to_dev(synth.q6k_matrix(512, N, 2)), 512, N)
+    wg = to_dev(synth.q4k_matrix(I, N, 3))
+    wd = ctx.q6k_repack(to_dev(synth.q6k_matrix(N, I, 4)), N, I)
+    wh = ctx.q6k_repack(to_dev(synth.q6k_matrix(V, N, 5)), V, N)
+    x = to_dev(synth.activations(1, N, 6)[0])
+    gate = to_dev(synth.activations(1, I, 7)[0])
+    up = to_dev(synth.activations(1, I, 8)[0])
+    yq = torch.empty(M, device=DEV)
+    yv = torch.empty(512, device=DEV)
+    yg = torch.empty(I, device=DEV)
+    act = torch.empty(I, device=DEV)
+    yd = torch.empty(N, device=DEV)
+    from q4k import Selection
+    sel = Selection(torch.empty(256, device=DEV), torch.empty(256, dtype=torch.int32, device=DEV),
+                    torch.empty(1, dtype=torch.int32, device=DEV), torch.empty(V, device=DEV))
+    p = Plan(ctx, 1)
+    p.gemv(0, wq, x, yq, M, N)
+    p.gemv_q6k(0, wv, x, yv, 512, N)
+    p.gemv(0, wg, x, yg, I, N)
+    p.lmhead_q6k(0, wh, x, V, N, 30.0, sel)
+    p.gelu_mul(1, gate, up, act)
+    p.gemv_q6k(1, wd, act, yd, N, I)
+    p.commit()
+    assert p.launches() == 3  # stage 0: a Q4_K and a Q6_K launch; stage 1: one Q6_K launch
+    p.run()
+    torch.cuda.synchronize()
+    assert torch.equal(yq, ctx.gemv(wq, x, M, N)[0])
+    assert torch.equal(yv, ctx.q6k_gemv(wv, x, 512, N)[0])
+    assert torch.equal(yg, ctx.gemv(wg, x, I, N)[0])
+    ref_act = ctx.gelu_mul(gate, up)
+    assert torch.equal(act, ref_act)
+    assert torch.equal(yd, ctx.q6k_gemv(wd, ref_act, N, I)[0])
+    ref = ctx.q6k_lmhead_select(wh, x, V, N, 30.0, return_logits=True)
+    assert torch.equal(sel.logits, ref.logits)
+    assert torch.equal(sel.cand_idx, ref.cand_idx) and torch.equal(sel.argmax, ref.argmax)
