@@ -262,6 +262,28 @@ def run_ours(args) -> None:
                   "launches": step4.launches_per_step()}
         del s4_graph, step4
 
+    # the real E2B shapes with a Q4_K_M-style Q4_K/Q6_K mix (q4k/e2b.py):
+    # the same two-stage plan, one engine launch per format per stage
+    real = None
+    if args.batch == 1 and not args.no_real:
+        from q4k.e2b import RealE2BStep
+
+        rstep = RealE2BStep(ctx)
+        r_ms, r_graph = time_body(rstep.run, reps)
+        rs_ms, rs_graph = time_body(rstep.run_serial, reps)
+        rl_ms, rl_graph = time_body(
+            lambda st: ctx.q6k_lmhead_select(rstep.lm_head, rstep.x["h"], 262144, 1536, 30.0, out=rstep.sel,
+                                             stream=st), reps)
+        rb = rstep.algorithmic_bytes()
+        wb = rstep.weight_bytes()
+        q6_lm = 262144 * 6 * 210 + 4 * 1536 + 2052
+        real = {"ms": round(r_ms, 4), "tokens_per_s": round(world / (r_ms / 1e3), 1),
+                "GB/s": round(rb / (r_ms / 1e3) / 1e9, 1), "launches": rstep.plan().launches(),
+                "weight_bytes": {"q4k": wb["q4k"], "q6k": wb["q6k"]}, "algorithmic_bytes": rb,
+                "serial_ms": round(rs_ms, 4),
+                "lmhead_q6k": {"ms": round(rl_ms, 4), "GB/s": round(q6_lm / (rl_ms / 1e3) / 1e9, 1)}}
+        del r_graph, rs_graph, rl_graph, rstep
+
     # config 2 at N > 1: the LM head split by vocabulary rows over the ranks,
     # one all-gather of 2 KB of candidates per rank, merged on every rank
     sharded = None
@@ -368,6 +390,9 @@ def run_ours(args) -> None:
                                     "frac_of_peak": round(lm_bytes / (lm_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
     if sweep4:
         kernels["sweep_batch4"] = sweep4
+    if real:
+        real["lmhead_q6k"]["frac_of_peak"] = round(real["lmhead_q6k"]["GB/s"] / pk["hbm_gbs"], 4)
+        kernels["e2b_real_q4km"] = real
     if sharded:
         sharded["frac_of_peak"] = round(sharded["GB/s"] / (world * pk["hbm_gbs"]), 4)
         kernels["lmhead_sharded"] = sharded
@@ -487,6 +512,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-real", action="store_true", help="skip the real-E2B-shape (Q4_K + Q6_K) sweep")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

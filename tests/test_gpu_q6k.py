@@ -213,3 +213,45 @@ def test_plan_mixed_formats_match_single_calls(ctx):
     ref = ctx.q6k_lmhead_select(wh, x, V, N, 30.0, return_logits=True)
     assert torch.equal(sel.logits, ref.logits)
     assert torch.equal(sel.cand_idx, ref.cand_idx) and torch.equal(sel.argmax, ref.argmax)
+
+
+def test_real_e2b_step_plan_matches_serial(ctx, oracle):
+    """The real-shape step (full-attention and sliding layers, producer and
+    consumer layers, Q4_K/Q6_K mix, PLE GEMVs, Q6_K LM head) through the plan
+    equals the one-call-per-dispatch order, and two of its GEMVs match the
+    oracle."""
+    from q4k.e2b import FMT_Q6K, RealE2BStep, layer_matrices, matrix_host, MAT_IDS, CONFIG
+
+    step = RealE2BStep(ctx, layers=(0, 4, 15, 34))
+    step.run()
+    torch.cuda.synchronize()
+    got = {k: v.clone() for k, v in step.out.items()}
+    sel = (step.sel.cand_idx.clone(), step.sel.argmax.clone())
+    ple = step.ple_out.clone()
+    # two stages x two formats, each engine launch preceded by a preparation
+    # launch when its CTAs cannot cache all of their activations
+    assert 4 <= step.plan().launches() <= 8
+    step.run_serial()
+    torch.cuda.synchronize()
+    for k in got:
+        if k[1] == "down":
+            # a stage of long-row downs splits each tile's K range over 4 warps
+            # (partial sums added in order): the same products, another order
+            d = (got[k] - step.out[k]).norm() / step.out[k].norm()
+            assert d <= 2e-5, (k, float(d))
+        else:
+            assert torch.equal(got[k], step.out[k]), k
+    assert torch.equal(sel[0], step.sel.cand_idx) and torch.equal(sel[1], step.sel.argmax)
+    assert torch.equal(ple, step.ple_out)
+    # layer 0's v and down are Q6_K, layer 4's q is 4096 x 1536 Q4_K, layer
+    # 15's down is 1536 x 12288 Q4_K (the plan's outputs, K-split downs included)
+    for (layer, name) in ((0, "v"), (4, "q"), (0, "down"), (15, "down")):
+        M, N, fmt, _ = layer_matrices(step.shape, layer)[name]
+        if name == "v" or (layer, name) == (0, "down"):
+            assert fmt == FMT_Q6K
+        w = matrix_host(M, N, fmt, synth.seed_for(CONFIG, 16 * layer + MAT_IDS.index(name)))
+        x = (step.act[layer] if name == "down" else step.x["h"]).cpu().numpy()[None]
+        ref = oracle.q6k_gemv(w, x, M, N) if fmt == FMT_Q6K else oracle.q4k_gemv(w, x, M, N)
+        _, wn = (oracle.q6k_gemv_f64 if fmt == FMT_Q6K else oracle.q4k_gemv_f64)(w, x, M, N)
+        ok, ratio, l2 = oracle.tolerance_ok(got[(layer, name)].cpu().numpy()[None], ref, wn, x)
+        assert ok and l2 <= L2_TOL, (layer, name, ratio, l2)
