@@ -48,9 +48,11 @@ __device__ __forceinline__ uint2 ldg_v2(const void* p) {
   return r;
 }
 
+// Not volatile: a pure function of its operands, so the compiler may
+// schedule it freely among the shared-memory loads and the dequantization.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint2 b) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -390,14 +392,20 @@ struct BlockRegs {
   uint4 ha, hb, qa0, qa1, qb0, qb1;
 };
 
+// Shared-memory loads as plain C++ loads (pointers into the kernel's
+// dynamic shared memory, so they compile to LDS): the compiler keeps them
+// after the stage's barrier wait and before the stage is handed back (both
+// asm statements clobber memory) and is otherwise free to schedule them.
+__device__ __forceinline__ uint4 sld128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
 __device__ __forceinline__ BlockRegs read_block(const uint8_t* ra_p, const uint8_t* rb_p, uint32_t c) {
   BlockRegs r;
-  r.ha = lds128(ra_p);
-  r.hb = lds128(rb_p);
-  r.qa0 = lds128(ra_p + 16 + 32 * c);
-  r.qa1 = lds128(ra_p + 32 + 32 * c);
-  r.qb0 = lds128(rb_p + 16 + 32 * c);
-  r.qb1 = lds128(rb_p + 32 + 32 * c);
+  r.ha = sld128(ra_p);
+  r.hb = sld128(rb_p);
+  r.qa0 = sld128(ra_p + 16 + 32 * c);
+  r.qa1 = sld128(ra_p + 32 + 32 * c);
+  r.qb0 = sld128(rb_p + 16 + 32 * c);
+  r.qb1 = sld128(rb_p + 32 + 32 * c);
   return r;
 }
 
@@ -407,11 +415,12 @@ __device__ __forceinline__ uint4 ldg_v4(const void* p) {
   return r;
 }
 
-// This lane's B fragments of k-steps w and w+8 (one 16-byte load).
+// This lane's B fragments of k-steps w and w+8 (one 16-byte load): from the
+// CTA's shared-memory activation cache (SX) or from global memory.
 template <bool SX>
-__device__ __forceinline__ uint4 load_frag(uint64_t addr) {
-  if constexpr (SX) return lds128_u32((uint32_t)addr);
-  return ldg_v4(reinterpret_cast<const void*>(addr));
+__device__ __forceinline__ uint4 load_frag(const uint8_t* p) {
+  if constexpr (SX) return *reinterpret_cast<const uint4*>(p);
+  return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
 // The math of one super-block: 2 rows x 64 weights per lane -> 16 (or 16*NT)
@@ -420,7 +429,7 @@ __device__ __forceinline__ uint4 load_frag(uint64_t addr) {
 // word offset an immediate.
 template <int NT, int COLS, bool SX>
 __device__ __forceinline__ void block_math(float (&acc)[NT][2][4], const BlockRegs& R, uint32_t c, uint32_t bsel,
-                                           const uint64_t (&base)[NT], const uint32_t (&wstep)[NT]) {
+                                           const uint8_t* const (&base)[NT], const uint32_t (&wstep)[NT]) {
   const RowConsts ka = row_consts(R.ha, c, bsel);
   const RowConsts kb = row_consts(R.hb, c, bsel);
 #pragma unroll
@@ -430,7 +439,7 @@ __device__ __forceinline__ void block_math(float (&acc)[NT][2][4], const BlockRe
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       const uint32_t ws = COLS > 0 ? (uint32_t)COLS * 64u : wstep[n];
-      const uint4 f = load_frag<SX>(base[n] + (uint64_t)(w * ws));
+      const uint4 f = load_frag<SX>(base[n] + w * ws);
       mma_16816(acc[n][0], A.lo02, B.lo02, A.lo13, B.lo13, make_uint2(f.x, f.y));
       mma_16816(acc[n][1], A.hi02, B.hi02, A.hi13, B.hi13, make_uint2(f.z, f.w));
     }
@@ -467,16 +476,16 @@ __device__ __forceinline__ uint32_t u4_word(const uint4& a, int w) {
 // the Q4_K order (word w = 4*is + j of the lane's half), same B fragments.
 template <int NT, int COLS, bool SX, bool EXACT>
 __device__ __forceinline__ void q6_block_math(float (&acc)[NT][2][4], const Q6Rows& R, uint32_t c,
-                                              const uint64_t (&base)[NT], const uint32_t (&wstep)[NT]) {
+                                              const uint8_t* const (&base)[NT], const uint32_t (&wstep)[NT]) {
   const uint32_t sh = (c & 1u) * 4u, h = c >> 1;
   const float d4a = 4.0f * __half2float(__ushort_as_half(R.da));
   const float d4b = 4.0f * __half2float(__ushort_as_half(R.db));
 #pragma unroll
   for (int is = 0; is < 2; ++is) {
-    const uint4 la0 = lds128(R.ra + 64 * h + 16 * is), la1 = lds128(R.ra + 64 * h + 32 + 16 * is);
-    const uint4 ha = lds128(R.ra + 128 + 32 * h + 16 * is);
-    const uint4 lb0 = lds128(R.rb + 64 * h + 16 * is), lb1 = lds128(R.rb + 64 * h + 32 + 16 * is);
-    const uint4 hb = lds128(R.rb + 128 + 32 * h + 16 * is);
+    const uint4 la0 = sld128(R.ra + 64 * h + 16 * is), la1 = sld128(R.ra + 64 * h + 32 + 16 * is);
+    const uint4 ha = sld128(R.ra + 128 + 32 * h + 16 * is);
+    const uint4 lb0 = sld128(R.rb + 64 * h + 16 * is), lb1 = sld128(R.rb + 64 * h + 32 + 16 * is);
+    const uint4 hb = sld128(R.rb + 128 + 32 * h + 16 * is);
     const Q6Consts ka = q6_consts(R.sa, is, d4a);
     const Q6Consts kb = q6_consts(R.sb, is, d4b);
 #pragma unroll
@@ -487,7 +496,7 @@ __device__ __forceinline__ void q6_block_math(float (&acc)[NT][2][4], const Q6Ro
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         const uint32_t ws = COLS > 0 ? (uint32_t)COLS * 64u : wstep[n];
-        const uint4 f = load_frag<SX>(base[n] + (uint64_t)(w * ws));
+        const uint4 f = load_frag<SX>(base[n] + w * ws);
         mma_16816(acc[n][0], A.lo02, B.lo02, A.lo13, B.lo13, make_uint2(f.x, f.y));
         mma_16816(acc[n][1], A.hi02, B.hi02, A.hi13, B.hi13, make_uint2(f.z, f.w));
       }
@@ -688,7 +697,6 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     lane_off[n] = ((g % cols) * 4u + c) * 16u;
     wstep[n] = cols * 64u;
   }
-  const uint32_t xs_base = smem_u32(xsm);
 
   uint32_t consumed = 0;
   uint32_t item = timed_out ? c1 : ring[0];
@@ -716,20 +724,23 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       // one super-block per stage: compute straight from the stage (the
       // other stages stay in flight meanwhile), then hand it back
       const Q6Rows R = q6_rows(stg, g, c);
-      uint64_t base[NT];
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const uint32_t off = n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n];
-        base[n] = sx ? (uint64_t)(xs_base + H.xs + off)
-                     : reinterpret_cast<uint64_t>(reinterpret_cast<const uint8_t*>(H.xfrag) + off);
-      }
+      // (each branch forms its own fragment pointers, so shared-memory ones
+      // stay recognisably shared and load with LDS)
       // a non-finite d anywhere in the warp's rows: the exact (slower) form
       const bool odd_d = ((R.da & 0x7C00u) == 0x7C00u) || ((R.db & 0x7C00u) == 0x7C00u);
-      if (__any_sync(0xffffffffu, odd_d)) {
-        if (sx) q6_block_math<NT, COLS, true, true>(acc, R, c, base, wstep);
-        else q6_block_math<NT, COLS, false, true>(acc, R, c, base, wstep);
+      const bool exact = __any_sync(0xffffffffu, odd_d);
+      if (sx) {
+        const uint8_t* base[NT];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) base[n] = xsm + H.xs + (n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n]);
+        if (exact) q6_block_math<NT, COLS, true, true>(acc, R, c, base, wstep);
+        else q6_block_math<NT, COLS, true, false>(acc, R, c, base, wstep);
       } else {
-        if (sx) q6_block_math<NT, COLS, true, false>(acc, R, c, base, wstep);
+        const uint8_t* base[NT];
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+          base[n] = reinterpret_cast<const uint8_t*>(H.xfrag) + (n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n]);
+        if (exact) q6_block_math<NT, COLS, false, true>(acc, R, c, base, wstep);
         else q6_block_math<NT, COLS, false, false>(acc, R, c, base, wstep);
       }
       fence_proxy_async_smem();
@@ -766,18 +777,21 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
           ++issued;
         }
       }
-      uint64_t base[NT];
+      // n-tiles before the last are full (8 columns): nb*4096 bytes each
+      // (each branch forms its own fragment pointers, so shared-memory ones
+      // stay recognisably shared and load with LDS)
+      if (sx) {
+        const uint8_t* base[NT];
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        // n-tiles before the last are full (8 columns): nb*4096 bytes each
-        const uint32_t off = n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n];
-        base[n] = sx ? (uint64_t)(xs_base + H.xs + off)
-                     : reinterpret_cast<uint64_t>(reinterpret_cast<const uint8_t*>(H.xfrag) + off);
-      }
-      if (sx)
+        for (int n = 0; n < NT; ++n) base[n] = xsm + H.xs + (n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n]);
         block_math<NT, COLS, true>(acc, R, c, bsel, base, wstep);
-      else
+      } else {
+        const uint8_t* base[NT];
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+          base[n] = reinterpret_cast<const uint8_t*>(H.xfrag) + (n * H.nb * 4096u + b * 8u * wstep[n] + lane_off[n]);
         block_math<NT, COLS, false>(acc, R, c, bsel, base, wstep);
+      }
     }
     }
     ++k;

@@ -4,13 +4,15 @@
     python gemma4-webgpu_b200/q4k/profile_case.py lmhead [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py sweep [--layers L] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py gemm [--batch T] [--reps R]
+    python gemma4-webgpu_b200/q4k/profile_case.py q6head [--reps R]
 
 `gemv` rotates over 35 distinct 6144x1536 Q4_K matrices (186 MB, more than
 the 126 MB L2, so each launch reads its weights from HBM); `lmhead` runs the
 fused 262144-row LM head (226 MB); `sweep` runs the decode-step plan of
 q4k.decode with L layers (default 8: 159 MB of layer weights plus a
 16384-row LM head); `gemm` runs q4k_gemm on one 6144x1536 matrix with T
-activation rows (default 512).  A few hundred MB of device memory at most;
+activation rows (default 512); `q6head` runs the fused LM head on a
+131072 x 1536 Q6_K matrix in the device layout (165 MB).  A few hundred MB of device memory at most;
 the process exits after `reps` runs.
 """
 from __future__ import annotations
@@ -28,7 +30,7 @@ from q4k import Context, synth  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep", "gemm"])
+    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep", "gemm", "q6head"])
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=40)
@@ -56,6 +58,13 @@ def main() -> None:
         step = DecodeStep(ctx, E2BShape(layers=a.layers, vocab=16384), batch=a.batch)
         for _ in range(a.reps):
             step.run()
+    elif a.kernel == "q6head":
+        V, N = 131072, 1536
+        w = ctx.q6k_repack(torch.from_numpy(synth.q6k_matrix(V, N, synth.seed_for(5, 999)).reshape(-1)).to(dev),
+                           V, N)
+        x = torch.from_numpy(synth.activations(1, N, 1)).to(dev)
+        for _ in range(a.reps):
+            ctx.q6k_lmhead_select(w, x[0], V, N, 30.0)
     else:
         V, N = 262144, 1536
         w = torch.from_numpy(synth.q4k_matrix(V, N, synth.seed_for(3, 999))).to(dev)
