@@ -59,23 +59,39 @@ __host__ __device__ constexpr uint32_t scale_sel(uint32_t c) {
   return (c & 1u) ? ((4u << 12) | (3u << 8) | (4u << 4) | 2u) : ((4u << 12) | (1u << 8) | (4u << 4) | 0u);
 }
 
-// sel = scale_sel(c).
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// sel = scale_sel(c).  Every step is exact: the 6-bit values enter as f16
+// magic numbers (1024 + v, or -(1024 + v) with the sign byte 0xE4), which one
+// f16 add turns into v; the products by -1024, 1/16 and -64 are powers of
+// two applied to values of at most 6 significant bits.
 __device__ __forceinline__ RowConsts row_consts(const uint4& h, uint32_t c, uint32_t sel) {
   RowConsts r;
   const ScaleMin4 sm = unpack_scale_min(h.y, h.z, h.w);
   const uint32_t scw = c < 2 ? sm.sc_lo : sm.sc_hi;
   const uint32_t mw = c < 2 ? sm.m_lo : sm.m_hi;
-  const uint32_t kMagic = 0x64006400u;  // f16x2 (1024, 1024)
-  const uint32_t sc = hsub2(prmt(scw, 0u, sel) | kMagic, kMagic);  // (sc_j0, sc_j1) f16x2, exact
-  const uint32_t mm = hsub2(prmt(mw, 0u, sel) | kMagic, kMagic);   // (m_j0, m_j1)
-  r.sc0 = prmt(sc, sc, 0x1010u);
-  r.nsc0 = hmul2(r.sc0, 0xE400E400u);                     // * (-1024)
-  const uint32_t s1 = prmt(sc, sc, 0x3232u);
-  r.sc1 = hmul2(s1, 0x2C002C00u);                         // * (1/16)
-  r.nsc1 = hmul2(s1, 0xD400D400u);                        // * (-64)
-  const uint16_t ndmin = (uint16_t)((h.x >> 16) ^ 0x8000u);  // -dmin
-  r.ndm0 = fma_h_h_f(ndmin, (uint16_t)(mm & 0xffffu), 0.0f);
-  r.ndm1 = fma_h_h_f(ndmin, (uint16_t)(mm >> 16), 0.0f);
+  // sel picks bytes (s, s+1) into halves 0 and 1 (s = 2(c&1)); sel ^ 0x100
+  // broadcasts byte s, sel | 1 broadcasts byte s+1
+  const uint32_t s0 = prmt(scw, 0x64646464u, sel ^ 0x100u);  // (1024 + sc_j0) x2
+  const uint32_t s1 = prmt(scw, 0x64646464u, sel | 1u);      // (1024 + sc_j1) x2
+  r.sc0 = hadd2(s0, 0xE400E400u);                            // sc_j0 x2
+  r.nsc0 = hmul2(r.sc0, 0xE400E400u);                        // -1024 sc_j0
+  r.sc1 = hfma2(s1, 0x2C002C00u, 0xD400D400u);               // (1024 + sc)/16 - 64 = sc_j1/16
+  r.nsc1 = hmul2(r.sc1, 0xE400E400u);                        // -64 sc_j1
+  const uint32_t nm = hadd2(prmt(mw, 0xE4E4E4E4u, sel), 0x64006400u);  // (-m_j0, -m_j1)
+  const uint16_t dmin = (uint16_t)(h.x >> 16);
+  r.ndm0 = fma_h_h_f(dmin, (uint16_t)(nm & 0xffffu), 0.0f);  // -dmin*m, exact
+  r.ndm1 = fma_h_h_f(dmin, (uint16_t)(nm >> 16), 0.0f);
   r.d = (uint16_t)(h.x & 0xffffu);
   return r;
 }

@@ -540,7 +540,10 @@ __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts,
   return h;
 }
 
-template <int NT, int COLS, int KS, int FMT>
+// XS = 1: a launch that prepares its activations in the engine (tl.prep), so
+// every task's activation sits in the CTA's shared-memory cache and the math
+// loop has only the shared-memory path.
+template <int NT, int COLS, int KS, int FMT, int XS>
 __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     engine_kernel(const TaskList tl, const __grid_constant__ CUtensorMap wmap,
                   const __grid_constant__ CUtensorMap dmap, uint32_t batch, int has_select, SelectScratch sel,
@@ -719,7 +722,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       break;
     }
     const uint8_t* stg = wsm + slot * kSB;
-    const bool sx = H.xs != 0xffffffffu;
+    const bool sx = XS ? true : (H.xs != 0xffffffffu);
     if constexpr (FMT == kFmtQ6K) {
       // one super-block per stage: compute straight from the stage (the
       // other stages stay in flight meanwhile), then hand it back
@@ -759,7 +762,9 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     } else {
     const uint32_t nblk = min(Pipe<FMT>::kBlocks, b_hi - b);
     const uint32_t rs = H.tile_bytes;
-#pragma unroll 1
+    // both super-blocks of a stage in one unrolled body, so the second
+    // block's shared-memory loads can be scheduled under the first one's math
+#pragma unroll
     for (uint32_t sb = 0; sb < nblk; ++sb, ++b) {
       const BlockRegs R = read_block(stg + g * rs + sb * kBlockBytes, stg + (g + 8) * rs + sb * kBlockBytes, c);
       if (sb + 1 == nblk) {
@@ -1026,8 +1031,8 @@ size_t xcache_bytes(int hs) {
          (hs ? kSelectSmem : kPartSmem);
 }
 
-template <int NT, int COLS, int KS = 1, int FMT = kFmtQ4K>
-cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, const CUtensorMap& dmap, uint32_t batch,
+template <int NT, int COLS, int KS, int FMT, int XS>
+cudaError_t launch_xs(const TaskList& tasks, const CUtensorMap& map, const CUtensorMap& dmap, uint32_t batch,
                            int hs, const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
   const size_t xcap = xcache_bytes<FMT>(hs);
   const size_t smem = kAlignSlack + weight_smem<FMT>() + kTaskSmem + xcap + (hs ? kSelectSmem : kPartSmem);
@@ -1035,7 +1040,7 @@ cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, const 
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS, FMT>,
+    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS, FMT, XS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(kSmemLimit - kStaticSmemHeadroom));
     if (e != cudaSuccess) return e;
@@ -1051,8 +1056,15 @@ cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, const 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, engine_kernel<NT, COLS, KS, FMT>, tasks, map, dmap, batch, hs, sel,
+  return cudaLaunchKernelEx(&cfg, engine_kernel<NT, COLS, KS, FMT, XS>, tasks, map, dmap, batch, hs, sel,
                             (uint32_t)xcap);
+}
+
+template <int NT, int COLS, int KS = 1, int FMT = kFmtQ4K>
+cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, const CUtensorMap& dmap, uint32_t batch,
+                           int hs, const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
+  return tasks.prep ? launch_xs<NT, COLS, KS, FMT, 1>(tasks, map, dmap, batch, hs, sel, grid, s)
+                    : launch_xs<NT, COLS, KS, FMT, 0>(tasks, map, dmap, batch, hs, sel, grid, s);
 }
 
 }  // namespace
