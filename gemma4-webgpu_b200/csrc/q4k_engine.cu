@@ -42,12 +42,6 @@ constexpr float kFloorE = -1e30f;
 
 // ---- small PTX helpers -------------------------------------------------------
 
-__device__ __forceinline__ uint2 ldg_v2(const void* p) {
-  uint2 r;
-  asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-  return r;
-}
-
 // Not volatile: a pure function of its operands, so the compiler may
 // schedule it freely among the shared-memory loads and the dequantization.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -329,6 +323,7 @@ __device__ __forceinline__ EngineTask task_get(const TaskList& tl, const TaskSrc
 // Where a warp's copy engine stands: work item, super-block and its task.
 struct Cursor {
   uint32_t item, b, b_hi, ti;
+  uint32_t claims, issued;  // items claimed, stages issued
   const CUtensorMap* map;
   const CUtensorMap* dmap;  // Q6_K: the d-plane map
   uint32_t tile_bytes, nb, item_begin, item_end;
@@ -406,12 +401,6 @@ __device__ __forceinline__ BlockRegs read_block(const uint8_t* ra_p, const uint8
   r.qa1 = sld128(ra_p + 32 + 32 * c);
   r.qb0 = sld128(rb_p + 16 + 32 * c);
   r.qb1 = sld128(rb_p + 32 + 32 * c);
-  return r;
-}
-
-__device__ __forceinline__ uint4 ldg_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
 
@@ -558,6 +547,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   __shared__ CtaSched s_sched;
   __shared__ uint32_t s_next;                    // next unclaimed item of this CTA's range
   __shared__ uint32_t s_ring[kEngineWarps][4];   // items claimed by each warp, in order
+  __shared__ Cursor s_cur[kEngineWarps];          // each warp's copy cursor (lane 0's)
   __shared__ float s_inv[kMaxCachedX][kMaxTokens];  // prep: 1/scale of each cached activation and token
   __shared__ float s_red[kEngineWarps];
   __shared__ uint64_t s_gbar[kEngineWarps];          // K-split launches: one per tile group
@@ -643,33 +633,37 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   // counter, so warps that finish early take more) and recorded in the
   // warp's ring, which the math follows in the same order.
   // (K-split launches: a group's tiles are fixed, c0 + grp + ngrp*i.)
-  uint32_t claims = 0;
-  auto claim = [&]() -> uint32_t {
-    uint32_t it = 0;
-    if (lane == 0) {
-      it = ks_n > 1 ? c0 + grp + ngrp * claims : atomicAdd(&s_next, 1u);
-      ring[claims & 3u] = it;
-    }
-    ++claims;
-    return __shfl_sync(0xffffffffu, it, 0);
+  // The copy cursor lives in shared memory and only lane 0 touches it (at
+  // the start and when a stage is handed back), so it holds no registers
+  // across the math.
+  auto claim = [&](Cursor& F) -> uint32_t {  // lane 0
+    const uint32_t it = ks_n > 1 ? c0 + grp + ngrp * F.claims : atomicAdd(&s_next, 1u);
+    ring[F.claims & 3u] = it;
+    ++F.claims;
+    return it;
   };
-
-  Cursor F;
-  F.ti = t_first;
-  F.item = timed_out ? c1 : claim();
-  cursor_task(F, tl, ts);
-  cursor_seek(F, tl, ts, c1);
-  cursor_range(F, gq, ks_n);
-  uint32_t issued = 0;
-  for (int st = 0; st < kSt && F.item < c1; ++st) {
-    issue_stage<FMT>(F, wsm + st * kSB, &bars[st], lane);
+  // Lane 0: issue the cursor's stage into `slot` and advance the cursor.
+  auto issue_next = [&](Cursor& F, uint32_t slot) {
+    issue_stage<FMT>(F, wsm + slot * kSB, &bars[slot], 0u);
     F.b += cursor_blocks<FMT>(F);
     if (F.b == F.b_hi) {
-      F.item = claim();
+      F.item = claim(F);
       cursor_seek(F, tl, ts, c1);
       cursor_range(F, gq, ks_n);
     }
-    ++issued;
+    ++F.issued;
+  };
+  if (lane == 0) {
+    Cursor F;
+    F.claims = 0;
+    F.issued = 0;
+    F.ti = t_first;
+    F.item = timed_out ? c1 : claim(F);
+    cursor_task(F, tl, ts);
+    cursor_seek(F, tl, ts, c1);
+    cursor_range(F, gq, ks_n);
+    for (int st = 0; st < kSt && F.item < c1; ++st) issue_next(F, st);
+    s_cur[warp] = F;
   }
   __syncwarp();
 
@@ -748,15 +742,10 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (F.item < c1) {
-        issue_stage<FMT>(F, wsm + slot * kSB, &bars[slot], lane);
-        F.b += cursor_blocks<FMT>(F);
-        if (F.b == F.b_hi) {
-          F.item = claim();
-          cursor_seek(F, tl, ts, c1);
-          cursor_range(F, gq, ks_n);
-        }
-        ++issued;
+      if (lane == 0 && s_cur[warp].item < c1) {
+        Cursor F = s_cur[warp];
+        issue_next(F, slot);
+        s_cur[warp] = F;
       }
       ++b;
     } else {
@@ -771,15 +760,10 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
         // the whole stage is in registers: hand it back to the copy engine
         fence_proxy_async_smem();
         __syncwarp();
-        if (F.item < c1) {
-          issue_stage<FMT>(F, wsm + slot * kSB, &bars[slot], lane);
-          F.b += cursor_blocks<FMT>(F);
-          if (F.b == F.b_hi) {
-            F.item = claim();
-            cursor_seek(F, tl, ts, c1);
-            cursor_range(F, gq, ks_n);
-          }
-          ++issued;
+        if (lane == 0 && s_cur[warp].item < c1) {
+          Cursor F = s_cur[warp];
+          issue_next(F, slot);
+          s_cur[warp] = F;
         }
       }
       // n-tiles before the last are full (8 columns): nb*4096 bytes each
@@ -851,22 +835,24 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
         }
       }
     } else {
-      if (c == 0) {
-        const EngineTask T = task_get(tl, ts, ti);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (!(h ? vb : va)) continue;
-          const uint32_t row = h ? rb : ra;
-          float v = (h ? ((acc[0][0][2] + acc[0][1][2]) + (acc[0][0][3] + acc[0][1][3]))
-                       : ((acc[0][0][0] + acc[0][1][0]) + (acc[0][0][1] + acc[0][1][1]))) * H.inv[0];
-          if (T.cap > 0.0f) v = softcap(v, T.cap);
-          if (T.logits) T.logits[row] = v;
-          const uint32_t gi = T.row_offset + row;
-          const uint32_t res = gi & 255u;
-          if (better(v, gi, s_bv[res], s_bi[res])) {
-            s_bv[res] = v;
-            s_bi[res] = gi;
-          }
+      // The token's results sit in the c == 0 lanes (row ra in [0..1], rb in
+      // [2..3]); lane c == 1 takes rb from its neighbour, so 16 lanes each
+      // finish one row (softcap, logits, per-residue best) in parallel.
+      const float v_a = ((acc[0][0][0] + acc[0][1][0]) + (acc[0][0][1] + acc[0][1][1])) * H.inv[0];
+      const float v_b = __shfl_sync(0xffffffffu,
+                                    ((acc[0][0][2] + acc[0][1][2]) + (acc[0][0][3] + acc[0][1][3])) * H.inv[0],
+                                    lane & ~3u);
+      if (c < 2 && (c ? vb : va)) {
+        const EngineTask& T = ts.table ? ts.table[ti - ts.t0] : tl.inl;
+        const uint32_t row = c ? rb : ra;
+        float v = c ? v_b : v_a;
+        if (T.cap > 0.0f) v = softcap(v, T.cap);
+        if (T.logits) T.logits[row] = v;
+        const uint32_t gi = T.row_offset + row;
+        const uint32_t res = gi & 255u;  // the 16 rows of a tile have distinct residues
+        if (better(v, gi, s_bv[res], s_bi[res])) {
+          s_bv[res] = v;
+          s_bi[res] = gi;
         }
       }
       __syncwarp();
@@ -887,7 +873,8 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   if (timed_out) {
     // record the failure, then let every copy still in flight land (bounded)
     if (lane == 0) atomicOr(sel.status, 1u);
-    for (uint32_t j = k; j < issued; ++j) mbar_wait(&bars[j % kSt], (j / kSt) & 1u);
+    if (lane == 0)
+      for (uint32_t j = k; j < s_cur[warp].issued; ++j) mbar_wait(&bars[j % kSt], (j / kSt) & 1u);
   }
 
   if (!has_select) return;
