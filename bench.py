@@ -262,6 +262,24 @@ def run_ours(args) -> None:
                   "launches": step4.launches_per_step()}
         del s4_graph, step4
 
+    # config 4: the layer weights at T activation rows per step (no LM head):
+    # the GEMV engine for T <= 16, the tcgen05 GEMM for T >= 64
+    batched = None
+    if args.batch == 1 and not args.no_c4:
+        from q4k.decode import BatchedSweep
+
+        batched = {}
+        bf16_peak = peaks()["bf16_tflops"]
+        for T in (4, 16, 64, 512):
+            bs = BatchedSweep(step, T)
+            t_ms, t_graph = time_body(bs.run, max(5, min(reps, 2000 // T)))
+            tf = bs.flops() / (t_ms / 1e3) / 1e12
+            batched[f"T={T}"] = {"ms": round(t_ms, 4), "tokens_per_s": round(world * T / (t_ms / 1e3), 1),
+                                 "TFLOP/s": round(tf, 2), "frac_of_bf16_peak": round(tf / bf16_peak, 4),
+                                 "path": "GEMV engine plan" if T <= 16 else "tcgen05 GEMM per matrix"}
+            del t_graph
+            bs.close()
+
     # the real E2B shapes with a Q4_K_M-style Q4_K/Q6_K mix (q4k/e2b.py):
     # the same two-stage plan, one engine launch per format per stage
     real = None
@@ -271,6 +289,7 @@ def run_ours(args) -> None:
         rstep = RealE2BStep(ctx)
         r_ms, r_graph = time_body(rstep.run, reps)
         rs_ms, rs_graph = time_body(rstep.run_serial, reps)
+        pl_ms, pl_graph = time_body(rstep.ple_stage1, reps)
         rl_ms, rl_graph = time_body(
             lambda st: ctx.q6k_lmhead_select(rstep.lm_head, rstep.x["h"], 262144, 1536, 30.0, out=rstep.sel,
                                              stream=st), reps)
@@ -281,8 +300,11 @@ def run_ours(args) -> None:
                 "GB/s": round(rb / (r_ms / 1e3) / 1e9, 1), "launches": rstep.plan().launches(),
                 "weight_bytes": {"q4k": wb["q4k"], "q6k": wb["q6k"]}, "algorithmic_bytes": rb,
                 "serial_ms": round(rs_ms, 4),
-                "lmhead_q6k": {"ms": round(rl_ms, 4), "GB/s": round(q6_lm / (rl_ms / 1e3) / 1e9, 1)}}
-        del r_graph, rs_graph, rl_graph, rstep
+                "lmhead_q6k": {"ms": round(rl_ms, 4), "GB/s": round(q6_lm / (rl_ms / 1e3) / 1e9, 1)},
+                "ple_stage1": {"us": round(pl_ms * 1e3, 2), "launches": 1,
+                               "what": "35 Q5_K super-blocks of the argmax token gathered from the 1.6 GB "
+                                       "table, decoded and fused with the normalised projection"}}
+        del r_graph, rs_graph, rl_graph, pl_graph, rstep
 
     # config 2 at N > 1: the LM head split by vocabulary rows over the ranks,
     # one all-gather of 2 KB of candidates per rank, merged on every rank
@@ -390,6 +412,8 @@ def run_ours(args) -> None:
                                     "frac_of_peak": round(lm_bytes / (lm_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
     if sweep4:
         kernels["sweep_batch4"] = sweep4
+    if batched is not None:
+        kernels["c4_batched"] = batched
     if real:
         real["lmhead_q6k"]["frac_of_peak"] = round(real["lmhead_q6k"]["GB/s"] / pk["hbm_gbs"], 4)
         kernels["e2b_real_q4km"] = real
@@ -513,6 +537,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-real", action="store_true", help="skip the real-E2B-shape (Q4_K + Q6_K) sweep")
+    ap.add_argument("--no-c4", action="store_true", help="skip the config-4 batched sweeps")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

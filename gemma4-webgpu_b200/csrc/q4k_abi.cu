@@ -143,8 +143,10 @@ int q4k_check(q4k_ctx* ctx) {
   if (status != 0) {
     const uint32_t zero = 0;
     cudaMemcpy(ctx->select.status, &zero, sizeof(zero), cudaMemcpyHostToDevice);
-    return ctx_fail(ctx, Q4K_ERR_TIMEOUT,
-                    "a kernel gave up waiting for its weight copies (bounded wait expired); its outputs are invalid");
+    if (status & 1u)
+      return ctx_fail(ctx, Q4K_ERR_TIMEOUT,
+                      "a kernel gave up waiting for its weight copies (bounded wait expired); its outputs are invalid");
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "a token id was >= vocab in q4k_ple_stage1; that token's outputs are NaN");
   }
   ctx->err[0] = 0;
   return Q4K_OK;

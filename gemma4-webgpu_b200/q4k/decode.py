@@ -257,3 +257,84 @@ class StepGraph:
     def replay(self) -> None:
         with torch.cuda.stream(self.stream):
             self.graph.replay()
+
+
+class BatchedSweep:
+    """Config 4: the 35 layers' seven matrices at T activation rows per step
+    (prefill, or T independent sequences sharing the weights), without the
+    LM head.  T <= 16 runs as a two-stage Plan on the GEMV engine (one weight
+    stream per matrix for all T rows); T >= 64 runs each matrix through the
+    tcgen05 GEMM (q4k_gemm via Context.gemv), with gelu_mul between up and
+    down as in src/engine.ts:1589-1605.  The layers are independent, so the
+    GEMM path spreads them over `streams` CUDA streams (one library context
+    each: a GEMM call prepares its activation operand in its context's
+    scratch), letting the launches of small matrices share the SMs."""
+
+    def __init__(self, step: DecodeStep, T: int, streams: int = 8):
+        self.step, self.T = step, T
+        ctx, s = step.ctx, step.shape
+        dev = ctx.device
+        shapes = layer_shapes(s)
+        self.x_h = torch.from_numpy(synth.activations(T, s.hidden, synth.seed_for(4, 100))).to(dev)
+        self.x_attn = torch.from_numpy(synth.activations(T, s.q, synth.seed_for(4, 101))).to(dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.out = {(layer, name): torch.empty((T, shapes[name][0]), **f32)
+                    for layer in range(s.layers) for name in LAYER_MATS}
+        self.act = [torch.empty((T, s.ffn), **f32) for _ in range(s.layers)]
+        self.plan = None
+        if T <= 16:
+            p = Plan(ctx, batch=T)
+            for layer in range(s.layers):
+                for name in ("q", "k", "v", "o", "gate", "up"):
+                    M, N = shapes[name]
+                    x = self.x_attn if name == "o" else self.x_h
+                    p.gemv(0, step.weights[(layer, name)], x, self.out[(layer, name)], M, N)
+                p.gelu_mul(1, self.out[(layer, "gate")], self.out[(layer, "up")], self.act[layer])
+                M, N = shapes["down"]
+                p.gemv(1, step.weights[(layer, "down")], self.act[layer], self.out[(layer, "down")], M, N)
+            p.commit()
+            self.plan = p
+        else:
+            self.ctxs = [Context(dev) for _ in range(streams)]
+            self.streams = [torch.cuda.Stream(device=dev) for _ in range(streams)]
+
+    def _layer(self, c: Context, layer: int, stream) -> None:
+        s, W, O = self.step.shape, self.step.weights, self.out
+        shapes = layer_shapes(s)
+        for name in ("q", "k", "v", "o", "gate", "up"):
+            M, N = shapes[name]
+            x = self.x_attn if name == "o" else self.x_h
+            c.gemv(W[(layer, name)], x, M, N, out=O[(layer, name)], stream=stream)
+        c.gelu_mul(O[(layer, "gate")], O[(layer, "up")], out=self.act[layer], stream=stream)
+        M, N = shapes["down"]
+        c.gemv(W[(layer, "down")], self.act[layer], M, N, out=O[(layer, "down")], stream=stream)
+
+    def run(self, stream: torch.cuda.Stream | None = None) -> None:
+        if self.plan is not None:
+            self.plan.run(stream)
+            return
+        main = stream or torch.cuda.current_stream(self.step.ctx.device)
+        fork = torch.cuda.Event()
+        fork.record(main)
+        joins = []
+        for k, (c, st) in enumerate(zip(self.ctxs, self.streams)):
+            st.wait_event(fork)
+            for layer in range(k, self.step.shape.layers, len(self.streams)):
+                self._layer(c, layer, st)
+            e = torch.cuda.Event()
+            e.record(st)
+            joins.append(e)
+        for e in joins:
+            main.wait_event(e)
+
+    def close(self) -> None:
+        for c in getattr(self, "ctxs", []):
+            c.close()
+        self.ctxs = []
+
+    def weights(self) -> int:
+        """Weights one step multiplies (each by all T rows)."""
+        return self.step.shape.layers * sum(M * N for M, N in layer_shapes(self.step.shape).values())
+
+    def flops(self) -> int:
+        return 2 * self.T * self.weights()

@@ -13,7 +13,10 @@ src/engine.ts:1520-1614 and the LM head of :1686-1741) differs:
   * every layer runs the two per-layer-embedding GEMVs, inp_gate 256 x 1536
     and post_proj 1536 x 256 (src/engine.ts:1612-1614), and the step starts
     with the global per-layer projection 8960 x 1536 (:1520-1525);
-  * the LM head is the tied 262144 x 1536 token embedding.
+  * the LM head is the tied 262144 x 1536 token embedding;
+  * per token, the per-layer embeddings of the current token (a Q5_K table
+    [262144, 35*256]) are gathered and fused with the normalised projection
+    (ple_stage1_fuse, src/engine.ts:1528-1535).
 
 A Q4_K_M file stores most matrices as Q4_K and some as Q6_K
 (docs/findings/why-q4km.md:33).  The mix used here follows the usual
@@ -101,6 +104,7 @@ class RealE2BStep:
     shape: RealE2B = field(default_factory=RealE2B)
     layers: tuple[int, ...] | None = None
     with_lm_head: bool = True
+    with_ple_table: bool = True
 
     def __post_init__(self):
         s, dev = self.shape, self.ctx.device
@@ -124,10 +128,34 @@ class RealE2BStep:
         self.out = {k: torch.empty(M, **f32) for k, (M, _, _, _) in self.mats.items()}
         self.act = {i: torch.empty(self.mats[(i, "gate")][0], **f32) for i in self.layer_ids}
         self.ple_out = torch.empty(ple_out, **f32)
+        self.ple_table = self._ple_table() if self.with_ple_table else None
+        gen = torch.Generator(device="cpu").manual_seed(synth.seed_for(CONFIG, 903))
+        self.ple_norm = torch.empty(s.ple_dim, dtype=torch.float16).uniform_(0.5, 1.5, generator=gen).view(
+            torch.int16).to(dev)
+        self.ple_inputs = torch.empty(ple_out, **f32)
         self.sel = Selection(cand_val=torch.empty(256, **f32),
                              cand_idx=torch.empty(256, dtype=torch.int32, device=dev),
                              argmax=torch.empty(1, dtype=torch.int32, device=dev), logits=None)
         self._plan: Plan | None = None
+
+    def _ple_table(self) -> torch.Tensor:
+        """The Q5_K per-layer embedding table [vocab, layers*176 bytes], made
+        on the device (1.6 GB): uniform bytes for the scales, qh and qs, and
+        d, dmin ~ |U(0, 4e-3)| as f16 in every super-block."""
+        s, dev = self.shape, self.ctx.device
+        nb = s.vocab * s.layers
+        gen = torch.Generator(device=dev).manual_seed(synth.seed_for(CONFIG, 902))
+        t = torch.randint(0, 256, (nb, synth.Q5K_BLOCK_BYTES), dtype=torch.uint8, device=dev, generator=gen)
+        dd = torch.empty((nb, 2), dtype=torch.float16, device=dev).uniform_(0.0, 4e-3, generator=gen)
+        t[:, 0:4] = dd.view(torch.uint8)
+        return t.reshape(s.vocab, s.layers * synth.Q5K_BLOCK_BYTES)
+
+    def ple_stage1(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Per-layer embedding stage 1 of the current token: the token id is
+        the LM head's last argmax, read on the device."""
+        s = self.shape
+        self.ctx.ple_stage1(self.ple_table, self.sel.argmax, s.vocab, s.layers, self.ple_out, self.ple_norm,
+                            1e-6, out=self.ple_inputs, stream=stream)
 
     def _upload(self, M: int, N: int, fmt: str, seed: int) -> torch.Tensor:
         w = torch.from_numpy(matrix_host(M, N, fmt, seed)).to(self.ctx.device)
@@ -163,6 +191,9 @@ class RealE2BStep:
             total += 3 * 4 * self.mats[(i, "gate")][0]
         if self.with_lm_head:
             total += 4 * s.hidden + 256 * 8 + 4
+        if self.ple_table is not None:
+            # one token's 35 Q5_K super-blocks, the projection in, the PLE inputs out, the norm weight
+            total += s.layers * synth.Q5K_BLOCK_BYTES + 2 * 4 * s.layers * s.ple_dim + 2 * s.ple_dim
         return total
 
     def plan(self) -> Plan:
@@ -188,7 +219,12 @@ class RealE2BStep:
         return p
 
     def run(self, stream: torch.cuda.Stream | None = None) -> None:
+        """The step's plan, then the per-layer embedding stage 1 of the token
+        the LM head just chose (the reference runs it at the start of the next
+        forward, right after the projection GEMV; the work is the same)."""
         self.plan().run(stream)
+        if self.ple_table is not None and self.with_lm_head:
+            self.ple_stage1(stream)
 
     def run_serial(self, stream: torch.cuda.Stream | None = None) -> None:
         """One libq4k call per reference dispatch, in encodeTransformerPass order."""
@@ -207,6 +243,8 @@ class RealE2BStep:
         if self.with_lm_head:
             c.q6k_lmhead_select(self.lm_head, self.x["h"], s.vocab, s.hidden, s.softcap, out=self.sel,
                                 stream=stream)
+            if self.ple_table is not None:
+                self.ple_stage1(stream)
 
     def result_tensors(self) -> list[torch.Tensor]:
         return [self.sel.argmax, self.sel.cand_val, self.sel.cand_idx]

@@ -22,6 +22,8 @@ from ._lib import Q4KError
 
 QK_K = 256
 BLOCK_BYTES = 144
+Q5K_BLOCK_BYTES = 176  # Q5_K super-block (per-layer embedding table)
+PLE_DIM = 256  # per_layer_input_dim: one Q5_K super-block per layer and token
 Q6K_BLOCK_BYTES = 210
 
 
@@ -160,6 +162,45 @@ class Context:
         nb = weight.numel() // BLOCK_BYTES
         out = torch.empty(nb * QK_K, dtype=torch.int16, device=self.device)
         self._check(self._L.q4k_dequant_f16(self._h, _ptr(weight), _ptr(out), nb, _stream(stream)))
+        return out
+
+    # ---- per-layer embeddings (Q5_K table; see include/q4k.h) ---------------
+
+    def q5k_dequant_f16(self, table: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """The f16 values (int16 bit patterns) the reference uploads for a Q5_K
+        table (decodeQ5_KBlock + f32ToF16Array), 256 per 176-byte super-block."""
+        _need(table, torch.uint8, "table", self.device)
+        if table.numel() % Q5K_BLOCK_BYTES:
+            raise ValueError("table size is not a whole number of 176-byte super-blocks")
+        nb = table.numel() // Q5K_BLOCK_BYTES
+        out = torch.empty(nb * QK_K, dtype=torch.int16, device=self.device)
+        self._check(self._L.q4k_q5k_dequant_f16(self._h, _ptr(table), _ptr(out), nb, _stream(stream)))
+        return out
+
+    def ple_stage1(self, table: torch.Tensor, token_ids: torch.Tensor, vocab: int, layers: int,
+                   projected: torch.Tensor, norm_w: torch.Tensor, eps: float = 1e-6,
+                   out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """shaders/ple_stage1_fuse.wgsl for every layer of T tokens (one
+        launch): per-layer embedding rows gathered from the Q5_K table
+        [vocab, layers*176 bytes], fused with the RMS-normalised projection.
+        token_ids: int32 [T] on the device; projected: f32 [T, layers*256];
+        norm_w: f16 bit patterns (int16) [256].  Returns f32 [T, layers*256]."""
+        _need(table, torch.uint8, "table", self.device)
+        _need(token_ids, torch.int32, "token_ids", self.device)
+        _need(projected, torch.float32, "projected", self.device)
+        _need(norm_w, torch.int16, "norm_w", self.device)
+        T = token_ids.numel()
+        if table.numel() < vocab * layers * Q5K_BLOCK_BYTES:
+            raise ValueError("table smaller than vocab*layers*176 bytes")
+        if projected.numel() != T * layers * PLE_DIM or norm_w.numel() != PLE_DIM:
+            raise ValueError("projected must be [T, layers*256] and norm_w [256]")
+        if out is None:
+            out = torch.empty((T, layers * PLE_DIM), dtype=torch.float32, device=self.device)
+        _need(out, torch.float32, "out", self.device)
+        if out.numel() != T * layers * PLE_DIM:
+            raise ValueError("out must be [T, layers*256]")
+        self._check(self._L.q4k_ple_stage1(self._h, _ptr(table), _ptr(token_ids), T, vocab, layers, _ptr(projected),
+                                           _ptr(norm_w), eps, _ptr(out), _stream(stream)))
         return out
 
     # ---- Q6_K matrices (device layout; see include/q4k.h) ---------------------

@@ -125,3 +125,34 @@ def q6k_matrix(rows: int, cols: int, seed: int) -> np.ndarray:
 def q6k_bytes(rows: int, cols: int) -> int:
     """Size rule of tensorByteSize for type 14 (src/gguf.ts:392)."""
     return rows * cols // QK_K * Q6K_BLOCK_BYTES
+
+
+Q5K_BLOCK_BYTES = 176
+
+
+def make_q5k_blocks(n_blocks: int, rng: np.random.Generator, d_sigma: float = 2e-3) -> np.ndarray:
+    """n_blocks seeded Q5_K super-blocks as uint8 [n_blocks, 176] (GGUF
+    layout: f16 d, f16 dmin, 12 packed scale/min bytes, qh[32], qs[128]);
+    d, dmin, scales and mins drawn as for Q4_K, qh and qs uniform bytes."""
+    d = np.abs(rng.normal(0.0, d_sigma, n_blocks)).astype(np.float16)
+    dmin = np.abs(rng.normal(0.0, d_sigma, n_blocks)).astype(np.float16)
+    raw = np.frombuffer(rng.bytes(n_blocks * Q5K_BLOCK_BYTES), dtype=np.uint8).reshape(n_blocks, -1)
+    out = np.empty((n_blocks, Q5K_BLOCK_BYTES), dtype=np.uint8)
+    out[:, 0:2] = d.view(np.uint8).reshape(n_blocks, 2)
+    out[:, 2:4] = dmin.view(np.uint8).reshape(n_blocks, 2)
+    out[:, 4:16] = pack_scale_min(raw[:, 0:8] & 0x3F, raw[:, 8:16] & 0x3F)
+    out[:, 16:176] = raw[:, 16:176]
+    return out
+
+
+def q5k_table(vocab: int, layers: int, seed: int) -> np.ndarray:
+    """A per-layer embedding table [vocab, layers*256] in Q5_K as GGUF stores
+    it: row v is `layers` consecutive super-blocks, block L = layer L's 256
+    values (src/engine.ts:681-702)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return make_q5k_blocks(vocab * layers, rng).reshape(vocab, layers * Q5K_BLOCK_BYTES)
+
+
+def q5k_bytes(rows: int, cols: int) -> int:
+    """Size rule of tensorByteSize for type 13 (src/gguf.ts:391)."""
+    return rows * cols // QK_K * Q5K_BLOCK_BYTES

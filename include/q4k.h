@@ -72,8 +72,10 @@ Q4K_API const char* q4k_last_error(const q4k_ctx* ctx);
 /* Synchronize the device and report whether any kernel launched through
  * `ctx` gave up one of its bounded waits since the last check (every wait
  * on an asynchronous copy has an iteration limit; on expiry the kernel
- * records it, drains its copies and returns instead of hanging).  Returns
- * Q4K_OK or Q4K_ERR_TIMEOUT, and clears the record.  The reference's
+ * records it, drains its copies and returns instead of hanging), or met an
+ * invalid device-side input (a token id past the vocabulary in
+ * q4k_ple_stage1).  Returns Q4K_OK, Q4K_ERR_TIMEOUT or Q4K_ERR_INVALID_ARG,
+ * and clears the record.  The reference's
  * counterpart is the device-lost flag checked before public calls
  * (src/engine.ts:385-388, 1677). */
 Q4K_API int q4k_check(q4k_ctx* ctx);
@@ -234,6 +236,38 @@ Q4K_API int q4k_q6k_gemv(q4k_ctx* ctx, const void* w_dev, const float* x, float*
 Q4K_API int q4k_q6k_lmhead_select(q4k_ctx* ctx, const void* w_dev, const float* x, uint32_t V, uint32_t N,
                                   float cap, uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
                                   uint32_t* argmax, void* stream);
+
+/* ---- per-layer embeddings (Q5_K) ---------------------------------------
+ * Gemma-4-E2B's per-layer embedding table per_layer_token_embd is Q5_K
+ * (176-byte super-blocks: f16 d, f16 dmin, 12 packed 6-bit scale/min bytes,
+ * qh[32], qs[128]); row v holds `layers` consecutive super-blocks, block L
+ * being layer L's 256 values.  The reference decodes the whole 1.6 GB table
+ * at load into one f16 buffer per layer (streamDecodePleQ5_K,
+ * src/engine.ts:642-721; decodeQ5_KBlock, src/gguf.ts:218-256) and per
+ * token runs ple_stage1_fuse once per layer (src/engine.ts:1528-1535).
+ * Here the table stays Q5_K on the device and is read only for the tokens
+ * being decoded. */
+
+/* Weight probe: out[n_blocks*256] = the f16 bit patterns of the decoded
+ * values, the reference's uploaded per-layer embedding entries
+ * (decodeQ5_KBlock + f32ToF16Array, src/engine.ts:683-702).  w 16-byte
+ * aligned. */
+Q4K_API int q4k_q5k_dequant_f16(q4k_ctx* ctx, const void* w, uint16_t* out, uint64_t n_blocks, void* stream);
+
+/* shaders/ple_stage1_fuse.wgsl (bind group {projected, norm_weight,
+ * embed_slice, ple_inputs, {layer_idx, token_id, per_layer_dim, eps}}) for
+ * every layer of T tokens in one launch, per_layer_dim = 256:
+ *   out[t][L*256+i] = ((projected[t][L*256+i] / rms_tL) * f32(norm_w[i])
+ *                      + embed_L[token_t][i] * 16) * inverseSqrt(2),
+ *   rms_tL = sqrt(sum_i projected[t][L*256+i]^2 / 256 + eps),
+ * embed_L[v][i] decoded from the Q5_K table (16-byte aligned, vocab rows of
+ * layers*176 bytes) exactly as the reference uploads it.  token_ids [T] are
+ * device memory (e.g. the previous step's argmax output, as
+ * src/engine.ts:1719-1727 feeds it); an id >= vocab makes that token's
+ * outputs NaN and q4k_check return Q4K_ERR_INVALID_ARG. */
+Q4K_API int q4k_ple_stage1(q4k_ctx* ctx, const void* table_q5k, const uint32_t* token_ids, uint32_t T,
+                           uint32_t vocab, uint32_t layers, const float* projected, const uint16_t* norm_w,
+                           float eps, float* out, void* stream);
 
 /* ---- plans ------------------------------------------------------------
  * A plan records a decode step's matmul-path operations once and replays

@@ -57,6 +57,9 @@ def lib() -> ctypes.CDLL:
     L.orc_q6k_dequant_f16.argtypes = [P, I64, P]
     L.orc_q6k_gemv.argtypes = [P, P, P, I64, I64, I64, I]
     L.orc_q6k_gemv_f64.argtypes = [P, P, P, P, I64, I64, I64, I]
+    L.orc_q5k_dequant_f32.argtypes = [P, I64, P]
+    L.orc_q5k_dequant_f16.argtypes = [P, I64, P]
+    L.orc_ple_stage1.argtypes = [P, P, I64, I64, P, P, ctypes.c_float, P]
     L.orc_logit_softcap.argtypes = [P, I64, ctypes.c_float]
     L.orc_argmax.argtypes = [P, I64]
     L.orc_argmax.restype = ctypes.c_uint32
@@ -173,6 +176,37 @@ def q6k_gemv_f64(w: np.ndarray, x: np.ndarray, M: int, N: int, threads: int = 0)
     wn = np.empty(M, dtype=np.float64)
     lib().orc_q6k_gemv_f64(_p(wb), _p(xx), _p(y), _p(wn), M, N, xx.shape[0], threads)
     return y, wn
+
+
+def q5k_dequant_f32(blocks: np.ndarray) -> np.ndarray:
+    """Q5_K super-blocks (GGUF layout, 176 bytes each) -> f32 (src/gguf.ts:212-256)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)
+    nb = b.size // 176
+    out = np.empty(nb * 256, dtype=np.float32)
+    lib().orc_q5k_dequant_f32(_p(b), nb, _p(out))
+    return out
+
+
+def q5k_dequant_f16(blocks: np.ndarray) -> np.ndarray:
+    """f16 bit patterns (uint16) of the decoded Q5_K values (RNE), the
+    per-layer embedding the reference uploads."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)
+    nb = b.size // 176
+    out = np.empty(nb * 256, dtype=np.uint16)
+    lib().orc_q5k_dequant_f16(_p(b), nb, _p(out))
+    return out
+
+
+def ple_stage1(table: np.ndarray, tokens: np.ndarray, layers: int, projected: np.ndarray,
+               norm_w16: np.ndarray, eps: float) -> np.ndarray:
+    """shaders/ple_stage1_fuse.wgsl for every layer of T tokens: out [T, layers*256]."""
+    tb = np.ascontiguousarray(table, dtype=np.uint8).reshape(-1)
+    tk = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
+    pr = np.ascontiguousarray(projected, dtype=np.float32).reshape(tk.size, layers * 256)
+    nw = np.ascontiguousarray(norm_w16, dtype=np.uint16).reshape(256)
+    out = np.empty_like(pr)
+    lib().orc_ple_stage1(_p(tb), _p(tk), tk.size, layers, _p(pr), _p(nw), eps, _p(out))
+    return out
 
 
 def logit_softcap(logits: np.ndarray, cap: float) -> np.ndarray:

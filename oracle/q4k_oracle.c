@@ -25,6 +25,9 @@
  *   f32 -> f16          src/gguf.ts:425-473   (f32ToF16Array: Float16Array RNE at
  *                                              :432-436, truncating fallback :443-471)
  *   Q6_K decode         src/gguf.ts:316-368   (dequantizeQ6_K)
+ *   Q5_K decode         src/gguf.ts:212-256   (decodeQ5_KBlock; :262-314 dequantizeQ5_K)
+ *   PLE stage 1         shaders/ple_stage1_fuse.wgsl:16-38, embedding slice upload
+ *                       src/engine.ts:681-702 (row v, layer L = block v*layers + L)
  *   GEMV                shaders/matmul_quant.wgsl:21-54
  *   4-row GEMV          shaders/matmul_quant_mr4.wgsl:33-88 (same per-row order)
  *   softcap             shaders/logit_softcap.wgsl:9-16
@@ -44,7 +47,7 @@
 
 #define ORC_API __attribute__((visibility("default")))
 
-enum { QK_K = 256, Q4K_BLOCK_BYTES = 144, Q6K_BLOCK_BYTES = 210 };
+enum { QK_K = 256, Q4K_BLOCK_BYTES = 144, Q6K_BLOCK_BYTES = 210, Q5K_BLOCK_BYTES = 176 };
 
 /* ---- f16 <-> f32 ------------------------------------------------------- */
 
@@ -201,6 +204,87 @@ ORC_API void orc_q6k_dequant_f16(const uint8_t* blocks, int64_t n_blocks, uint16
   for (int64_t b = 0; b < n_blocks; ++b) {
     dequant_q6k_block_f32(blocks + b * Q6K_BLOCK_BYTES, tmp);
     for (int i = 0; i < QK_K; ++i) out[b * QK_K + i] = orc_f32_to_f16_rne(tmp[i]);
+  }
+}
+
+/* ---- Q5_K super-block decode ------------------------------------------- */
+
+/* One Q5_K super-block (176 bytes: f16 d, f16 dmin, 12 packed scale/min
+ * bytes, qh[32], qs[128]) -> 256 f32, as src/gguf.ts:218-256 evaluates it:
+ * group g (0..3) of 64 elements takes the low nibbles of qs[32g..32g+31]
+ * plus bit 2g of qh[l] as the 5th bit (value 16), then the high nibbles plus
+ * bit 2g+1; d1*(q) - min1 in f64, one rounding to f32 at the store. */
+static void dequant_q5k_block_f32(const uint8_t* blk, float* out) {
+  const double d = f16_to_f64((uint16_t)(blk[0] | (blk[1] << 8)));
+  const double dmin = f16_to_f64((uint16_t)(blk[2] | (blk[3] << 8)));
+  const uint8_t* scales = blk + 4;
+  const uint8_t* qh = blk + 16;
+  const uint8_t* qs = blk + 48;
+  for (int g = 0; g < 4; ++g) {
+    int sc1, m1, sc2, m2;
+    get_scale_min(scales, 2 * g, &sc1, &m1);
+    get_scale_min(scales, 2 * g + 1, &sc2, &m2);
+    const double d1 = d * sc1, min1 = dmin * m1;
+    const double d2 = d * sc2, min2 = dmin * m2;
+    const int u1 = 1 << (2 * g), u2 = 2 << (2 * g);
+    for (int l = 0; l < 32; ++l) {
+      const int q = (qs[32 * g + l] & 0x0f) + ((qh[l] & u1) ? 16 : 0);
+      out[64 * g + l] = (float)(d1 * q - min1);
+    }
+    for (int l = 0; l < 32; ++l) {
+      const int q = ((qs[32 * g + l] >> 4) & 0x0f) + ((qh[l] & u2) ? 16 : 0);
+      out[64 * g + 32 + l] = (float)(d2 * q - min2);
+    }
+  }
+}
+
+ORC_API void orc_q5k_dequant_f32(const uint8_t* blocks, int64_t n_blocks, float* out) {
+  for (int64_t b = 0; b < n_blocks; ++b) dequant_q5k_block_f32(blocks + b * Q5K_BLOCK_BYTES, out + b * QK_K);
+}
+
+/* Q5_K -> f16 bit patterns: the per-layer embedding values the reference
+ * uploads (decodeQ5_KBlock then f32ToF16Array, RNE; src/engine.ts:683-702). */
+ORC_API void orc_q5k_dequant_f16(const uint8_t* blocks, int64_t n_blocks, uint16_t* out) {
+  float tmp[QK_K];
+  for (int64_t b = 0; b < n_blocks; ++b) {
+    dequant_q5k_block_f32(blocks + b * Q5K_BLOCK_BYTES, tmp);
+    for (int i = 0; i < QK_K; ++i) out[b * QK_K + i] = orc_f32_to_f16_rne(tmp[i]);
+  }
+}
+
+/* shaders/ple_stage1_fuse.wgsl:16-38 for T tokens and `layers` layers, with
+ * D = 256 (one Q5_K super-block per layer per token):
+ *   rms = sqrt(sum_i projected[L*D+i]^2 / D + eps)   (256-lane tree sum)
+ *   out[L*D+i] = ((projected[L*D+i] / rms) * f32(norm_w[i])
+ *                 + f32(embed_L[token*D+i]) * sqrt(D)) * inverseSqrt(2)
+ * where embed_L[token*D+i] is element i of super-block token*layers + L of
+ * the Q5_K table, decoded and rounded to f16 as the upload does.  The
+ * per-lane squares, the tree order and the f32 operation order follow the
+ * shader; inverseSqrt(2) is taken as 1/sqrt(2) rounded to f32. */
+ORC_API void orc_ple_stage1(const uint8_t* table, const uint32_t* tokens, int64_t T, int64_t layers,
+                            const float* projected, const uint16_t* norm_w, float eps, float* out) {
+  enum { D = 256 };
+  float emb[QK_K];
+  float sq[D];
+  const float sqrt_d = sqrtf((float)D);
+  const float inv_sqrt2 = (float)(1.0 / sqrt(2.0));
+  for (int64_t t = 0; t < T; ++t) {
+    for (int64_t L = 0; L < layers; ++L) {
+      const float* pr = projected + (t * layers + L) * D;
+      float* o = out + (t * layers + L) * D;
+      dequant_q5k_block_f32(table + ((int64_t)tokens[t] * layers + L) * Q5K_BLOCK_BYTES, emb);
+      for (int i = 0; i < D; ++i) sq[i] = pr[i] * pr[i];
+      for (int stride = 128; stride > 0; stride >>= 1)
+        for (int i = 0; i < stride; ++i) sq[i] = sq[i] + sq[i + stride];
+      const float rms = sqrtf(sq[0] / (float)D + eps);
+      for (int i = 0; i < D; ++i) {
+        const float nw = orc_f16_to_f32(norm_w[i]);
+        const float e16 = orc_f16_to_f32(orc_f32_to_f16_rne(emb[i]));
+        const float proj_normed = (pr[i] / rms) * nw;
+        const float embed_val = e16 * sqrt_d;
+        o[i] = (proj_normed + embed_val) * inv_sqrt2;
+      }
+    }
   }
 }
 

@@ -20,6 +20,12 @@ implementations of the algorithms it cites:
   decoded by gguf-py's Q6_K.dequantize_blocks (llama.cpp's
   dequantize_row_q6_K, the layout src/gguf.ts:316-368 decodes) and the RNE
   f16 bit patterns of those values.
+* q5k_blocks.npz -- Q5_K super-blocks (seeded random plus hand-built edge
+  cases: every 5-bit quant with each qh bit, max scales/mins, subnormal and
+  NaN d, negative dmin) decoded by gguf-py's Q5_K.dequantize_blocks
+  (llama.cpp's dequantize_row_q5_K, the layout src/gguf.ts:212-314 decodes)
+  and the RNE f16 bit patterns of those values (what the per-layer embedding
+  upload stores, src/engine.ts:697-702).
 * select.npz -- small logit vectors with planted ties, NaN and -1e30 entries,
   with argmax / per-residue max computed by a numpy restatement of
   shaders/argmax.wgsl and shaders/topk256.wgsl.
@@ -146,6 +152,46 @@ def make_q6k_fixture() -> None:
     np.savez_compressed(OUT / "q6k_blocks.npz", blocks=blocks, f32=f32, f16=f16)
 
 
+def q5k_edge_blocks() -> np.ndarray:
+    """Hand-built Q5_K super-blocks: d | dmin | scales | qh | qs."""
+    def blk(d, dmin, sc, mn, qh, qs):
+        b = np.zeros(176, dtype=np.uint8)
+        b[0:2] = np.array([d], dtype=np.float16).view(np.uint8)
+        b[2:4] = np.array([dmin], dtype=np.float16).view(np.uint8)
+        b[4:16] = synth.pack_scale_min(np.array([sc]), np.array([mn]))[0]
+        b[16:48] = qh
+        b[48:176] = qs
+        return b
+
+    ramp_qs = (np.arange(128) * 37 % 256).astype(np.uint8)
+    ramp_qh = (np.arange(32) * 11 % 256).astype(np.uint8)
+    out = [np.zeros(176, dtype=np.uint8)]
+    out.append(blk(1.0, 0.0, [1] * 8, [0] * 8, np.zeros(32, np.uint8), ramp_qs))            # q without the 5th bit
+    out.append(blk(1.0, 0.0, [1] * 8, [0] * 8, np.full(32, 0xFF, np.uint8), ramp_qs))      # q + 16
+    out.append(blk(1.0, 1.0, [63] * 8, [63] * 8, np.full(32, 0xFF, np.uint8), np.full(128, 0xFF, np.uint8)))
+    out.append(blk(0.5, 0.25, list(range(0, 64, 8)), list(range(63, -1, -8)), ramp_qh, ramp_qs))
+    out.append(blk(6.0e-8, 6.0e-8, [63, 1] * 4, [1, 63] * 4, ramp_qh, ramp_qs))               # subnormal d, dmin
+    out.append(blk(2.0e-3, -3.0e-3, [17, 42, 5, 63, 0, 31, 48, 9], [3, 60, 22, 0, 63, 7, 14, 40], ramp_qh, ramp_qs))
+    out.append(blk(40.0, 0.0, [63] * 8, [0] * 8, np.full(32, 0xFF, np.uint8), np.full(128, 0xFF, np.uint8)))  # > f16 max
+    b = blk(1.0, 1.0, [1] * 8, [1] * 8, ramp_qh, ramp_qs)                                    # NaN d
+    b[0:2] = np.array([0x7E00], dtype=np.uint16).view(np.uint8)
+    out.append(b)
+    return np.stack(out)
+
+
+def make_q5k_fixture() -> None:
+    from gguf import quants
+    from gguf.constants import GGMLQuantizationType
+
+    rand = synth.make_q5k_blocks(64, np.random.Generator(np.random.PCG64(synth.seed_for(0, 997))))
+    wide = synth.make_q5k_blocks(32, np.random.Generator(np.random.PCG64(13)), d_sigma=0.5)
+    blocks = np.concatenate([q5k_edge_blocks(), rand, wide]).astype(np.uint8)
+    with np.errstate(all="ignore"):
+        f32 = quants.dequantize(blocks.reshape(-1), GGMLQuantizationType.Q5_K).astype(np.float32).reshape(-1)
+        f16 = f32.astype(np.float16).view(np.uint16)
+    np.savez_compressed(OUT / "q5k_blocks.npz", blocks=blocks, f32=f32, f16=f16)
+
+
 def make_gemv_fixture() -> None:
     M, N = 2048, 1536
     w = synth.q4k_matrix(M, N, synth.seed_for(0, 0))
@@ -216,6 +262,7 @@ def make_select_fixture() -> None:
 if __name__ == "__main__":
     make_blocks_fixture()
     make_q6k_fixture()
+    make_q5k_fixture()
     make_gemv_fixture()
     make_select_fixture()
     for f in sorted(OUT.glob("*.npz")):

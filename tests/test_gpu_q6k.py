@@ -228,6 +228,7 @@ def test_real_e2b_step_plan_matches_serial(ctx, oracle):
     got = {k: v.clone() for k, v in step.out.items()}
     sel = (step.sel.cand_idx.clone(), step.sel.argmax.clone())
     ple = step.ple_out.clone()
+    ple_in = step.ple_inputs.clone()
     # two stages x two formats, each engine launch preceded by a preparation
     # launch when its CTAs cannot cache all of their activations
     assert 4 <= step.plan().launches() <= 8
@@ -243,6 +244,14 @@ def test_real_e2b_step_plan_matches_serial(ctx, oracle):
             assert torch.equal(got[k], step.out[k]), k
     assert torch.equal(sel[0], step.sel.cand_idx) and torch.equal(sel[1], step.sel.argmax)
     assert torch.equal(ple, step.ple_out)
+    assert torch.equal(ple_in, step.ple_inputs)
+    # the per-layer embedding stage 1 of the chosen token, read from the Q5_K
+    # table on the device, against the oracle on that token's table row
+    tok = int(step.sel.argmax.cpu()[0])
+    row = step.ple_table[tok].cpu().numpy()[None]
+    ref = oracle.ple_stage1(row, np.zeros(1, dtype=np.uint32), step.shape.layers, ple.cpu().numpy()[None],
+                            step.ple_norm.cpu().numpy().view(np.uint16), 1e-6)
+    assert np.max(np.abs(ple_in.cpu().numpy() - ref[0]) / (np.abs(ref[0]) + 1e-30)) <= 2.5e-7
     # layer 0's v and down are Q6_K, layer 4's q is 4096 x 1536 Q4_K, layer
     # 15's down is 1536 x 12288 Q4_K (the plan's outputs, K-split downs included)
     for (layer, name) in ((0, "v"), (4, "q"), (0, "down"), (15, "down")):

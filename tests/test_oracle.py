@@ -212,3 +212,59 @@ def test_q6k_gemv_matches_f64(oracle):
     assert np.allclose(y64, x.astype(np.float64) @ w16.T, rtol=1e-12, atol=1e-12)
     assert np.allclose(wn, np.linalg.norm(w16, axis=1))
     assert np.all(np.abs(y - y64) <= 1e-5 * wn[None, :] * np.linalg.norm(x, axis=1)[:, None])
+
+
+# ---- Q5_K and the per-layer embedding stage 1 --------------------------------
+# (src/gguf.ts:212-314, src/engine.ts:642-721, shaders/ple_stage1_fuse.wgsl)
+
+def test_q5k_dequant_f32_matches_gguf_py(oracle, golden_dir):
+    g = np.load(golden_dir / "q5k_blocks.npz")
+    out = oracle.q5k_dequant_f32(g["blocks"])
+    ref = g["f32"]
+    assert np.array_equal(np.isnan(out), np.isnan(ref))
+    m = ~np.isnan(ref)
+    assert np.array_equal(out[m].view(np.uint32), ref[m].view(np.uint32))
+
+
+def test_q5k_dequant_f16_matches_golden(oracle, golden_dir):
+    g = np.load(golden_dir / "q5k_blocks.npz")
+    assert _f16_equal(oracle.q5k_dequant_f16(g["blocks"]), g["f16"])
+
+
+def test_q5k_known_answer_positions(oracle):
+    """d = 1, dmin = 0, every scale 1: element 64g + 32h + l is the low (h=0)
+    or high (h=1) nibble of qs[32g + l] plus 16 when bit 2g+h of qh[l] is set."""
+    rng = np.random.default_rng(4)
+    b = np.zeros(176, dtype=np.uint8)
+    b[0:2] = np.array([1.0], dtype=np.float16).view(np.uint8)
+    b[4:16] = synth.pack_scale_min(np.ones((1, 8), np.uint8), np.zeros((1, 8), np.uint8))[0]
+    qh = rng.integers(0, 256, 32, dtype=np.uint8)
+    qs = rng.integers(0, 256, 128, dtype=np.uint8)
+    b[16:48], b[48:176] = qh, qs
+    w = oracle.q5k_dequant_f32(b)
+    for g in range(4):
+        for h in range(2):
+            for l in range(32):
+                nib = (int(qs[32 * g + l]) >> (4 * h)) & 15
+                q = nib + (16 if (int(qh[l]) >> (2 * g + h)) & 1 else 0)
+                assert w[64 * g + 32 * h + l] == q
+
+
+def test_ple_stage1_oracle_matches_numpy(oracle):
+    """The oracle's PLE stage 1 against a float64 statement of the shader's
+    formula on the same f16 embedding values: equal to f32 rounding."""
+    vocab, layers, T = 16, 5, 3
+    table = synth.q5k_table(vocab, layers, 21)
+    tokens = np.array([0, 15, 7], dtype=np.uint32)
+    rng = np.random.default_rng(22)
+    proj = rng.standard_normal((T, layers * 256)).astype(np.float32)
+    nw = rng.uniform(0.5, 1.5, 256).astype(np.float16)
+    out = oracle.ple_stage1(table, tokens, layers, proj, nw.view(np.uint16), 1e-6)
+    emb = oracle.q5k_dequant_f16(table).view(np.float16).astype(np.float64).reshape(vocab, layers, 256)
+    for t in range(T):
+        for L in range(layers):
+            p = proj[t, 256 * L:256 * (L + 1)].astype(np.float64)
+            rms = np.sqrt(np.sum(p * p) / 256 + 1e-6)
+            ref = (p / rms * nw.astype(np.float64) + emb[tokens[t], L] * 16.0) / np.sqrt(2.0)
+            got = out[t, 256 * L:256 * (L + 1)]
+            assert np.allclose(got, ref, rtol=2e-6, atol=1e-6)
