@@ -16,11 +16,13 @@
 //     per activation row, scaled per row by a power of two), arrives by one
 //     TMA tensor copy in the 128-byte swizzled K-major layout;
 //   * the A operand, the 256 x 64 f16 weights, is dequantized by 8 warps
-//     from the Q4_K bytes (loaded four K steps ahead) into the same swizzled
-//     layout, computed before the stage is free and stored once it is;
+//     into the same swizzled layout, computed before the stage is free and
+//     stored once it is; the raw Q4_K super-blocks reach shared memory by
+//     TMA, one 144-byte box per tile row per super-block column (four K
+//     steps), two columns in flight (a copy warp of its own);
 //   * one thread issues the 8 MMAs and commits them to the stage's "empty"
 //     barrier, which frees the stage for the producers.
-// Three operand stages are in flight.  The epilogue (8 warps: per accumulator one per
+// Two operand stages are in flight.  The epilogue (8 warps: per accumulator one per
 // 32-lane quarter of tensor memory) reads the accumulators, adds each activation
 // row's hi and lo columns, undoes the scale and stores Y.  f16 x f16
 // products are exact and the hi/lo split carries x to ~2^-22, so the result
@@ -47,15 +49,18 @@ constexpr uint32_t kGHalves = 2;                        // MMA row blocks per CT
 constexpr uint32_t kGRows = kGMmaM * kGHalves;          // weight rows per CTA tile
 constexpr uint32_t kGTokens = 128;                      // max activation rows per tile (MMA N = 2 per row)
 constexpr uint32_t kGK = 64;                            // K per stage: 128 bytes of f16 per operand row
-constexpr uint32_t kGStages = 3;
+constexpr uint32_t kGStages = 2;
 constexpr uint32_t kGASub = kGMmaM * kGK * 2;           // 16 KB: one 128-row A block
 constexpr uint32_t kGABytes = kGHalves * kGASub;        // 32 KB
 constexpr uint32_t kGBBytes = 2 * kGTokens * kGK * 2;   // 32 KB
 constexpr uint32_t kGDqWarps = 8;                       // dequantizing warps, also the epilogue
-constexpr uint32_t kGThreads = (2 + kGDqWarps) * 32;    // + B-copy warp + MMA warp
+constexpr uint32_t kGRawWarp = 2 + kGDqWarps;            // the raw-weight copy warp
+constexpr uint32_t kGThreads = (3 + kGDqWarps) * 32;    // + B-copy warp + MMA warp + raw-copy warp
+constexpr uint32_t kGRawStages = 2;                     // raw super-block columns in flight
+constexpr uint32_t kGRawBytes = kGRows * kBlockBytes;   // 36 KB: one super-block of each of the 256 rows
 constexpr uint32_t kGAccCols = 2 * kGTokens;            // fp32 columns of one accumulator
 constexpr uint32_t kGTmemCols = kGHalves * kGAccCols;   // 512: all of tensor memory
-constexpr size_t kGSmem = 1024 + (size_t)kGStages * (kGABytes + kGBBytes);
+constexpr size_t kGSmem = 1024 + (size_t)kGStages * (kGABytes + kGBBytes) + (size_t)kGRawStages * kGRawBytes;
 
 // UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzled
 // layout: 128-byte rows, 8-row groups 1024 bytes apart (stride offset), the
@@ -123,20 +128,18 @@ struct GemmArgs {
 };
 
 // The raw Q4_K bytes one A-producer thread (one row) needs for one K step:
-// the super-block header and the step's 32-byte qs group.  The loads are
-// unconditional (the caller clamps the row, and steps past the end reload
-// the last one), so no register move waits on them before their step.
+// the super-block header and the step's 32-byte qs group, read from the
+// row's 144 bytes in a raw stage (rows 144 bytes apart: the 8 lanes of each
+// 16-byte load phase hit distinct banks).
 struct RawGroup {
   uint4 hd, q0, q1;
 };
 
-__device__ __forceinline__ RawGroup load_group(const uint8_t* wrow, uint32_t ks, uint32_t ksteps) {
+__device__ __forceinline__ RawGroup raw_group(const uint8_t* srow, uint32_t j) {
   RawGroup g;
-  const uint32_t k = ks < ksteps ? ks : ksteps - 1;
-  const uint8_t* b = wrow + (size_t)(k >> 2) * kBlockBytes;
-  g.hd = ldg_nc_v4(b);
-  g.q0 = ldg_nc_v4(b + 16 + 32 * (k & 3u));
-  g.q1 = ldg_nc_v4(b + 32 + 32 * (k & 3u));
+  g.hd = *reinterpret_cast<const uint4*>(srow);
+  g.q0 = *reinterpret_cast<const uint4*>(srow + 16 + 32 * j);
+  g.q1 = *reinterpret_cast<const uint4*>(srow + 32 + 32 * j);
   return g;
 }
 
@@ -159,13 +162,16 @@ __device__ __forceinline__ RowChunks dequant_group(const RawGroup& g, uint32_t j
   return o;
 }
 
-__global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap bmap, const GemmArgs a) {
+__global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap bmap,
+                                                            const __grid_constant__ CUtensorMap amap, const GemmArgs a) {
   extern __shared__ uint8_t g_smem_raw[];
   // swizzled operand tiles start on 1024-byte boundaries
   uint8_t* smem = g_smem_raw + ((1024u - (smem_u32(g_smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + kGStages * kGABytes;
+  uint8_t* sRaw = sB + kGStages * kGBBytes;
   __shared__ uint64_t full_a[kGStages], full_b[kGStages], empty_bar[kGStages], done_bar;
+  __shared__ uint64_t raw_full[kGRawStages], raw_empty[kGRawStages];
   __shared__ uint32_t s_tmem;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -183,6 +189,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&done_bar, 1);
+    for (uint32_t s = 0; s < kGRawStages; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kGDqWarps);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -238,47 +248,43 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       }
       umma_commit(&done_bar);  // the accumulators are final once every MMA above completes
     }
-  } else {
+  } else if (warp < kGRawWarp) {
     // A producers: thread r (0..255) dequantizes tile row r's 64 weights of
     // each K step (its 32-byte qs group, both nibbles: low -> local k 0..31
     // of sub-block 2j, high -> local k 32..63 of sub-block 2j+1) into row
-    // r%128 of A block r/128.  The raw bytes of the next four steps are in
-    // flight in fixed registers, and a step's weights are computed before
-    // waiting for its stage to be free, so only the stores sit between the
-    // tensor core releasing a stage and refilling it.  A warp covers 32
-    // consecutive rows: the 8 lanes of each 16-byte store phase hit 8
-    // different swizzled chunks.
+    // r%128 of A block r/128.  The raw super-blocks arrive by TMA, one
+    // column of the tile's 256 rows per raw stage (four K steps); a step's
+    // weights are computed before waiting for its A stage to be free, so
+    // only the stores sit between the tensor core releasing a stage and
+    // refilling it.  A warp covers 32 consecutive rows: the 8 lanes of each
+    // 16-byte store phase hit 8 different swizzled chunks.  Rows past M
+    // arrive as zeros; their accumulator rows are never stored.
     const uint32_t r = threadIdx.x - 64;
-    const uint32_t nb = a.N >> 8;
-    // rows past M read row M-1: their accumulator rows are never stored
-    const uint8_t* wrow = a.w + (size_t)min(row0 + r, a.M - 1) * nb * kBlockBytes;
     const uint32_t rb = r & (kGMmaM - 1), sw = rb & 7u;  // 128-byte swizzle: chunk index ^ row%8
-    auto produce = [&](const RawGroup& g, uint32_t ks) -> bool {
-      const RowChunks ch = dequant_group(g, ks & 3u);
+    for (uint32_t ks = 0; ks < ksteps && !failed; ++ks) {
+      const uint32_t sb = ks >> 2, j = ks & 3u, rs = sb % kGRawStages;
+      if (j == 0 && !mbar_wait(&raw_full[rs], (sb / kGRawStages) & 1u)) {
+        failed = true;
+        break;
+      }
+      const RawGroup g = raw_group(sRaw + rs * kGRawBytes + r * kBlockBytes, j);
+      if (j == 3) {
+        // the column is in registers: hand the raw stage back
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      }
+      const RowChunks ch = dequant_group(g, j);
       const uint32_t s = ks % kGStages, use = ks / kGStages;
-      if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u)) return false;
+      if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u)) {
+        failed = true;
+        break;
+      }
       uint8_t* dst = sA + s * kGABytes + (r / kGMmaM) * kGASub + rb * 128;
 #pragma unroll
       for (uint32_t c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = ch.c[c];
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(&full_a[s]);
-      return true;
-    };
-    RawGroup ga = load_group(wrow, 0, ksteps), gb = load_group(wrow, 1, ksteps);
-    RawGroup gc = load_group(wrow, 2, ksteps), gd = load_group(wrow, 3, ksteps);
-    for (uint32_t ks = 0; ks < ksteps && !failed; ks += 4) {
-      if (!produce(ga, ks)) { failed = true; break; }
-      ga = load_group(wrow, ks + 4, ksteps);
-      if (ks + 1 >= ksteps) break;
-      if (!produce(gb, ks + 1)) { failed = true; break; }
-      gb = load_group(wrow, ks + 5, ksteps);
-      if (ks + 2 >= ksteps) break;
-      if (!produce(gc, ks + 2)) { failed = true; break; }
-      gc = load_group(wrow, ks + 6, ksteps);
-      if (ks + 3 >= ksteps) break;
-      if (!produce(gd, ks + 3)) { failed = true; break; }
-      gd = load_group(wrow, ks + 7, ksteps);
     }
     // epilogue: warp w reads accumulator (w-2)/4 (rows 128*that ..) in its
     // tensor-memory lane quarter w%4
@@ -298,6 +304,25 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         }
       }
     }
+  } else if (lane == 0) {
+    // raw-weight copy warp: super-block column sb of the tile's 256 rows (one
+    // 144-byte box per row) into raw stage sb % 2, once the producers have
+    // taken the column that stage held
+    const uint32_t nb = a.N >> 8;
+    uint32_t issued = 0;
+    for (uint32_t sb = 0; sb < nb; ++sb) {
+      const uint32_t rs = sb % kGRawStages, use = sb / kGRawStages;
+      if (use > 0 && !mbar_wait(&raw_empty[rs], (use - 1) & 1u)) {
+        failed = true;
+        break;
+      }
+      mbar_arrive_expect_tx(&raw_full[rs], kGRawBytes);
+      tma_tile_g2s(sRaw + rs * kGRawBytes, &amap, sb * (kBlockBytes / 4), row0, &raw_full[rs]);
+      ++issued;
+    }
+    // every issued copy has landed before the CTA can exit
+    for (uint32_t sb = (issued > kGRawStages ? issued - kGRawStages : 0); sb < issued; ++sb)
+      if (!mbar_wait(&raw_full[sb % kGRawStages], (sb / kGRawStages) & 1u)) failed = true;
   }
   if (failed) atomicOr(a.status, 1u);
   if (warp == 1 && lane == 0 && failed) mbar_wait(&done_bar, 0);  // MMAs still running must finish first
@@ -374,6 +399,19 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
   cap -= cap % kGTokens;
   if (cap == 0) return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "N=%u too large for the GEMM scratch", N);
   __half* bbuf = reinterpret_cast<__half*>(ctx->xfrag);
+  // the raw Q4_K matrix as [M rows][N/256*36 words], read in boxes of one
+  // super-block (36 words) x 256 rows; rows past M read as zeros
+  CUtensorMap amap;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)(N / 256) * (kBlockBytes / 4), M};
+    const cuuint64_t strides[1] = {(cuuint64_t)(N / 256) * kBlockBytes};
+    const cuuint32_t box[2] = {kBlockBytes / 4, kGRows};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return ctx_fail(ctx, Q4K_ERR_CUDA, "q4k_gemm weight tensor map");
+  }
   for (uint32_t done = 0; done < T;) {
     const uint32_t tc = (T - done) < cap ? (T - done) : cap;
     gemm_xprep_kernel<<<tc, 256, 0, s>>>(x + (size_t)done * N, bbuf, ctx->inv_scale, N);
@@ -404,7 +442,7 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     ga.tile_tokens = tile;
     ga.status = ctx->select.status;
     const dim3 grid((M + kGRows - 1) / kGRows, (tc + ga.tile_tokens - 1) / ga.tile_tokens);
-    gemm_kernel<<<grid, kGThreads, kGSmem, s>>>(bmap, ga);
+    gemm_kernel<<<grid, kGThreads, kGSmem, s>>>(bmap, amap, ga);
     e = cudaGetLastError();
     if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm launch");
     done += tc;
