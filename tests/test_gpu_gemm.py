@@ -67,3 +67,23 @@ def test_gemm_repeatable_and_leaves_neighbours(ctx):
     assert torch.equal(first.view(torch.int32), y.view(torch.int32))
     assert torch.all(canary[T * M:] == 7.25)
     ctx.check()
+
+
+def test_batched_sweep_streams_match_single_calls(ctx):
+    """Config 4's GEMM path spreads the layers over several streams, each with
+    its own library context: every output equals a single q4k_gemm call on
+    the default stream, bit for bit."""
+    from q4k.decode import BatchedSweep, DecodeStep, E2BShape, layer_shapes
+
+    step = DecodeStep(ctx, E2BShape(layers=3, vocab=1024))
+    bs = BatchedSweep(step, 64, streams=2)
+    bs.run()
+    torch.cuda.synchronize()
+    shapes = layer_shapes(step.shape)
+    for layer in range(3):
+        for name, (M, N) in shapes.items():
+            x = bs.act[layer] if name == "down" else (bs.x_attn if name == "o" else bs.x_h)
+            ref = ctx.gemm(step.weights[(layer, name)], x, M, N)
+            torch.cuda.synchronize()
+            assert torch.equal(ref.view(torch.int32), bs.out[(layer, name)].view(torch.int32)), (layer, name)
+    bs.close()
