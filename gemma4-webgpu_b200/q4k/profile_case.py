@@ -5,6 +5,7 @@
     python gemma4-webgpu_b200/q4k/profile_case.py sweep [--layers L] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py gemm [--batch T] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py q6head [--reps R]
+    python gemma4-webgpu_b200/q4k/profile_case.py ple [--batch T] [--reps R]
 
 `gemv` rotates over 35 distinct 6144x1536 Q4_K matrices (186 MB, more than
 the 126 MB L2, so each launch reads its weights from HBM); `lmhead` runs the
@@ -12,7 +13,10 @@ fused 262144-row LM head (226 MB); `sweep` runs the decode-step plan of
 q4k.decode with L layers (default 8: 159 MB of layer weights plus a
 16384-row LM head); `gemm` runs q4k_gemm on one 6144x1536 matrix with T
 activation rows (default 512); `q6head` runs the fused LM head on a
-131072 x 1536 Q6_K matrix in the device layout (165 MB).  A few hundred MB of device memory at most;
+131072 x 1536 Q6_K matrix in the device layout (165 MB); `ple` runs the
+per-layer-embedding stage 1 for T tokens (default 1) on a 262144 x 35
+super-block Q5_K table (1.6 GB, made on the device), each rep a new
+random token.  A few hundred MB of device memory at most;
 the process exits after `reps` runs.
 """
 from __future__ import annotations
@@ -30,7 +34,7 @@ from q4k import Context, synth  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep", "gemm", "q6head"])
+    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep", "gemm", "q6head", "ple"])
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=40)
@@ -58,6 +62,17 @@ def main() -> None:
         step = DecodeStep(ctx, E2BShape(layers=a.layers, vocab=16384), batch=a.batch)
         for _ in range(a.reps):
             step.run()
+    elif a.kernel == "ple":
+        vocab, layers, T = 262144, 35, a.batch
+        gen = torch.Generator(device=dev).manual_seed(7)
+        table = torch.randint(0, 256, (vocab * layers, 176), dtype=torch.uint8, device=dev, generator=gen)
+        table[:, 0:4] = torch.empty((vocab * layers, 2), dtype=torch.float16, device=dev).uniform_(
+            0.0, 4e-3, generator=gen).view(torch.uint8)
+        proj = torch.randn((T, layers * 256), device=dev, generator=gen)
+        norm = torch.ones(256, dtype=torch.float16, device=dev).view(torch.int16)
+        for _ in range(a.reps):
+            tok = torch.randint(0, vocab, (T,), dtype=torch.int32, device=dev, generator=gen)
+            ctx.ple_stage1(table, tok, vocab, layers, proj, norm)
     elif a.kernel == "q6head":
         V, N = 131072, 1536
         w = ctx.q6k_repack(torch.from_numpy(synth.q6k_matrix(V, N, synth.seed_for(5, 999)).reshape(-1)).to(dev),
