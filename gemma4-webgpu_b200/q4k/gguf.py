@@ -113,6 +113,20 @@ class GGUFFile:
             raise GGUFError(f"{name}: N={N} is not a multiple of 256")
         return self.tensor_bytes(t).reshape(M, N // 256 * 210), M, N
 
+    def q5k_table(self, name: str, layers: int) -> tuple[np.ndarray, int]:
+        """A Q5_K per-layer embedding table (per_layer_token_embd) as
+        q4k_ple_stage1 takes it: (bytes [vocab, layers*176], vocab).  GGUF
+        stores it as [ne0 = layers*256, ne1 = vocab]: row v is `layers`
+        consecutive super-blocks, block L being layer L's 256 values
+        (src/engine.ts:681-702)."""
+        t = self.by_name[name]
+        if t.type != TYPE_Q5_K:
+            raise GGUFError(f"{name} is {TYPE_NAMES.get(t.type, t.type)}, not Q5_K")
+        vocab, width = t.matrix_shape
+        if width != layers * 256:
+            raise GGUFError(f"{name}: row length {width} is not layers*256 = {layers * 256}")
+        return self.tensor_bytes(t).reshape(vocab, layers * 176), vocab
+
     def q4k_matrix(self, name: str) -> tuple[np.ndarray, int, int]:
         """A Q4_K matrix as libq4k takes it: (bytes [M, N/256*144], M, N)."""
         t = self.by_name[name]

@@ -163,3 +163,34 @@ def test_gguf_tied_embedding_lm_head(gf, ctx, oracle):
     # the fused candidates are the standalone topk256 of the device logits
     buf = ctx.topk256(sel.logits).cpu().numpy()
     assert np.array_equal(buf[1::2].view(np.uint32), sel.cand_idx.cpu().numpy().view(np.uint32))
+
+
+def test_q5k_table_shape_checks(gf):
+    b, vocab = gf.q5k_table("blk.0.q5_k.weight", 1)
+    assert b.shape == (2, 176) and vocab == 2
+    with pytest.raises(G.GGUFError):
+        gf.q5k_table("blk.0.q5_k.weight", 2)  # the rows hold one layer, not two
+    with pytest.raises(G.GGUFError):
+        gf.q5k_table("blk.0.q6_k.weight", 1)
+
+
+@pytest.mark.gpu
+def test_gguf_q5k_table_through_ple_stage1(gf, ctx, oracle):
+    """The Q5_K tensor of the file, used as a one-layer per-layer-embedding
+    table: its decoded values (weight probe) and ple_stage1 for both rows
+    equal the oracle's."""
+    torch = pytest.importorskip("torch")
+    b, vocab = gf.q5k_table("blk.0.q5_k.weight", 1)
+    table = torch.from_numpy(np.array(b)).to(ctx.device)
+    probe = ctx.q5k_dequant_f16(table.reshape(-1)).cpu().numpy().view(np.uint16)
+    assert np.array_equal(probe, oracle.q5k_dequant_f16(b))
+    tokens = np.array([1, 0], dtype=np.uint32)
+    proj = synth.activations(2, 256, seed=78)
+    nw = np.linspace(0.5, 1.5, 256).astype(np.float16).view(np.uint16)
+    out = ctx.ple_stage1(table, torch.from_numpy(tokens.view(np.int32)).to(ctx.device), vocab, 1,
+                         torch.from_numpy(proj).to(ctx.device), torch.from_numpy(nw.view(np.int16)).to(ctx.device),
+                         1e-6).cpu().numpy()
+    ref = oracle.ple_stage1(b, tokens, 1, proj, nw, 1e-6)
+    # same f32 operations in the same order on both sides: at most 1 ulp apart
+    ia, ib = out.view(np.int32).astype(np.int64), ref.view(np.int32).astype(np.int64)
+    assert np.max(np.abs(ia - ib)) <= 1
