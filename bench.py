@@ -358,10 +358,10 @@ def run_ours(args) -> None:
                                      "launches_per_call": 1, "matches_unsharded": fsame}
 
     # end to end through the public API: pinned host inputs in, results out
-    x_host = [torch.empty_like(step.x_h, device="cpu").pin_memory(),
-              torch.empty_like(step.x_attn, device="cpu").pin_memory()]
-    x_host[0].copy_(step.x_h)
-    x_host[1].copy_(step.x_attn)
+    # the step's inputs (x_h | x_attn) and results (candidates | argmax) each
+    # sit in one device buffer: one host->device and one device->host copy
+    x_host = [torch.empty_like(step.inputs, device="cpu").pin_memory()]
+    x_host[0].copy_(step.inputs)
     res = step.result_tensors()
     res_host = [torch.empty_like(t, device="cpu").pin_memory() for t in res]
     h2d = sum(t.numel() * t.element_size() for t in x_host)
@@ -369,8 +369,7 @@ def run_ours(args) -> None:
 
     def e2e_step():
         with torch.cuda.stream(s):
-            step.x_h.copy_(x_host[0], non_blocking=True)
-            step.x_attn.copy_(x_host[1], non_blocking=True)
+            step.inputs.copy_(x_host[0], non_blocking=True)
             graph.graph.replay()
             for d, h in zip(res, res_host):
                 h.copy_(d, non_blocking=True)

@@ -97,18 +97,24 @@ class DecodeStep:
                     w = synth.q4k_matrix(M, N, matrix_seed(layer, name))
                     self.weights[(layer, name)] = torch.from_numpy(w).to(dev)
             self.lm_head = torch.from_numpy(synth.q4k_matrix(s.vocab, s.hidden, LMHEAD_SEED)).to(dev)
-        self.x_h = torch.from_numpy(synth.activations(B, s.hidden, synth.seed_for(CONFIG, 100))).to(dev)
-        self.x_attn = torch.from_numpy(synth.activations(B, s.q, synth.seed_for(CONFIG, 101))).to(dev)
+        # the step's inputs share one buffer (one host->device copy per token)
+        self.inputs = torch.empty(B * (s.hidden + s.q), dtype=torch.float32, device=dev)
+        self.x_h = self.inputs[: B * s.hidden].view(B, s.hidden)
+        self.x_attn = self.inputs[B * s.hidden:].view(B, s.q)
+        self.x_h.copy_(torch.from_numpy(synth.activations(B, s.hidden, synth.seed_for(CONFIG, 100))))
+        self.x_attn.copy_(torch.from_numpy(synth.activations(B, s.q, synth.seed_for(CONFIG, 101))))
         f32 = dict(dtype=torch.float32, device=dev)
         # distinct outputs per layer: a plan runs the layers concurrently
         self.out = {(layer, name): torch.empty((B, shapes[name][0]), **f32)
                     for layer in range(s.layers) for name in LAYER_MATS}
         self.act = [torch.empty((B, s.ffn), **f32) for _ in range(s.layers)]
         if B == 1:
+            # candidates and argmax share one buffer (one device->host copy per token)
+            self.results = torch.empty(513, dtype=torch.int32, device=dev)
             self.sel = Selection(
-                cand_val=torch.empty(256, **f32),
-                cand_idx=torch.empty(256, dtype=torch.int32, device=dev),
-                argmax=torch.empty(1, dtype=torch.int32, device=dev),
+                cand_val=self.results[:256].view(torch.float32),
+                cand_idx=self.results[256:512],
+                argmax=self.results[512:],
                 logits=None,
             )
         else:
@@ -226,7 +232,7 @@ class DecodeStep:
         """What a decode step hands back to the host: the sampled token and the
         2 KB topk256 candidates (src/engine.ts:1731-1741)."""
         if self.batch == 1:
-            return [self.sel.argmax, self.sel.cand_val, self.sel.cand_idx]
+            return [self.results]  # cand_val [256] f32 | cand_idx [256] | argmax [1]
         return [self.argmax, self.topk]
 
     def sample_matrices(self, layers: int = 1) -> list[tuple[np.ndarray, int, int]]:
