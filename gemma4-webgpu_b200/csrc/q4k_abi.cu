@@ -104,7 +104,8 @@ int q4k_create(int device, q4k_ctx** out) {
   ctx->sm_count = prop.multiProcessorCount;
   const size_t sel_bytes = 256 * sizeof(unsigned long long) + 256;
   const size_t scale_bytes = kCtxScaleSlots * sizeof(float);
-  const size_t total = sel_bytes + scale_bytes + kCtxXfragBytes;
+  const size_t rows_bytes = kMaxSelectRows * 256 * sizeof(unsigned long long) + 256;
+  const size_t total = sel_bytes + scale_bytes + kCtxXfragBytes + rows_bytes;
   if (cudaMalloc(&ctx->scratch, total) != cudaSuccess) {
     delete ctx;
     return Q4K_ERR_CUDA;
@@ -116,7 +117,11 @@ int q4k_create(int device, q4k_ctx** out) {
   ctx->inv_scale = reinterpret_cast<float*>(base + sel_bytes);
   ctx->xfrag = reinterpret_cast<uint2*>(base + sel_bytes + scale_bytes);
   ctx->xfrag_cap = kCtxXfragBytes;
-  if (init_select_scratch(ctx->select, nullptr) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+  ctx->row_slots = reinterpret_cast<unsigned long long*>(base + sel_bytes + scale_bytes + kCtxXfragBytes);
+  ctx->row_counters = reinterpret_cast<uint32_t*>(ctx->row_slots + kMaxSelectRows * 256);
+  if (init_select_scratch(ctx->select, nullptr) != cudaSuccess ||
+      init_row_slots(ctx->row_slots, ctx->row_counters, kMaxSelectRows, nullptr) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(ctx->scratch);
     delete ctx;
     return Q4K_ERR_CUDA;
@@ -207,6 +212,19 @@ int q4k_topk256(q4k_ctx* ctx, const float* logits, uint32_t n, float* result, vo
   if (!ctx) return Q4K_ERR_INVALID_ARG;
   if (!logits || !result) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
   return ctx_cuda(ctx, launch_topk256(logits, n, result, static_cast<cudaStream_t>(stream)), "q4k_topk256 launch");
+}
+
+int q4k_select_rows(q4k_ctx* ctx, float* logits, uint32_t B, uint32_t n, float cap, float* cand_val,
+                    uint32_t* cand_idx, uint32_t* argmax, void* stream) {
+  if (!ctx) return Q4K_ERR_INVALID_ARG;
+  if (!logits || !cand_val || !cand_idx || !argmax) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (B == 0 || B > kMaxSelectRows)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "q4k_select_rows: B=%u outside [1, %u]", B, kMaxSelectRows);
+  if (n == 0 || n >= (1u << 31)) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "q4k_select_rows: n=%u out of range", n);
+  return ctx_cuda(ctx,
+                  launch_select_rows(logits, B, n, cap, ctx->row_slots, ctx->row_counters, cand_val, cand_idx, argmax,
+                                     ctx->sm_count, static_cast<cudaStream_t>(stream)),
+                  "q4k_select_rows launch");
 }
 
 int q4k_gelu_mul(q4k_ctx* ctx, const float* gate, const float* up, float* out, uint32_t n, void* stream) {

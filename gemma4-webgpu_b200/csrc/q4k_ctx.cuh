@@ -18,6 +18,8 @@ struct q4k_ctx {
   uint2* xfrag = nullptr;
   size_t xfrag_cap = 0;  // bytes
   float* inv_scale = nullptr;  // [kCtxScaleSlots]: 1/scale per activation row
+  unsigned long long* row_slots = nullptr;  // [kMaxSelectRows][256]: q4k_select_rows keys
+  uint32_t* row_counters = nullptr;         // [kMaxSelectRows]
   void* scratch = nullptr;     // the one allocation holding all of the above
   char err[512] = {0};
 };

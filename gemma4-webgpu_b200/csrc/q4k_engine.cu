@@ -70,25 +70,6 @@ __device__ __forceinline__ EngineTask task_at(const TaskList& tl, uint32_t i) {
   return tl.dev ? tl.dev[i] : tl.inl;
 }
 
-// Order key for the cross-warp atomicMax merge of selection candidates:
-// larger value first, then lower index; -0.0 orders with +0.0 and keeps its
-// sign in bit 0.  Index < 2^31.
-__device__ __forceinline__ unsigned long long sel_key(float v, uint32_t idx) {
-  uint32_t b = __float_as_uint(v);
-  const uint32_t neg_zero = (b == 0x80000000u) ? 1u : 0u;
-  if (neg_zero) b = 0u;
-  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return ((unsigned long long)ord << 32) | ((unsigned long long)(0x7fffffffu - idx) << 1) | neg_zero;
-}
-
-__device__ __forceinline__ void sel_unkey(unsigned long long k, float& v, uint32_t& idx) {
-  const uint32_t ord = (uint32_t)(k >> 32);
-  uint32_t b = (ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord;
-  if (k & 1ull) b = 0x80000000u;
-  v = __uint_as_float(b);
-  idx = 0x7fffffffu - (uint32_t)((k >> 1) & 0x7fffffffu);
-}
-
 // ---- programmatic dependent launch ----------------------------------------------------
 // Engine launches are made with programmatic stream serialization: a launch
 // may start while the previous kernel on the stream finishes, runs its

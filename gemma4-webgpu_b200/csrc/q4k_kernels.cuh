@@ -35,6 +35,15 @@ cudaError_t launch_argmax(const float* logits, uint32_t n, uint32_t* result, cud
 cudaError_t launch_topk256(const float* logits, uint32_t n, float* result512, cudaStream_t s);
 cudaError_t launch_gelu_mul(const float* gate, const float* up, float* out, uint32_t n, cudaStream_t s);
 
+// Softcap (cap > 0) + per-residue candidates + argmax of B <= kMaxSelectRows
+// rows of n logits in one launch, over the row scratch (slots [rows][256],
+// counters [rows]) that init_row_slots prepares.
+constexpr uint32_t kMaxSelectRows = 16;
+cudaError_t init_row_slots(unsigned long long* slots, uint32_t* counters, uint32_t rows, cudaStream_t s);
+cudaError_t launch_select_rows(float* logits, uint32_t B, uint32_t n, float cap, unsigned long long* slots,
+                               uint32_t* counters, float* cand_val, uint32_t* cand_idx, uint32_t* argmax, int sms,
+                               cudaStream_t s);
+
 // Merge G ranks' candidate sets ([G][256] each, rank-major) into one.
 cudaError_t launch_merge_candidates(const float* vals, const uint32_t* idx, uint32_t G, float* out_val,
                                     uint32_t* out_idx, uint32_t* argmax, cudaStream_t s);

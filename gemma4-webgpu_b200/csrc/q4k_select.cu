@@ -92,6 +92,71 @@ __global__ void __launch_bounds__(1024) select_kernel(const float* __restrict__ 
   }
 }
 
+// Softcap + topk256 + argmax for B rows in one launch (the batch-B tail of
+// sampleNextTokenSubmit, src/engine.ts:1686-1741): CTA (c, row) scans
+// 256-element groups [c*gpc, (c+1)*gpc) of its row, thread t keeping residue
+// t's first strict maximum (softcapping and storing the logits on the way
+// when cap > 0, as logit_softcap.wgsl does in place), publishes it as an
+// order key with atomicMax into the row's 256 slots, and the last CTA of the
+// row (completion counter) turns the keys into the candidates and runs the
+// reference's argmax tree, then puts the slots and counter back to their
+// between-calls state.
+__global__ void __launch_bounds__(256) select_rows_kernel(float* __restrict__ logits, uint32_t n, float cap,
+                                                          uint32_t gpc, unsigned long long* __restrict__ slots,
+                                                          uint32_t* __restrict__ counters, float* __restrict__ cand_val,
+                                                          uint32_t* __restrict__ cand_idx,
+                                                          uint32_t* __restrict__ argmax_out) {
+  __shared__ float s_v[256];
+  __shared__ uint32_t s_i[256];
+  __shared__ uint32_t s_last;
+  const uint32_t row = blockIdx.y, t = threadIdx.x;
+  float* L = logits + (size_t)row * n;
+  const uint32_t groups = (n + 255u) / 256u;
+  const uint32_t g0 = blockIdx.x * gpc, g1 = min(groups, g0 + gpc);
+  float bv = kFloor;
+  uint32_t bi = 0u;
+  for (uint32_t g = g0; g < g1; ++g) {
+    const uint32_t i = g * 256u + t;
+    if (i < n) {
+      float v = L[i];
+      if (cap > 0.0f) {
+        v = softcap(v, cap);
+        L[i] = v;
+      }
+      if (better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+  }
+  unsigned long long* S = slots + (size_t)row * 256u;
+  if (!(bv == kFloor && bi == 0u)) atomicMax(&S[t], sel_key(bv, bi));
+  __threadfence();
+  __syncthreads();
+  if (t == 0) s_last = (atomicAdd(&counters[row], 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float v;
+  uint32_t i;
+  sel_unkey(atomicExch(&S[t], sel_key(kFloor, 0u)), v, i);
+  cand_val[(size_t)row * 256u + t] = v;
+  cand_idx[(size_t)row * 256u + t] = i;
+  s_v[t] = v;
+  s_i[t] = i;
+  __syncthreads();
+  const uint32_t am = residue_argmax(s_v, s_i);
+  if (t == 0) {
+    argmax_out[row] = am;
+    counters[row] = 0u;
+  }
+}
+
+__global__ void init_row_slots_kernel(unsigned long long* slots, uint32_t* counters) {
+  slots[blockIdx.x * 256u + threadIdx.x] = sel_key(kFloor, 0u);
+  if (threadIdx.x == 0) counters[blockIdx.x] = 0u;
+}
+
 // shaders/gelu_mul.wgsl:14-16.
 __global__ void gelu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up,
                                 float* __restrict__ out, uint32_t n) {
@@ -150,6 +215,23 @@ cudaError_t launch_gelu_mul(const float* gate, const float* up, float* out, uint
   if (grid > 4096) grid = 4096;
   if (grid == 0) grid = 1;
   gelu_mul_kernel<<<grid, 256, 0, s>>>(gate, up, out, n);
+  return cudaGetLastError();
+}
+
+cudaError_t init_row_slots(unsigned long long* slots, uint32_t* counters, uint32_t rows, cudaStream_t s) {
+  init_row_slots_kernel<<<rows, 256, 0, s>>>(slots, counters);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select_rows(float* logits, uint32_t B, uint32_t n, float cap, unsigned long long* slots,
+                               uint32_t* counters, float* cand_val, uint32_t* cand_idx, uint32_t* argmax, int sms,
+                               cudaStream_t s) {
+  const uint32_t groups = (n + 255u) / 256u;
+  uint32_t per_row = (2u * (uint32_t)sms) / B;  // about two CTAs per SM over all rows
+  per_row = per_row == 0 ? 1u : per_row;
+  const uint32_t gpc = (groups + per_row - 1) / per_row;
+  const uint32_t ctas = (groups + gpc - 1) / gpc;
+  select_rows_kernel<<<dim3(ctas, B), 256, 0, s>>>(logits, n, cap, gpc, slots, counters, cand_val, cand_idx, argmax);
   return cudaGetLastError();
 }
 

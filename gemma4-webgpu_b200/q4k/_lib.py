@@ -34,6 +34,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_logit_softcap": ([_P, _P, _U32, _F, _P], _I),
     "q4k_argmax": ([_P, _P, _U32, _P, _P], _I),
     "q4k_topk256": ([_P, _P, _U32, _P, _P], _I),
+    "q4k_select_rows": ([_P, _P, _U32, _U32, _F, _P, _P, _P, _P], _I),
     "q4k_gelu_mul": ([_P, _P, _P, _P, _U32, _P], _I),
     "q4k_lmhead_select": ([_P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_merge_candidates": ([_P, _P, _P, _U32, _P, _P, _P, _P], _I),

@@ -119,8 +119,11 @@ class DecodeStep:
             )
         else:
             self.logits = torch.empty((B, s.vocab), **f32)
-            self.topk = torch.empty((B, 512), **f32)
-            self.argmax = torch.empty((B,), dtype=torch.int32, device=dev)
+            # per row: candidates and argmax, all rows in one buffer (one copy back)
+            self.results = torch.empty(B * 513, dtype=torch.int32, device=dev)
+            self.cand_val = self.results[: 256 * B].view(torch.float32).view(B, 256)
+            self.cand_idx = self.results[256 * B: 512 * B].view(B, 256)
+            self.argmax = self.results[512 * B:]
         self._plan: Plan | None = None
 
     # ---- accounting ---------------------------------------------------------
@@ -153,11 +156,11 @@ class DecodeStep:
         return total + synth.q4k_bytes(s.vocab, s.hidden) + 4 * B * s.hidden + B * (256 * 8 + 4)
 
     def launches_per_step(self) -> int:
-        return self.plan().launches() + (0 if self.batch == 1 else 3 * self.batch)
+        return self.plan().launches() + (0 if self.batch == 1 else 1)
 
     def serial_calls_per_step(self) -> int:
         per_layer = len(LAYER_MATS) + 1  # 7 GEMVs + gelu_mul
-        lm = 1 if self.batch == 1 else 1 + 3 * self.batch
+        lm = 1 if self.batch == 1 else 2
         return self.shape.layers * per_layer + lm
 
     # ---- the plan ---------------------------------------------------------------
@@ -192,11 +195,9 @@ class DecodeStep:
         return p
 
     def _select_rows(self, stream) -> None:
-        c, s = self.ctx, self.shape
-        for b in range(self.batch):
-            c.logit_softcap(self.logits[b], s.softcap, stream=stream)
-            c.topk256(self.logits[b], out=self.topk[b], stream=stream)
-            c.argmax(self.logits[b], out=self.argmax[b:b + 1], stream=stream)
+        """Softcap + topk256 + argmax of every row's logits, one launch."""
+        self.ctx.select_rows(self.logits, self.shape.softcap, self.cand_val, self.cand_idx, self.argmax,
+                             stream=stream)
 
     def run(self, stream: torch.cuda.Stream | None = None) -> None:
         """One decode step through the plan (4 launches at batch 1)."""
@@ -231,9 +232,9 @@ class DecodeStep:
     def result_tensors(self) -> list[torch.Tensor]:
         """What a decode step hands back to the host: the sampled token and the
         2 KB topk256 candidates (src/engine.ts:1731-1741)."""
-        if self.batch == 1:
-            return [self.results]  # cand_val [256] f32 | cand_idx [256] | argmax [1]
-        return [self.argmax, self.topk]
+        # batch 1: cand_val [256] f32 | cand_idx [256] | argmax [1]; batch B:
+        # cand_val [B][256] | cand_idx [B][256] | argmax [B]
+        return [self.results]
 
     def sample_matrices(self, layers: int = 1) -> list[tuple[np.ndarray, int, int]]:
         """Host copies (regenerated from the same seeds) of the first `layers`

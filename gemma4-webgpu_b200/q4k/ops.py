@@ -303,6 +303,30 @@ class Context:
         self._check(self._L.q4k_topk256(self._h, _ptr(logits), logits.numel(), _ptr(out), _stream(stream)))
         return out
 
+    def select_rows(self, logits: torch.Tensor, cap: float = 30.0, cand_val: torch.Tensor | None = None,
+                    cand_idx: torch.Tensor | None = None, argmax: torch.Tensor | None = None,
+                    stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Softcap (cap > 0, in place) + topk256 + argmax of every row of
+        logits [B, n] in one launch (q4k_select_rows).  Returns (cand_val
+        [B, 256] f32, cand_idx [B, 256] int32, argmax [B] int32)."""
+        _need(logits, torch.float32, "logits", self.device)
+        if logits.dim() != 2:
+            raise ValueError("logits must be [B, n]")
+        B, n = logits.shape
+        f32 = dict(dtype=torch.float32, device=self.device)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        cand_val = torch.empty((B, 256), **f32) if cand_val is None else cand_val
+        cand_idx = torch.empty((B, 256), **i32) if cand_idx is None else cand_idx
+        argmax = torch.empty(B, **i32) if argmax is None else argmax
+        _need(cand_val, torch.float32, "cand_val", self.device)
+        _need(cand_idx, torch.int32, "cand_idx", self.device)
+        _need(argmax, torch.int32, "argmax", self.device)
+        if cand_val.numel() < B * 256 or cand_idx.numel() < B * 256 or argmax.numel() < B:
+            raise ValueError("output buffers smaller than [B, 256] / [B]")
+        self._check(self._L.q4k_select_rows(self._h, _ptr(logits), B, n, cap, _ptr(cand_val), _ptr(cand_idx),
+                                            _ptr(argmax), _stream(stream)))
+        return cand_val, cand_idx, argmax
+
     def gelu_mul(self, gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None,
                  stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """GELU_tanh(gate) * up, shaders/gelu_mul.wgsl."""

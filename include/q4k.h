@@ -125,6 +125,18 @@ Q4K_API int q4k_argmax(q4k_ctx* ctx, const float* logits, uint32_t n, uint32_t* 
  * (shaders/topk256.wgsl:5-21; buffer src/engine.ts:1042). */
 Q4K_API int q4k_topk256(q4k_ctx* ctx, const float* logits, uint32_t n, float* result, void* stream);
 
+/* logitSoftcap + topk256 + argmax for B (1..16) rows of n logits (row b at
+ * logits + b*n) in one launch: the per-token tail of sampleNextTokenSubmit
+ * (src/engine.ts:1686-1741) when several sequences decode together.  cap > 0
+ * softcaps the logits in place first (shaders/logit_softcap.wgsl:9-16);
+ * cap <= 0 leaves them.  cand_val [B][256] / cand_idx [B][256] are each
+ * row's topk256 pairs (shaders/topk256.wgsl:5-21), argmax [B] its argmax
+ * (shaders/argmax.wgsl:7-34), bit-identical to q4k_logit_softcap then
+ * q4k_topk256 and q4k_argmax per row.  Uses the context's row scratch: order
+ * the calls of one context on one stream. */
+Q4K_API int q4k_select_rows(q4k_ctx* ctx, float* logits, uint32_t B, uint32_t n, float cap, float* cand_val,
+                            uint32_t* cand_idx, uint32_t* argmax, void* stream);
+
 /* gelu_mul: out[i] = GELU_tanh(gate[i]) * up[i] (shaders/gelu_mul.wgsl:1-17). */
 Q4K_API int q4k_gelu_mul(q4k_ctx* ctx, const float* gate, const float* up, float* out, uint32_t n, void* stream);
 

@@ -119,6 +119,52 @@ def test_standalone_select_ops_exact(ctx, golden_dir):
         assert np.array_equal(buf[1::2].view(np.uint32), g[f"{case}_idx"]), case
 
 
+def test_select_rows_golden_exact(ctx, golden_dir):
+    """The batched softcap/topk256/argmax (one launch for all rows) on the
+    golden selection cases (ties, NaN, the -1e30 floor, ragged and tiny
+    lengths), without a softcap: bit-exact candidates and argmax."""
+    g = np.load(golden_dir / "select.npz")
+    for case in ("plain", "ties", "nan", "floor", "ragged", "tiny"):
+        logits = g[f"{case}_logits"]
+        rows = np.stack([logits, logits])  # two identical rows: both must give the golden answer
+        cv, ci, am = ctx.select_rows(to_dev(rows), 0.0)
+        for b in range(2):
+            assert int(am[b].cpu()) == int(g[f"{case}_argmax"]), case
+            assert np.array_equal(cv[b].cpu().numpy().view(np.uint32), g[f"{case}_vals"].view(np.uint32)), case
+            assert np.array_equal(ci[b].cpu().numpy().view(np.uint32), g[f"{case}_idx"]), case
+
+
+@pytest.mark.parametrize("B,n", [(1, 262144), (4, 262144), (3, 1000), (16, 4096), (2, 37)])
+def test_select_rows_equals_per_row_ops(ctx, B, n):
+    """With a softcap: the one-launch form equals q4k_logit_softcap +
+    q4k_topk256 + q4k_argmax run row by row, bit for bit (softcapped logits
+    included), on rows with planted ties and NaN."""
+    rng = np.random.default_rng(B * 1000 + n)
+    x = (rng.standard_normal((B, n)) * 40).astype(np.float32)
+    x[:, n // 3] = 500.0
+    x[:, (2 * n) // 3] = 500.0  # a tie at the top (after the softcap too)
+    x[0, n // 2] = np.nan
+    got = to_dev(x)
+    cv, ci, am = ctx.select_rows(got, 30.0)
+    for b in range(B):
+        row = to_dev(x[b])
+        ctx.logit_softcap(row, 30.0)
+        assert torch.equal(row.view(torch.int32), got[b].view(torch.int32)), b
+        buf = ctx.topk256(row).cpu().numpy()
+        assert np.array_equal(cv[b].cpu().numpy().view(np.uint32), buf[0::2].view(np.uint32)), b
+        assert np.array_equal(ci[b].cpu().numpy().view(np.uint32), buf[1::2].view(np.uint32)), b
+        assert int(am[b].cpu()) == int(ctx.argmax(row).cpu()[0]), b
+
+
+def test_select_rows_repeat_calls(ctx):
+    """The row scratch is back in its between-calls state after every call."""
+    x = torch.randn(4, 5000, device=DEV)
+    first = [t.clone() for t in ctx.select_rows(x.clone(), 0.0)]
+    for _ in range(3):
+        again = ctx.select_rows(x.clone(), 0.0)
+        assert all(torch.equal(a, b) for a, b in zip(first, again))
+
+
 def test_softcap_and_gelu(ctx, oracle):
     rng = np.random.default_rng(4)
     v = (rng.standard_normal(100_000) * 200).astype(np.float32)
