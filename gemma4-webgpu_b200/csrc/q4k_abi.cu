@@ -71,6 +71,10 @@ int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
       tl.inl.tile_bytes = tile_bytes;
       tl.total_items = tiles_of(M);
       tl.total_cost = tiles_of(M) * (N / Q4K_QK);
+      // long rows (e.g. the FFN down projection): 4 warps share each tile,
+      // one K quarter each, as plans do for such stages
+      const uint32_t nb = N / Q4K_QK;
+      tl.ksplit = (b <= 4 && nb >= 16 && nb % 4 == 0) ? 4u : 0u;
       e = launch_engine(tl, map, b, false, ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv engine launch");
     } else {

@@ -1047,8 +1047,11 @@ cudaError_t launch_xprep(const JobList& jobs, uint32_t batch, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// One CTA per SM up to the item count: a launch with fewer items than SMs
+// gives each item an SM of its own (the math of an item then runs with the
+// whole SM to itself instead of sharing it with 15 other warps).
 uint32_t engine_grid(uint32_t total_items, int sm_count) {
-  uint32_t grid = (total_items + kEngineWarps - 1) / kEngineWarps;
+  uint32_t grid = total_items;
   if (grid > (uint32_t)sm_count) grid = (uint32_t)sm_count;
   return grid == 0 ? 1 : grid;
 }

@@ -235,9 +235,11 @@ def test_real_e2b_step_plan_matches_serial(ctx, oracle):
     step.run_serial()
     torch.cuda.synchronize()
     for k in got:
-        if k[1] == "down":
-            # a stage of long-row downs splits each tile's K range over 4 warps
-            # (partial sums added in order): the same products, another order
+        M, N, fmt, _ = step.mats[k]
+        if k[1] == "down" or (fmt != FMT_Q6K and N // 256 >= 16):
+            # long rows split each tile's K range over 4 warps (partial sums
+            # added in order) in a stage of downs and in single calls: the
+            # same products, another order
             d = (got[k] - step.out[k]).norm() / step.out[k].norm()
             assert d <= 2e-5, (k, float(d))
         else:
