@@ -248,12 +248,26 @@ class DecodeStep:
 
 class StepGraph:
     """A decode step captured once as a CUDA graph and replayed per token (the
-    way the engine pre-builds its bind groups and only re-dispatches)."""
+    way the engine pre-builds its bind groups and only re-dispatches).
 
-    def __init__(self, step: DecodeStep, stream: torch.cuda.Stream | None = None, body=None):
+    host_io = (inputs_host, results_host), pinned host tensors shaped like
+    step.inputs and step.results: the graph then also copies the token's
+    inputs in and its results out, so one replay is the whole host-visible
+    step (read results_host after synchronizing the stream)."""
+
+    def __init__(self, step: DecodeStep, stream: torch.cuda.Stream | None = None, body=None,
+                 host_io: tuple[torch.Tensor, torch.Tensor] | None = None):
         self.step = step
         self.stream = stream or torch.cuda.Stream(device=step.ctx.device)
         body = body or step.run
+        if host_io is not None:
+            x_host, r_host = host_io
+            inner = body
+
+            def body(st):  # noqa: F811 -- the step with its host copies around it
+                step.inputs.copy_(x_host, non_blocking=True)
+                inner(st)
+                r_host.copy_(step.results, non_blocking=True)
         with torch.cuda.stream(self.stream):
             body(self.stream)  # warm-up outside capture
         self.stream.synchronize()
