@@ -241,6 +241,11 @@ def run_ours(args) -> None:
     s0_ms, s0_graph = time_body(lambda st: stage0.run(st), reps)
     s0_bytes = step.stage0_bytes()
     s0_gbs = s0_bytes / (s0_ms / 1e3) / 1e9
+    # the second launch: gelu_mul + the 35 down projections (4 warps per tile)
+    stage1 = step.plan(stages=(1,))
+    s1_ms, s1_graph = time_body(lambda st: stage1.run(st), reps)
+    s1_gbs = step.stage1_bytes() / (s1_ms / 1e3) / 1e9
+    del s1_graph
     # the same step as one libq4k call per reference dispatch (246 launches)
     serial_ms, serial_graph = time_body(step.run_serial, reps)
     # the LM head alone
@@ -404,6 +409,8 @@ def run_ours(args) -> None:
     }
     kernels = {"stage0_engine": {"ms": round(s0_ms, 4), "GB/s": round(s0_gbs, 1),
                                  "frac_of_peak": round(s0_gbs / pk["hbm_gbs"], 4)},
+               "stage1_engine": {"ms": round(s1_ms, 4), "GB/s": round(s1_gbs, 1),
+                                 "frac_of_peak": round(s1_gbs / pk["hbm_gbs"], 4)},
                "serial_step": {"ms": round(serial_ms, 4), "launches": step.serial_calls_per_step(),
                                "GB/s": round(bytes_step / (serial_ms / 1e3) / 1e9, 1),
                                "tokens_per_s": round(args.batch / (serial_ms / 1e3), 1)}}

@@ -155,6 +155,13 @@ class DecodeStep:
                 total += s.layers * (synth.q4k_bytes(M, N) + 4 * B * (M + N))
         return total + synth.q4k_bytes(s.vocab, s.hidden) + 4 * B * s.hidden + B * (256 * 8 + 4)
 
+    def stage1_bytes(self) -> int:
+        """Algorithmic bytes of the plan's second engine launch: gelu_mul
+        (gate, up in; act out) and the down projections."""
+        s, B = self.shape, self.batch
+        M, N = layer_shapes(s)["down"]
+        return s.layers * (synth.q4k_bytes(M, N) + 4 * B * (M + N) + 3 * 4 * B * s.ffn)
+
     def launches_per_step(self) -> int:
         return self.plan().launches() + (0 if self.batch == 1 else 1)
 

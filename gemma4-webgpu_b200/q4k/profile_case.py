@@ -6,6 +6,7 @@
     python gemma4-webgpu_b200/q4k/profile_case.py gemm [--batch T] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py q6head [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py ple [--batch T] [--reps R]
+    python gemma4-webgpu_b200/q4k/profile_case.py downs [--reps R]
 
 `gemv` rotates over 35 distinct 6144x1536 Q4_K matrices (186 MB, more than
 the 126 MB L2, so each launch reads its weights from HBM); `lmhead` runs the
@@ -16,7 +17,8 @@ activation rows (default 512); `q6head` runs the fused LM head on a
 131072 x 1536 Q6_K matrix in the device layout (165 MB); `ple` runs the
 per-layer-embedding stage 1 for T tokens (default 1) on a 262144 x 35
 super-block Q5_K table (1.6 GB, made on the device), each rep a new
-random token.  A few hundred MB of device memory at most;
+random token; `downs` runs the decode step's second plan stage alone
+(gelu_mul + the 35 down projections 1536 x 6144, 186 MB, 4 warps per tile).  A few hundred MB of device memory at most;
 the process exits after `reps` runs.
 """
 from __future__ import annotations
@@ -34,7 +36,7 @@ from q4k import Context, synth  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep", "gemm", "q6head", "ple"])
+    ap.add_argument("kernel", choices=["gemv", "lmhead", "sweep", "gemm", "q6head", "ple", "downs"])
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=40)
@@ -62,6 +64,14 @@ def main() -> None:
         step = DecodeStep(ctx, E2BShape(layers=a.layers, vocab=16384), batch=a.batch)
         for _ in range(a.reps):
             step.run()
+    elif a.kernel == "downs":
+        from q4k.decode import DecodeStep, E2BShape
+
+        step = DecodeStep(ctx, E2BShape(vocab=256), batch=1)
+        step.run()  # gate/up outputs for the stage below
+        p = step.plan(stages=(1,))
+        for _ in range(a.reps):
+            p.run()
     elif a.kernel == "ple":
         vocab, layers, T = 262144, 35, a.batch
         gen = torch.Generator(device=dev).manual_seed(7)
