@@ -75,6 +75,7 @@ int run_gemv(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
       // one K quarter each, as plans do for such stages
       const uint32_t nb = N / Q4K_QK;
       tl.ksplit = (b <= 4 && nb >= 16 && nb % 4 == 0) ? 4u : 0u;
+      tl.pairs = pairs_of(N, tl.ksplit, tile_bytes) ? 1u : 0u;
       e = launch_engine(tl, map, b, false, ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemv engine launch");
     } else {
@@ -289,6 +290,7 @@ int q4k_lmhead_select(q4k_ctx* ctx, const void* w, const float* x, uint32_t V, u
   tl.inl.tile_bytes = tile_bytes;
   tl.total_items = tiles_of(V);
   tl.total_cost = tiles_of(V) * (N / Q4K_QK);
+  tl.pairs = pairs_of(N, 0, tile_bytes) ? 1u : 0u;
   return ctx_cuda(ctx, launch_engine(tl, map, 1, true, ctx->select, ctx->sm_count, s), "q4k_lmhead_select launch");
 }
 

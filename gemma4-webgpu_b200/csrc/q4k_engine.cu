@@ -513,7 +513,7 @@ __device__ __forceinline__ Hot<NT> hot_of(const TaskList& tl, const TaskSrc& ts,
 // XS = 1: a launch that prepares its activations in the engine (tl.prep), so
 // every task's activation sits in the CTA's shared-memory cache and the math
 // loop has only the shared-memory path.
-template <int NT, int COLS, int KS, int FMT, int XS>
+template <int NT, int COLS, int KS, int FMT, int XS, int PR>
 __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     engine_kernel(const TaskList tl, const __grid_constant__ CUtensorMap wmap,
                   const __grid_constant__ CUtensorMap dmap, uint32_t batch, int has_select, SelectScratch sel,
@@ -730,8 +730,9 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       }
       ++b;
     } else {
-    const uint32_t nblk = min(Pipe<FMT>::kBlocks, b_hi - b);
-    const uint32_t rs = H.tile_bytes;
+    // PR: both super-blocks of every stage, tile rows kPairTileBytes apart
+    const uint32_t nblk = PR ? Pipe<FMT>::kBlocks : min(Pipe<FMT>::kBlocks, b_hi - b);
+    const uint32_t rs = PR ? kPairTileBytes : H.tile_bytes;
     // both super-blocks of a stage in one unrolled body, so the second
     // block's shared-memory loads can be scheduled under the first one's math
 #pragma unroll
@@ -999,7 +1000,7 @@ size_t xcache_bytes(int hs) {
          (hs ? kSelectSmem : kPartSmem);
 }
 
-template <int NT, int COLS, int KS, int FMT, int XS>
+template <int NT, int COLS, int KS, int FMT, int XS, int PR>
 cudaError_t launch_xs(const TaskList& tasks, const CUtensorMap& map, const CUtensorMap& dmap, uint32_t batch,
                            int hs, const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
   const size_t xcap = xcache_bytes<FMT>(hs);
@@ -1008,7 +1009,7 @@ cudaError_t launch_xs(const TaskList& tasks, const CUtensorMap& map, const CUten
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS, FMT, XS>,
+    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS, FMT, XS, PR>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)(kSmemLimit - kStaticSmemHeadroom));
     if (e != cudaSuccess) return e;
@@ -1024,15 +1025,20 @@ cudaError_t launch_xs(const TaskList& tasks, const CUtensorMap& map, const CUten
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, engine_kernel<NT, COLS, KS, FMT, XS>, tasks, map, dmap, batch, hs, sel,
+  return cudaLaunchKernelEx(&cfg, engine_kernel<NT, COLS, KS, FMT, XS, PR>, tasks, map, dmap, batch, hs, sel,
                             (uint32_t)xcap);
 }
 
 template <int NT, int COLS, int KS = 1, int FMT = kFmtQ4K>
 cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, const CUtensorMap& dmap, uint32_t batch,
                            int hs, const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
-  return tasks.prep ? launch_xs<NT, COLS, KS, FMT, 1>(tasks, map, dmap, batch, hs, sel, grid, s)
-                    : launch_xs<NT, COLS, KS, FMT, 0>(tasks, map, dmap, batch, hs, sel, grid, s);
+  if constexpr (FMT == kFmtQ4K) {
+    if (tasks.pairs)
+      return tasks.prep ? launch_xs<NT, COLS, KS, FMT, 1, 1>(tasks, map, dmap, batch, hs, sel, grid, s)
+                        : launch_xs<NT, COLS, KS, FMT, 0, 1>(tasks, map, dmap, batch, hs, sel, grid, s);
+  }
+  return tasks.prep ? launch_xs<NT, COLS, KS, FMT, 1, 0>(tasks, map, dmap, batch, hs, sel, grid, s)
+                    : launch_xs<NT, COLS, KS, FMT, 0, 0>(tasks, map, dmap, batch, hs, sel, grid, s);
 }
 
 }  // namespace

@@ -120,8 +120,23 @@ struct TaskList {
   uint32_t ksplit;      // > 1: KS warps share each tile, one K slice each (plain tasks, batch <= 4,
                         // every task's N/256 a multiple of KS; Q4_K only)
   uint32_t fmt;         // WeightFormat of every task
+  uint32_t pairs;       // 1: every warp's super-block range has an even length and every tile row
+                        // is kPairTileBytes (Q4_K only; see pairs_of)
   Exchange xc;          // LM-head candidate exchange across ranks (xc.world > 0)
 };
+
+// Bytes per tile row of a two-super-block Q4_K stage (the box of
+// encode_weight_map: 2 x 144 bytes + 16).
+constexpr uint32_t kPairTileBytes = 304;
+
+// Whether a Q4_K task of N columns, split over ks warps (0 or 1: no split),
+// always fills both super-blocks of its stages from tile rows of
+// kPairTileBytes: launches whose tasks all do run a kernel with the
+// per-stage block count and row pitch fixed at compile time.
+__host__ __device__ inline bool pairs_of(uint32_t N, uint32_t ks, uint32_t tile_bytes) {
+  const uint32_t nb = N >> 8, k = ks > 1 ? ks : 1u;
+  return nb % k == 0 && (nb / k) % 2 == 0 && tile_bytes == kPairTileBytes;
+}
 
 struct JobList {
   const XJob* dev;

@@ -127,6 +127,7 @@ int q4k_lmhead_select_sharded(q4k_ctx* ctx, q4k_exchange* ex, const void* w, con
   tl.inl.tile_bytes = tile_bytes;
   tl.total_items = tiles_of(V);
   tl.total_cost = tiles_of(V) * item_cost(N, kTaskSelect);
+  tl.pairs = pairs_of(N, 0, tile_bytes) ? 1u : 0u;
   for (uint32_t p = 0; p < ex->world; ++p) tl.xc.peer[p] = ex->peer[p];
   tl.xc.epoch = ex->mailbox + kMaxRanks * kSlotWords;
   tl.xc.rank = ex->rank;

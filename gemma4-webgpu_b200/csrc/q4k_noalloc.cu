@@ -115,6 +115,7 @@ extern "C" int q4k_lmhead_select_static(const void* w, const float* x, uint32_t 
   tl.inl.tile_bytes = tile_bytes;
   tl.total_items = tiles_of(V);
   tl.total_cost = tiles_of(V) * (N / Q4K_QK);
+  tl.pairs = pairs_of(N, 0, tile_bytes) ? 1u : 0u;
   if (launch_engine(tl, map, 1, true, sel, sms, s) != cudaSuccess) return Q4K_ERR_CUDA;
   return Q4K_OK;
 }

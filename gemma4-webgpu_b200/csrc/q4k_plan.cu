@@ -62,6 +62,7 @@ struct Stage {
   bool prep = false;  // activations prepared inside the engine launch (no preparation launch)
   uint32_t ksplit = 0;  // warps sharing each tile (long rows only; see TaskList::ksplit)
   uint32_t fmt = kFmtQ4K;  // after commit: the weight format of every task of this launch unit
+  bool pairs = false;      // after commit: every task fills both super-blocks of its stages (TaskList::pairs)
 };
 
 // Commit splits each recorded stage into launch units of one weight format
@@ -360,6 +361,8 @@ int q4k_plan_commit(q4k_plan* p) {
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit weight tensor map");
       t.tmap = st.maps_dev + mpt * i;
     }
+    st.pairs = st.fmt == kFmtQ4K && st.n_tasks > 0;
+    for (const EngineTask& t : tasks[s]) st.pairs = st.pairs && pairs_of(t.N, st.ksplit, t.tile_bytes);
     if (st.n_tasks) {
       e = cudaMemcpy(st.maps_dev, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
@@ -433,6 +436,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
       tl.prep = st.prep ? 1u : 0u;
       tl.ksplit = st.ksplit;
       tl.fmt = st.fmt;
+      tl.pairs = st.pairs ? 1u : 0u;
       cudaError_t e = launch_engine(tl, kNoMap, p->batch, !st.selects.empty(), ctx->select, ctx->sm_count, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run engine launch");
     }
