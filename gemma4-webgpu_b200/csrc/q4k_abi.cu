@@ -180,6 +180,14 @@ int q4k_gemm(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, 
   return run_gemm(ctx, static_cast<const uint8_t*>(w), x, y, M, N, T, static_cast<cudaStream_t>(stream));
 }
 
+int q4k_gemm_f16x(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
+                  void* stream) {
+  int rc = check_matmul(ctx, w, x, y, M, N, T);
+  if (rc != Q4K_OK) return rc;
+  if (M == 0) return Q4K_OK;
+  return run_gemm(ctx, static_cast<const uint8_t*>(w), x, y, M, N, T, static_cast<cudaStream_t>(stream), 1u);
+}
+
 int q4k_matmul_quant(q4k_ctx* ctx, const float* input, const void* weight, float* output, uint32_t M, uint32_t N,
                      void* stream) {
   return q4k_gemv(ctx, weight, input, output, M, N, 1, stream);

@@ -57,8 +57,10 @@ inline uint32_t tiles_of(uint32_t M) { return (M + kTileRows - 1) / kTileRows; }
 constexpr uint32_t kGemmMinRows = 64;
 
 // Batched Q4_K GEMM (tcgen05, q4k_gemm.cu): y[t][m] = sum_k w16[m][k] x[t][k]
-// for T activation rows, on the context's scratch.
+// for T activation rows, on the context's scratch.  parts = 2: x enters as
+// exact f16 hi + lo parts; parts = 1: x rounded once to f16 (after its
+// power-of-two row scale), half the tensor-core work.
 int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
-             cudaStream_t s);
+             cudaStream_t s, uint32_t parts = 2);
 
 }  // namespace q4k

@@ -123,7 +123,9 @@ struct GemmArgs {
   float* y;                // [T][M]
   const float* inv_scale;  // [T]: 1/scale of each activation row
   uint32_t M, N, T;
-  uint32_t tile_tokens;    // activation rows per CTA tile (64 or 128; the B map's box is 2x that)
+  uint32_t tile_tokens;    // activation rows per CTA tile (parts x tile_tokens = 128 or 256 operand rows,
+                           // the B map's box)
+  uint32_t parts;          // operand rows per activation row: 2 (exact f16 hi + lo) or 1 (f16 only)
   uint32_t* status;        // bit 0: a bounded wait expired
 };
 
@@ -177,8 +179,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t row0 = blockIdx.x * kGRows, tok0 = blockIdx.y * a.tile_tokens;
   const uint32_t ntok = min(a.tile_tokens, a.T - tok0);
-  const uint32_t b_bytes = 2 * a.tile_tokens * kGK * 2;  // one B box
-  const uint32_t n_mma = 2u * ((ntok + 7u) & ~7u);
+  const uint32_t b_bytes = a.parts * a.tile_tokens * kGK * 2;  // one B box
+  // MMA N: the tile's operand rows, a multiple of 16
+  const uint32_t n_mma = a.parts == 2 ? 2u * ((ntok + 7u) & ~7u) : ((ntok + 15u) & ~15u);
   const uint32_t ksteps = a.N / kGK;
   bool failed = false;
 
@@ -207,7 +210,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   const uint32_t tmem = s_tmem;
 
   if (warp == 0) {
-    // B producer: one TMA box (2 x tile_tokens operand rows x 64 halves) per stage
+    // B producer: one TMA box (parts x tile_tokens operand rows x 64 halves) per stage
     if (lane == 0) {
       uint32_t issued = 0;
       for (uint32_t ks = 0; ks < ksteps; ++ks) {
@@ -217,7 +220,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
           break;
         }
         mbar_arrive_expect_tx(&full_b[s], b_bytes);
-        tma_tile_g2s(sB + s * kGBBytes, &bmap, ks * kGK, 2 * tok0, &full_b[s]);
+        tma_tile_g2s(sB + s * kGBBytes, &bmap, ks * kGK, a.parts * tok0, &full_b[s]);
         ++issued;
       }
       // every issued copy has landed before the CTA can exit
@@ -297,10 +300,18 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       for (uint32_t c0 = 0; c0 < n_mma; c0 += 32) {
         float v[32];
         tmem_ld32(tmem + ((32u * q) << 16) + hb * kGAccCols + c0, v);
+        if (a.parts == 2) {
 #pragma unroll
-        for (uint32_t t = 0; t < 16; ++t) {
-          const uint32_t tok = tok0 + c0 / 2 + t;
-          if (tok < a.T && erow < a.M) a.y[(size_t)tok * a.M + erow] = (v[2 * t] + v[2 * t + 1]) * a.inv_scale[tok];
+          for (uint32_t t = 0; t < 16; ++t) {
+            const uint32_t tok = tok0 + c0 / 2 + t;
+            if (tok < a.T && erow < a.M) a.y[(size_t)tok * a.M + erow] = (v[2 * t] + v[2 * t + 1]) * a.inv_scale[tok];
+          }
+        } else {
+#pragma unroll
+          for (uint32_t t = 0; t < 32; ++t) {
+            const uint32_t tok = tok0 + c0 + t;
+            if (tok < a.T && erow < a.M) a.y[(size_t)tok * a.M + erow] = v[t] * a.inv_scale[tok];
+          }
         }
       }
     }
@@ -334,10 +345,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   }
 }
 
-// x [T][N] f32 -> B operand [2T][N] f16: row 2t = hi(x_t * s_t), row 2t+1 =
-// lo = x_t*s_t - hi, s_t a power of two with max|x_t| * s_t < 2^15, each
-// 8-element chunk in the A tiles' K order (chunk_elem).
-__global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* x, __half* b, float* inv_scale, uint32_t N) {
+// x [T][N] f32 -> B operand [parts*T][N] f16: row parts*t = hi(x_t * s_t)
+// and, for parts = 2, row 2t+1 = lo = x_t*s_t - hi; s_t a power of two with
+// max|x_t| * s_t < 2^15, each 8-element chunk in the A tiles' K order
+// (chunk_elem).
+__global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* x, __half* b, float* inv_scale, uint32_t N,
+                                                         uint32_t parts) {
   __shared__ float s_red[8];
   const uint32_t t = blockIdx.x;
   const float* xr = x + (size_t)t * N;
@@ -356,13 +369,13 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* x, __half*
   }
   const float s = ldexpf(1.0f, sexp);
   if (threadIdx.x == 0) inv_scale[t] = ldexpf(1.0f, -sexp);
-  __half* hi = b + (size_t)(2 * t) * N;
+  __half* hi = b + (size_t)(parts * t) * N;
   __half* lo = hi + N;
   for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) {
     const float v = xr[(k & ~7u) | chunk_elem(k & 7u)] * s;  // the A tiles' K order
     const __half hv = __float2half_rn(v);
     hi[k] = hv;
-    lo[k] = __float2half_rn(v - __half2float(hv));
+    if (parts == 2) lo[k] = __float2half_rn(v - __half2float(hv));
   }
 }
 
@@ -383,7 +396,8 @@ EncodeTiledFn gemm_encode_fn() {
 }  // namespace
 
 int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
-             cudaStream_t s) {
+             cudaStream_t s, uint32_t parts) {
+  if (parts != 1 && parts != 2) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "parts=%u must be 1 or 2", parts);
   EncodeTiledFn enc = gemm_encode_fn();
   if (!enc) return ctx_fail(ctx, Q4K_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   static int attr_dev = -1;
@@ -414,19 +428,21 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
   }
   for (uint32_t done = 0; done < T;) {
     const uint32_t tc = (T - done) < cap ? (T - done) : cap;
-    gemm_xprep_kernel<<<tc, 256, 0, s>>>(x + (size_t)done * N, bbuf, ctx->inv_scale, N);
+    gemm_xprep_kernel<<<tc, 256, 0, s>>>(x + (size_t)done * N, bbuf, ctx->inv_scale, N, parts);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm activation prep launch");
-    // 64-row activation tiles when 128-row ones leave SMs idle and the
-    // smaller tiles still fit in one wave
+    // tiles of 256 operand rows (kGTokens x 2 / parts activation rows), or
+    // half that when the full ones leave SMs idle and the smaller tiles
+    // still fit in one wave
     const uint32_t row_tiles = (M + kGRows - 1) / kGRows;
     const uint32_t sms = (uint32_t)ctx->sm_count;
-    const uint32_t tile = (row_tiles * ((tc + kGTokens - 1) / kGTokens) < sms && row_tiles * ((tc + 63) / 64) <= sms)
-                              ? 64u : kGTokens;
+    const uint32_t full = 2 * kGTokens / parts, half = full / 2;
+    const uint32_t tile =
+        (row_tiles * ((tc + full - 1) / full) < sms && row_tiles * ((tc + half - 1) / half) <= sms) ? half : full;
     CUtensorMap bmap;
-    const cuuint64_t dims[2] = {N, 2ull * tc};
+    const cuuint64_t dims[2] = {N, (cuuint64_t)parts * tc};
     const cuuint64_t strides[1] = {2ull * N};
-    const cuuint32_t box[2] = {kGK, 2 * tile};
+    const cuuint32_t box[2] = {kGK, parts * tile};
     const cuuint32_t estr[2] = {1, 1};
     if (enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bbuf, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -440,6 +456,7 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     ga.N = N;
     ga.T = tc;
     ga.tile_tokens = tile;
+    ga.parts = parts;
     ga.status = ctx->select.status;
     const dim3 grid((M + kGRows - 1) / kGRows, (tc + ga.tile_tokens - 1) / ga.tile_tokens);
     gemm_kernel<<<grid, kGThreads, kGSmem, s>>>(bmap, amap, ga);

@@ -30,6 +30,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_matmul_quant": ([_P, _P, _P, _P, _U32, _U32, _P], _I),
     "q4k_gemv": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
     "q4k_gemm": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
+    "q4k_gemm_f16x": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
     "q4k_dequant_f16": ([_P, _P, _P, _U64, _P], _I),
     "q4k_logit_softcap": ([_P, _P, _U32, _F, _P], _I),
     "q4k_argmax": ([_P, _P, _U32, _P, _P], _I),

@@ -292,14 +292,16 @@ class BatchedSweep:
     (prefill, or T independent sequences sharing the weights), without the
     LM head.  T <= 16 runs as a two-stage Plan on the GEMV engine (one weight
     stream per matrix for all T rows); T >= 64 runs each matrix through the
-    tcgen05 GEMM (q4k_gemm via Context.gemv), with gelu_mul between up and
+    tcgen05 GEMM (q4k_gemm via Context.gemm), with gelu_mul between up and
     down as in src/engine.ts:1589-1605.  The layers are independent, so the
     GEMM path spreads them over `streams` CUDA streams (one library context
     each: a GEMM call prepares its activation operand in its context's
-    scratch), letting the launches of small matrices share the SMs."""
+    scratch), letting the launches of small matrices share the SMs.  f16x
+    (T >= 64 only): activations rounded once to f16 in the GEMM
+    (q4k_gemm_f16x, the 2e-3 prefill tolerance) instead of exact hi + lo."""
 
-    def __init__(self, step: DecodeStep, T: int, streams: int = 8):
-        self.step, self.T = step, T
+    def __init__(self, step: DecodeStep, T: int, streams: int = 8, f16x: bool = False):
+        self.step, self.T, self.f16x = step, T, f16x
         ctx, s = step.ctx, step.shape
         dev = ctx.device
         shapes = layer_shapes(s)
@@ -332,10 +334,10 @@ class BatchedSweep:
         for name in ("q", "k", "v", "o", "gate", "up"):
             M, N = shapes[name]
             x = self.x_attn if name == "o" else self.x_h
-            c.gemv(W[(layer, name)], x, M, N, out=O[(layer, name)], stream=stream)
+            c.gemm(W[(layer, name)], x, M, N, out=O[(layer, name)], stream=stream, f16x=self.f16x)
         c.gelu_mul(O[(layer, "gate")], O[(layer, "up")], out=self.act[layer], stream=stream)
         M, N = shapes["down"]
-        c.gemv(W[(layer, "down")], self.act[layer], M, N, out=O[(layer, "down")], stream=stream)
+        c.gemm(W[(layer, "down")], self.act[layer], M, N, out=O[(layer, "down")], stream=stream, f16x=self.f16x)
 
     def run(self, stream: torch.cuda.Stream | None = None) -> None:
         if self.plan is not None:

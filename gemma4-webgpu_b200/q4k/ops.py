@@ -136,9 +136,11 @@ class Context:
         return out
 
     def gemm(self, weight: torch.Tensor, x: torch.Tensor, M: int, N: int, out: torch.Tensor | None = None,
-             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+             stream: torch.cuda.Stream | None = None, f16x: bool = False) -> torch.Tensor:
         """y[t, m] for x [T, N] on the tensor cores (q4k_gemm): the batched
-        prefill form of matmul_quant for many activation rows."""
+        prefill form of matmul_quant for many activation rows.  f16x: each
+        activation row rounded once to f16 (q4k_gemm_f16x, half the
+        tensor-core work, 2e-3 relative tolerance) instead of exact hi + lo."""
         _need(weight, torch.uint8, "weight", self.device)
         _need(x, torch.float32, "x", self.device)
         if x.numel() % N:
@@ -151,7 +153,8 @@ class Context:
         _need(out, torch.float32, "out", self.device)
         if out.numel() < T * M:
             raise ValueError("out smaller than T*M")
-        self._check(self._L.q4k_gemm(self._h, _ptr(weight), _ptr(x), _ptr(out), M, N, T, _stream(stream)))
+        fn = self._L.q4k_gemm_f16x if f16x else self._L.q4k_gemm
+        self._check(fn(self._h, _ptr(weight), _ptr(x), _ptr(out), M, N, T, _stream(stream)))
         return out
 
     def dequant_f16(self, weight: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:

@@ -3,7 +3,7 @@
     python gemma4-webgpu_b200/q4k/profile_case.py gemv [--batch B] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py lmhead [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py sweep [--layers L] [--reps R]
-    python gemma4-webgpu_b200/q4k/profile_case.py gemm [--batch T] [--reps R]
+    python gemma4-webgpu_b200/q4k/profile_case.py gemm [--batch T] [--reps R] [--f16x]
     python gemma4-webgpu_b200/q4k/profile_case.py q6head [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py ple [--batch T] [--reps R]
     python gemma4-webgpu_b200/q4k/profile_case.py downs [--reps R]
@@ -40,6 +40,7 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=40)
+    ap.add_argument("--f16x", action="store_true", help="gemm: activations rounded to f16 (q4k_gemm_f16x)")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     ctx = Context(0)
@@ -57,7 +58,7 @@ def main() -> None:
         x = torch.from_numpy(synth.activations(T, N, 2)).to(dev)
         y = torch.empty((T, M), dtype=torch.float32, device=dev)
         for _ in range(a.reps):
-            ctx.gemm(w, x, M, N, out=y)
+            ctx.gemm(w, x, M, N, out=y, f16x=a.f16x)
     elif a.kernel == "sweep":
         from q4k.decode import DecodeStep, E2BShape
 

@@ -105,6 +105,18 @@ Q4K_API int q4k_gemv(q4k_ctx* ctx, const void* w, const float* x, float* y, uint
 Q4K_API int q4k_gemm(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
                      void* stream);
 
+/* q4k_gemm with each activation row rounded once to f16 (after a
+ * power-of-two row scale that keeps it in range) instead of entering as
+ * exact f16 hi + lo parts: half the tensor-core work and operand traffic,
+ * for prefill and batched sequences where the relative tolerance of 2e-3
+ * applies (the weights are still the reference's f16 values exactly; the
+ * product error is that of an f16 activation, ~3e-4 relative in L2).
+ * Replaces the same per-row matmul_quant passes as q4k_gemm
+ * (shaders/matmul_quant.wgsl:21-54, run per prompt token by
+ * src/engine.ts:1932-1934).  Any T >= 1. */
+Q4K_API int q4k_gemm_f16x(q4k_ctx* ctx, const void* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
+                          void* stream);
+
 /* The f16 weights the reference uploads for a Q4_K tensor (its
  * dequantizeQ4_K + f32ToF16Array + createF16Buffer, src/gguf.ts:168-210,
  * 425-473, src/engine.ts:553-578, 828-841): n_blocks super-blocks ->

@@ -4,6 +4,11 @@ Same tolerance as the GEMV (per output 1e-3*|y_ref| + 1e-6*||w_row||*||x||,
 L2 relative 1e-4): the weights are the reference's f16 values exactly and x
 enters the tensor core split into exact f16 hi + lo parts, so only the fp32
 accumulation order differs from the oracle's.
+
+q4k_gemm_f16x rounds each scaled activation row once to f16.  Against the
+oracle on the f32 activations it meets the prefill tolerance (L2 relative
+2e-3; per output 2e-3*|y_ref| + 1e-4*||w_row||*||x||); against the oracle
+on the same f16-rounded activations it meets the GEMV tolerance above.
 """
 from __future__ import annotations
 
@@ -40,6 +45,40 @@ def test_gemm_shapes(ctx, oracle, M, N, T):
     x = synth.activations(T, N, synth.seed_for(4, 700 + T))
     y = ctx.gemm(to_dev(w), to_dev(x), M, N).cpu().numpy()
     check(oracle, y, w, x, M, N)
+
+
+def f16_rounded(x: np.ndarray) -> np.ndarray:
+    """Each row of x scaled by the GEMM's power of two (max|x_t| * s < 2^15),
+    rounded to f16 and scaled back: the activations q4k_gemm_f16x multiplies."""
+    out = np.empty_like(x)
+    for t in range(x.shape[0]):
+        mx = float(np.max(np.abs(x[t])))
+        sexp = 0
+        if mx > 0.0:
+            sexp = int(np.clip(15 - np.frexp(mx)[1], -100, 100))
+        s = np.float32(2.0 ** sexp)
+        out[t] = (x[t] * s).astype(np.float16).astype(np.float32) / s
+    return out
+
+
+@pytest.mark.parametrize("M,N,T", [
+    (256, 1536, 64), (300, 768, 100), (2048, 1536, 256), (1536, 2048, 257), (130, 6144, 65),
+    (1024, 1536, 512), (64, 512, 1), (200, 1024, 17), (6144, 1536, 600),
+])
+def test_gemm_f16x_shapes(ctx, oracle, M, N, T):
+    w = synth.q4k_matrix(M, N, synth.seed_for(4, M + N + 1))
+    x = synth.activations(T, N, synth.seed_for(4, 900 + T))
+    y = ctx.gemm(to_dev(w), to_dev(x), M, N, f16x=True).cpu().numpy()
+    # exactly the f16-rounded activations, up to accumulation order
+    check(oracle, y, w, f16_rounded(x), M, N)
+    # and within the prefill tolerance of the f32 activations
+    y_ref = oracle.q4k_gemv(w, x, M, N)
+    _, wn = oracle.q4k_gemv_f64(w, x, M, N)
+    y = y.reshape(y_ref.shape)
+    l2 = float(np.linalg.norm(y - y_ref) / np.linalg.norm(y_ref))
+    assert l2 <= 2e-3, f"L2 relative {l2:.3g}"
+    bound = 2e-3 * np.abs(y_ref) + 1e-4 * wn[None, :] * np.linalg.norm(x, axis=1)[:, None]
+    assert np.all(np.abs(y - y_ref) <= bound)
 
 
 def test_gemv_hands_large_batches_to_the_gemm(ctx, oracle):
@@ -84,6 +123,23 @@ def test_batched_sweep_streams_match_single_calls(ctx):
         for name, (M, N) in shapes.items():
             x = bs.act[layer] if name == "down" else (bs.x_attn if name == "o" else bs.x_h)
             ref = ctx.gemm(step.weights[(layer, name)], x, M, N)
+            torch.cuda.synchronize()
+            assert torch.equal(ref.view(torch.int32), bs.out[(layer, name)].view(torch.int32)), (layer, name)
+    bs.close()
+
+
+def test_batched_sweep_f16x_matches_single_calls(ctx):
+    from q4k.decode import BatchedSweep, DecodeStep, E2BShape, layer_shapes
+
+    step = DecodeStep(ctx, E2BShape(layers=2, vocab=1024))
+    bs = BatchedSweep(step, 300, streams=2, f16x=True)
+    bs.run()
+    torch.cuda.synchronize()
+    shapes = layer_shapes(step.shape)
+    for layer in range(2):
+        for name, (M, N) in shapes.items():
+            x = bs.act[layer] if name == "down" else (bs.x_attn if name == "o" else bs.x_h)
+            ref = ctx.gemm(step.weights[(layer, name)], x, M, N, f16x=True)
             torch.cuda.synchronize()
             assert torch.equal(ref.view(torch.int32), bs.out[(layer, name)].view(torch.int32)), (layer, name)
     bs.close()
