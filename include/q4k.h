@@ -110,7 +110,7 @@ Q4K_API int q4k_gemm(q4k_ctx* ctx, const void* w, const float* x, float* y, uint
  * exact f16 hi + lo parts: half the tensor-core work and operand traffic,
  * for prefill and batched sequences where the relative tolerance of 2e-3
  * applies (the weights are still the reference's f16 values exactly; the
- * product error is that of an f16 activation, ~3e-4 relative in L2).
+ * product error is that of an f16 activation, ~2e-4 relative in L2).
  * Replaces the same per-row matmul_quant passes as q4k_gemm
  * (shaders/matmul_quant.wgsl:21-54, run per prompt token by
  * src/engine.ts:1932-1934).  Any T >= 1. */
