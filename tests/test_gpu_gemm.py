@@ -38,7 +38,7 @@ def check(oracle, y, w, x, M, N):
 
 @pytest.mark.parametrize("M,N,T", [
     (128, 256, 64), (256, 1536, 64), (300, 768, 100), (2048, 1536, 128), (1536, 2048, 200),
-    (130, 6144, 65), (1024, 1536, 512), (64, 512, 1), (200, 1024, 17),
+    (130, 6144, 65), (1024, 1536, 512), (64, 512, 1), (200, 1024, 17), (6144, 1536, 512),
 ])
 def test_gemm_shapes(ctx, oracle, M, N, T):
     w = synth.q4k_matrix(M, N, synth.seed_for(4, M + N))
