@@ -432,13 +432,17 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm activation prep launch");
     // tiles of 256 operand rows (kGTokens x 2 / parts activation rows), or
-    // half that when the full ones leave SMs idle and the smaller tiles
-    // still fit in one wave
+    // half that when the full ones would fill at most a quarter of the SMs
+    // and the smaller tiles still fit in one wave.  Every activation tile
+    // reconstructs its rows' weights again, so larger tiles do less work in
+    // total; with several matrices in flight on other streams (config 4)
+    // that outweighs the idle SMs of a single call.
     const uint32_t row_tiles = (M + kGRows - 1) / kGRows;
     const uint32_t sms = (uint32_t)ctx->sm_count;
     const uint32_t full = 2 * kGTokens / parts, half = full / 2;
     const uint32_t tile =
-        (row_tiles * ((tc + full - 1) / full) < sms && row_tiles * ((tc + half - 1) / half) <= sms) ? half : full;
+        (row_tiles * ((tc + full - 1) / full) * 4 <= sms && row_tiles * ((tc + half - 1) / half) <= sms) ? half
+                                                                                                        : full;
     CUtensorMap bmap;
     const cuuint64_t dims[2] = {N, (cuuint64_t)parts * tc};
     const cuuint64_t strides[1] = {2ull * N};
