@@ -283,7 +283,7 @@ def run_ours(args) -> None:
             t_ms, t_graph = time_body(bs.run, max(5, min(reps, 2000 // T)))
             t_ms = max_over_ranks(t_ms, world, dev)  # each rank runs its own T rows (data parallel)
             tf = world * bs.flops() / (t_ms / 1e3) / 1e12
-            path = "GEMV engine plan" if T <= 16 else "tcgen05 GEMM per matrix, 8 streams"
+            path = "GEMV engine plan" if T <= 16 else "tcgen05 GEMM per matrix, 18 streams"
             if f16x:
                 path += ", activations rounded to f16 (tolerance 2e-3)"
             batched[f"T={T}" + (" f16x" if f16x else "")] = {

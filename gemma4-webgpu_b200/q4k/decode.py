@@ -300,7 +300,7 @@ class BatchedSweep:
     (T >= 64 only): activations rounded once to f16 in the GEMM
     (q4k_gemm_f16x, the 2e-3 prefill tolerance) instead of exact hi + lo."""
 
-    def __init__(self, step: DecodeStep, T: int, streams: int = 8, f16x: bool = False):
+    def __init__(self, step: DecodeStep, T: int, streams: int = 18, f16x: bool = False):
         self.step, self.T, self.f16x = step, T, f16x
         ctx, s = step.ctx, step.shape
         dev = ctx.device
