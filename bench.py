@@ -8,6 +8,7 @@ as a CUDA graph and replayed once per step.  923 MB of Q4_K weights per step,
 more than the 126 MB L2, so every step streams the weights from HBM.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+    python bench.py --case {gemv,lmhead,sweep,gemm,q6head,ple,downs} [--reps R] ...   (profiler cases)
 
 N > 1 (torchrun, one rank per GPU): every rank runs its own replica of the
 step (independent sequences, no collective on the data path: the M=1 sweep
@@ -151,10 +152,15 @@ def barrier(world: int):
 
 # ---- CPU baseline (oracle port) -----------------------------------------------------
 
-def cpu_sample_rate(mats, target_s: float, threads: int):
-    """Time the oracle's fused Q4_K GEMV (decode + RNE f16 + WGSL-order dot)
-    over the sample matrices, repeating until target_s; returns
-    (GB/s of algorithmic bytes, seconds, bytes, passes)."""
+def cpu_sample_rate(mats, target_s: float, threads: int, variant: str = "fused"):
+    """Time the oracle on the sample matrices, repeating until target_s.
+    variant "fused": the Q4_K GEMV with the decode in every call (Q4_K decode
+    + RNE f16 + WGSL-order f32 dot); "f16": the reference's per-token work,
+    the matmul_quant GEMV over weights dequantized to f16 beforehand (the
+    reference decodes once at load, src/gguf.ts:157-210, 425-473, and its
+    shaders/matmul_quant.wgsl:21-54 reads the f16 buffer; the decode is not
+    timed).  Returns (GB/s of the sample's algorithmic bytes -- Q4_K weight
+    bytes + f32 I/O, the unit of the GPU figure --, seconds, bytes, passes)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import numpy as np
     import oracle as O
@@ -165,15 +171,40 @@ def cpu_sample_rate(mats, target_s: float, threads: int):
         if N not in xs:
             xs[N] = np.random.default_rng(N).standard_normal((1, N), dtype=np.float32)
         total_bytes += w.nbytes + 4 * (M + N)
+    if variant == "f16":
+        w16 = [O.dequant_f16(w) for w, _, _ in mats]
+
+        def one_pass():
+            for (_, M, N), w in zip(mats, w16):
+                O.matmul_quant_f16(w, xs[N], M, N, threads=threads)
+    else:
+        def one_pass():
+            for w, M, N in mats:
+                O.q4k_gemv(w, xs[N], M, N, threads=threads)
     passes, t0 = 0, time.perf_counter()
     while True:
-        for w, M, N in mats:
-            O.q4k_gemv(w, xs[N], M, N, threads=threads)
+        one_pass()
         passes += 1
         el = time.perf_counter() - t0
         if el >= target_s:
             break
     return passes * total_bytes / el / 1e9, el, total_bytes, passes
+
+
+def cpu_baseline_variants(mats, seconds: float, bytes_step: int) -> dict:
+    """The CPU restatement on the host cores in both forms (fused decode +
+    GEMV, and the GEMV over pre-dequantized f16 weights) on 1 core and on all
+    cores, seconds/4 each; GB/s of algorithmic bytes and the decode
+    tokens/s each rate would give on the full step."""
+    cores = os.cpu_count() or 1
+    out = {}
+    for variant in ("fused", "f16"):
+        for threads in (1, cores):
+            gbs, el, nbytes, passes = cpu_sample_rate(mats, seconds / 4, threads, variant)
+            out[f"{variant}_{threads}core" + ("s" if threads > 1 else "")] = {
+                "GB/s": round(gbs, 3), "cores": threads, "seconds": round(el, 2), "passes": passes,
+                "tokens_per_s_equiv": round(gbs * 1e9 / bytes_step, 3)}
+    return out
 
 
 # ---- our arm ------------------------------------------------------------------------------
@@ -437,11 +468,15 @@ def run_ours(args) -> None:
     if world == 1 and not args.no_cpu:
         mats = step.sample_matrices(layers=1)
         threads = os.cpu_count() or 1
-        gbs, el, nbytes, passes = cpu_sample_rate(mats, args.cpu_seconds, threads)
-        cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"layer 0's 7 GEMVs ({nbytes / 1e6:.1f} MB of Q4_K+f32 I/O) x {passes} passes, "
-                         f"{el:.1f} s, fused Q4_K decode + RNE f16 + WGSL-order f32 dot",
-               "tokens_per_s_equiv": round(gbs * 1e9 / bytes_step, 3)}
+        variants = cpu_baseline_variants(mats, args.cpu_seconds, bytes_step)
+        head = variants[f"fused_{threads}core" + ("s" if threads > 1 else "")]
+        nbytes = sum(w.nbytes + 4 * (M + N) for w, M, N in mats)
+        cpu = {"value": head["GB/s"], "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"layer 0's 7 GEMVs ({nbytes / 1e6:.1f} MB of Q4_K+f32 I/O), repeated for "
+                         f"{args.cpu_seconds / 4:.1f} s per variant; value = fused Q4_K decode + RNE f16 + "
+                         f"WGSL-order f32 dot on all {threads} host threads",
+               "tokens_per_s_equiv": head["tokens_per_s_equiv"],
+               "variants": variants}
 
     line = {
         "metric": METRIC,
@@ -483,6 +518,95 @@ def run_ours(args) -> None:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+# ---- profiler cases ---------------------------------------------------------------------------
+
+CASES = ("gemv", "lmhead", "sweep", "gemm", "q6head", "ple", "downs")
+
+
+def run_case(args) -> None:
+    """Small, self-contained launches of one kernel for profiler captures
+    (`--case`), a few hundred MB of device memory at most; the process exits
+    after `--reps` runs and prints nothing that is a bench value.
+
+      gemv    rotates over 35 distinct 6144x1536 Q4_K matrices (186 MB, more than
+              the 126 MB L2, so each launch reads its weights from HBM), --batch rows
+      lmhead  the fused 262144-row LM head (226 MB)
+      sweep   the decode-step plan of q4k.decode with --layers layers (default 8:
+              159 MB of layer weights plus a 16384-row LM head), --batch rows
+      gemm    q4k_gemm on one 6144x1536 matrix with --batch activation rows
+              (default 512; --f16x: q4k_gemm_f16x)
+      q6head  the fused LM head on a 131072x1536 Q6_K matrix in the device layout
+      ple     per-layer-embedding stage 1 for --batch tokens on a 262144 x 35
+              super-block Q5_K table (1.6 GB, made on the device), a new random
+              token each rep
+      downs   the decode step's second plan stage alone (gelu_mul + the 35 down
+              projections 1536x6144, 186 MB, 4 warps per tile)
+    """
+    import torch
+
+    from q4k import Context, synth
+
+    dev = torch.device("cuda", 0)
+    ctx = Context(0)
+    if args.case == "gemv":
+        M, N = 6144, 1536
+        ws = [torch.from_numpy(synth.q4k_matrix(M, N, synth.seed_for(3, 8 * i + 4))).to(dev) for i in range(35)]
+        x = torch.from_numpy(synth.activations(args.batch, N, 1)).to(dev)
+        y = torch.empty((args.batch, M), dtype=torch.float32, device=dev)
+        for r in range(args.reps):
+            ctx.gemv(ws[r % len(ws)], x, M, N, out=y)
+    elif args.case == "gemm":
+        M, N = 6144, 1536
+        w = torch.from_numpy(synth.q4k_matrix(M, N, synth.seed_for(4, 1))).to(dev)
+        T = args.batch if args.batch > 1 else 512
+        x = torch.from_numpy(synth.activations(T, N, 2)).to(dev)
+        y = torch.empty((T, M), dtype=torch.float32, device=dev)
+        for _ in range(args.reps):
+            ctx.gemm(w, x, M, N, out=y, f16x=args.f16x)
+    elif args.case == "sweep":
+        from q4k.decode import DecodeStep, E2BShape
+
+        step = DecodeStep(ctx, E2BShape(layers=args.layers, vocab=16384), batch=args.batch)
+        for _ in range(args.reps):
+            step.run()
+    elif args.case == "downs":
+        from q4k.decode import DecodeStep, E2BShape
+
+        step = DecodeStep(ctx, E2BShape(vocab=256), batch=1)
+        step.run()  # gate/up outputs for the stage below
+        p = step.plan(stages=(1,))
+        for _ in range(args.reps):
+            p.run()
+    elif args.case == "ple":
+        vocab, layers, T = 262144, 35, args.batch
+        gen = torch.Generator(device=dev).manual_seed(7)
+        table = torch.randint(0, 256, (vocab * layers, 176), dtype=torch.uint8, device=dev, generator=gen)
+        table[:, 0:4] = torch.empty((vocab * layers, 2), dtype=torch.float16, device=dev).uniform_(
+            0.0, 4e-3, generator=gen).view(torch.uint8)
+        proj = torch.randn((T, layers * 256), device=dev, generator=gen)
+        norm = torch.ones(256, dtype=torch.float16, device=dev).view(torch.int16)
+        for _ in range(args.reps):
+            tok = torch.randint(0, vocab, (T,), dtype=torch.int32, device=dev, generator=gen)
+            ctx.ple_stage1(table, tok, vocab, layers, proj, norm)
+    elif args.case == "q6head":
+        V, N = 131072, 1536
+        w = ctx.q6k_repack(torch.from_numpy(synth.q6k_matrix(V, N, synth.seed_for(5, 999)).reshape(-1)).to(dev),
+                           V, N)
+        x = torch.from_numpy(synth.activations(1, N, 1)).to(dev)
+        for _ in range(args.reps):
+            ctx.q6k_lmhead_select(w, x[0], V, N, 30.0)
+    else:  # lmhead
+        V, N = 262144, 1536
+        w = torch.from_numpy(synth.q4k_matrix(V, N, synth.seed_for(3, 999))).to(dev)
+        x = torch.from_numpy(synth.activations(1, N, 1)).to(dev)
+        for _ in range(args.reps):
+            ctx.lmhead_select(w, x[0], V, N, 30.0)
+    torch.cuda.synchronize()
+    ctx.check()
+    ctx.close()
+    print(f"case {args.case} done", flush=True)
 
 
 # ---- reference arm --------------------------------------------------------------------------
@@ -546,11 +670,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--batch", type=int, default=1, help="activation rows per step (config 3: 1 or 4)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-seconds", type=float, default=16.0, help="CPU baseline: total seconds over its 4 variants")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-real", action="store_true", help="skip the real-E2B-shape (Q4_K + Q6_K) sweep")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 batched sweeps")
+    ap.add_argument("--case", choices=CASES, default=None,
+                    help="run one kernel's small profiler case instead of the benchmark (see run_case)")
+    ap.add_argument("--reps", type=int, default=40, help="--case: launches to run")
+    ap.add_argument("--layers", type=int, default=8, help="--case sweep: layers of the plan")
+    ap.add_argument("--f16x", action="store_true", help="--case gemm: activations rounded to f16 (q4k_gemm_f16x)")
     args = ap.parse_args()
+    if args.case is not None:
+        run_case(args)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":

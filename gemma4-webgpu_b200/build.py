@@ -12,6 +12,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -59,16 +60,21 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     LIB_DIR.mkdir(exist_ok=True)
     obj_dir = PKG / "_build"
     obj_dir.mkdir(exist_ok=True)
-    objs = []
+    srcs = sources()
+    objs = [str(obj_dir / (src.stem + ".o")) for src in srcs]
+
+    def compile_one(src: Path, obj: str) -> subprocess.CompletedProcess:
+        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", obj]
+        return subprocess.run(cmd, capture_output=True, text=True)
+
+    # one nvcc process per translation unit, in parallel
+    with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as pool:
+        results = list(pool.map(compile_one, srcs, objs))
     log = []
-    for src in sources():
-        obj = obj_dir / (src.stem + ".o")
-        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-dc" if False else "-c", str(src), "-o", str(obj)]
-        r = subprocess.run(cmd, capture_output=True, text=True)
+    for src, r in zip(srcs, results):
         log.append(r.stdout + r.stderr)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
-        objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *objs, "-lcuda"]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -143,6 +143,13 @@ void q4k_destroy(q4k_ctx* ctx) {
 
 const char* q4k_last_error(const q4k_ctx* ctx) { return ctx ? ctx->err : "null context"; }
 
+int q4k_set_wait_limit(q4k_ctx* ctx, uint32_t polls) {
+  if (!ctx) return Q4K_ERR_INVALID_ARG;
+  ctx->select.spin_limit = polls;  // 0: the built-in default
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
 int q4k_check(q4k_ctx* ctx) {
   if (!ctx) return Q4K_ERR_INVALID_ARG;
   cudaError_t e = cudaDeviceSynchronize();
@@ -155,7 +162,8 @@ int q4k_check(q4k_ctx* ctx) {
     cudaMemcpy(ctx->select.status, &zero, sizeof(zero), cudaMemcpyHostToDevice);
     if (status & 1u)
       return ctx_fail(ctx, Q4K_ERR_TIMEOUT,
-                      "a kernel gave up waiting for its weight copies (bounded wait expired); its outputs are invalid");
+                      "a kernel gave up a bounded wait (its weight copies, a K-split partner or a peer rank's "
+                      "candidates did not arrive within the wait limit); its outputs are invalid");
     return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "a token id was >= vocab in q4k_ple_stage1; that token's outputs are NaN");
   }
   ctx->err[0] = 0;

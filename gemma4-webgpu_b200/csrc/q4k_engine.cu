@@ -535,6 +535,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t g = lane >> 2, c = lane & 3u;
+  const uint32_t spin = spin_or_default(sel.spin_limit);  // polls per bounded wait
   // bytes (2(c&1), 2(c&1)+1) of a packed scale word -> bytes 0 and 2
   const uint32_t bsel = scale_sel(c);
   uint8_t* wsm = smem + warp * (kSt * kSB);
@@ -602,7 +603,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   __syncthreads();
   const uint32_t c0 = s_sched.c0, c1 = s_sched.c1;
   bool timed_out = false;
-  if (!mbar_wait(&s_xbar, 0)) timed_out = true;
+  if (!mbar_wait(&s_xbar, 0, spin)) timed_out = true;
   TaskSrc ts;
   ts.table = !tl.dev ? nullptr : (s_sched.nt ? s_tasks : tl.dev);
   ts.t0 = s_sched.nt ? s_sched.t0 : 0u;
@@ -692,7 +693,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
 
   while (item < c1 && !timed_out) {
     const uint32_t slot = k % kSt;
-    if (!mbar_wait(&bars[slot], (k / kSt) & 1u)) {
+    if (!mbar_wait(&bars[slot], (k / kSt) & 1u, spin)) {
       timed_out = true;
       break;
     }
@@ -786,7 +787,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_gbar[grp]);
-      if (!mbar_wait(&s_gbar[grp], par)) {
+      if (!mbar_wait(&s_gbar[grp], par, spin)) {
         timed_out = true;
         break;
       }
@@ -856,7 +857,7 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     // record the failure, then let every copy still in flight land (bounded)
     if (lane == 0) atomicOr(sel.status, 1u);
     if (lane == 0)
-      for (uint32_t j = k; j < s_cur[warp].issued; ++j) mbar_wait(&bars[j % kSt], (j / kSt) & 1u);
+      for (uint32_t j = k; j < s_cur[warp].issued; ++j) mbar_wait(&bars[j % kSt], (j / kSt) & 1u, spin);
   }
 
   if (!has_select) return;
@@ -909,6 +910,10 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     // Sharded head: push this rank's candidates to every rank's mailbox,
     // wait for every rank's, merge (per residue: larger value, then lower
     // index) into the outputs; the argmax tree below runs on the merge.
+    // Each sender has two slots per mailbox, used by calls of alternating
+    // epoch parity: a rank reaches call e+2's stores only after every rank
+    // raised its call-(e+1) flag, which each does after finishing its call-e
+    // merge, so a slot is never overwritten while its reader still needs it.
     const Exchange& X = tl.xc;
     __shared__ uint32_t s_epoch;
     if (threadIdx.x == 0) {
@@ -917,8 +922,9 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     }
     __syncthreads();
     const uint32_t ep = s_epoch;
+    const uint32_t par = ep & 1u;
     for (uint32_t p = 0; p < X.world; ++p) {
-      uint32_t* slot = X.peer[p] + X.rank * kSlotWords;
+      uint32_t* slot = X.peer[p] + mailbox_slot(X.rank, par);
       if (threadIdx.x < 256) {
         slot[threadIdx.x] = __float_as_uint(f_v[threadIdx.x]);
         slot[256 + threadIdx.x] = f_i[threadIdx.x];
@@ -927,14 +933,14 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x < X.world)
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.peer[threadIdx.x] + X.rank * kSlotWords + kSlotFlag),
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.peer[threadIdx.x] + mailbox_slot(X.rank, par) + kSlotFlag),
                    "r"(ep)
                    : "memory");
     // every rank's slot in this rank's mailbox (bounded wait)
     if (threadIdx.x < X.world) {
-      const uint32_t* flag = X.peer[X.rank] + threadIdx.x * kSlotWords + kSlotFlag;
+      const uint32_t* flag = X.peer[X.rank] + mailbox_slot(threadIdx.x, par) + kSlotFlag;
       bool ok = false;
-      for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) {
+      for (uint32_t i = 0; i < spin && !ok; ++i) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
         ok = (v == ep);
@@ -946,11 +952,11 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
     if (threadIdx.x < 256) {
       const uint32_t r = threadIdx.x;
       const uint32_t* mb = X.peer[X.rank];
-      float bv = __uint_as_float(__ldcv(mb + r));
-      uint32_t bi = __ldcv(mb + 256 + r);
+      float bv = __uint_as_float(__ldcv(mb + mailbox_slot(0, par) + r));
+      uint32_t bi = __ldcv(mb + mailbox_slot(0, par) + 256 + r);
       for (uint32_t q = 1; q < X.world; ++q) {
-        const float v = __uint_as_float(__ldcv(mb + q * kSlotWords + r));
-        const uint32_t i = __ldcv(mb + q * kSlotWords + 256 + r);
+        const float v = __uint_as_float(__ldcv(mb + mailbox_slot(q, par) + r));
+        const uint32_t i = __ldcv(mb + mailbox_slot(q, par) + 256 + r);
         if (better(v, i, bv, bi)) {
           bv = v;
           bi = i;
@@ -979,11 +985,11 @@ __global__ void __launch_bounds__(kEngineWarps * 32, 1)
   }
 }
 
-__global__ void init_select_kernel(SelectScratch sc) {
+__global__ void init_select_kernel(SelectScratch sc, int clear_status) {
   sc.slots[threadIdx.x] = sel_key(kFloorE, 0u);
   if (threadIdx.x == 0) {
     *sc.counter = 0u;
-    *sc.status = 0u;
+    if (clear_status) *sc.status = 0u;
   }
 }
 
@@ -1005,16 +1011,12 @@ cudaError_t launch_xs(const TaskList& tasks, const CUtensorMap& map, const CUten
                            int hs, const SelectScratch& sel, uint32_t grid, cudaStream_t s) {
   const size_t xcap = xcache_bytes<FMT>(hs);
   const size_t smem = kAlignSlack + weight_smem<FMT>() + kTaskSmem + xcap + (hs ? kSelectSmem : kPartSmem);
-  static int attr_dev = -1;
+  static std::atomic<uint8_t> attr_set[kAttrDevices];
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(engine_kernel<NT, COLS, KS, FMT, XS, PR>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(kSmemLimit - kStaticSmemHeadroom));
-    if (e != cudaSuccess) return e;
-    attr_dev = dev;
-  }
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = smem_attr_once(attr_set, dev, engine_kernel<NT, COLS, KS, FMT, XS, PR>, (int)(kSmemLimit - kStaticSmemHeadroom));
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kEngineWarps * 32);
@@ -1043,8 +1045,8 @@ cudaError_t launch_variant(const TaskList& tasks, const CUtensorMap& map, const 
 
 }  // namespace
 
-cudaError_t init_select_scratch(const SelectScratch& sc, cudaStream_t s) {
-  init_select_kernel<<<1, 256, 0, s>>>(sc);
+cudaError_t init_select_scratch(const SelectScratch& sc, cudaStream_t s, bool clear_status) {
+  init_select_kernel<<<1, 256, 0, s>>>(sc, clear_status ? 1 : 0);
   return cudaGetLastError();
 }
 

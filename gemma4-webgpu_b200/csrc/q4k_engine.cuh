@@ -86,14 +86,22 @@ struct XJob {
 // Tasks / jobs either live in device memory (plans) or are passed inline as
 // kernel parameters (single calls).
 // Candidate exchange of a vocabulary-sharded LM head (q4k_exchange): every
-// rank owns a mailbox of kMaxRanks slots in its own device memory; the last
-// CTA of a rank's LM-head launch writes its 256 candidates into slot `rank`
-// of every rank's mailbox (peer stores over NVLink), raises the slot's flag
-// to this call's epoch, waits (bounded) until all `world` slots of its own
-// mailbox carry the epoch, and merges them.
+// rank owns a mailbox of 2 x kMaxRanks slots in its own device memory; the
+// last CTA of a rank's LM-head launch for call epoch e writes its 256
+// candidates into slot (rank, e & 1) of every rank's mailbox (peer stores
+// over NVLink), raises that slot's flag to e, waits (bounded) until the
+// (q, e & 1) slots of all `world` senders q in its own mailbox carry e, and
+// merges them.  Two slots per sender, alternating by epoch parity, keep a
+// fast rank's next call from overwriting candidates a slower rank is still
+// merging.
 constexpr uint32_t kMaxRanks = 8;
 constexpr uint32_t kSlotWords = 576;      // 256 values, 256 indices, flag at word 512; 2304 bytes
 constexpr uint32_t kSlotFlag = 512;
+constexpr uint32_t kMailboxSlots = 2 * kMaxRanks;
+constexpr uint32_t kMailboxEpochWord = kMailboxSlots * kSlotWords;  // this rank's call counter
+
+// Word offset of sender q's slot for epoch parity `par` in a mailbox.
+__host__ __device__ inline uint32_t mailbox_slot(uint32_t q, uint32_t par) { return (2u * q + par) * kSlotWords; }
 
 struct Exchange {
   uint32_t* peer[kMaxRanks];  // mailbox of each rank as mapped on this device (peer[rank] = own)

@@ -18,13 +18,14 @@ using namespace q4k;
 struct q4k_exchange {
   q4k_ctx* ctx = nullptr;
   uint32_t rank = 0, world = 0;
-  uint32_t* mailbox = nullptr;          // own: kMaxRanks slots + the epoch word
+  uint32_t* mailbox = nullptr;          // own: kMailboxSlots slots + the epoch word
   uint32_t* peer[kMaxRanks] = {nullptr};  // mapped peer mailboxes (peer[rank] = mailbox)
   bool opened[kMaxRanks] = {false};
+  bool ipc[kMaxRanks] = {false};        // peer mapped through CUDA IPC (closed on destroy)
 };
 
 namespace {
-constexpr size_t kMailboxBytes = (size_t)kMaxRanks * kSlotWords * 4 + 256;
+constexpr size_t kMailboxBytes = (size_t)kMailboxEpochWord * 4 + 256;
 }
 
 extern "C" {
@@ -71,6 +72,33 @@ int q4k_exchange_open(q4k_exchange* ex, uint32_t peer, const void* handle) {
   if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_exchange_open");
   ex->peer[peer] = static_cast<uint32_t*>(p);
   ex->opened[peer] = true;
+  ex->ipc[peer] = true;
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
+int q4k_exchange_open_local(q4k_exchange* ex, uint32_t peer, const q4k_exchange* other) {
+  if (!ex || !other) return Q4K_ERR_INVALID_ARG;
+  q4k_ctx* ctx = ex->ctx;
+  if (peer >= ex->world) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "peer %u outside world %u", peer, ex->world);
+  if (other->world != ex->world || other->rank != peer)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "the other mailbox is rank %u of %u, expected rank %u of %u",
+                    other->rank, other->world, peer, ex->world);
+  if (peer == ex->rank || ex->opened[peer]) return Q4K_OK;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return ctx_fail(ctx, Q4K_ERR_CUDA, "cudaSetDevice failed");
+  const int pdev = other->ctx->device;
+  if (pdev != ctx->device) {
+    int can = 0;
+    cudaError_t e = cudaDeviceCanAccessPeer(&can, ctx->device, pdev);
+    if (e != cudaSuccess || !can)
+      return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "device %d cannot access device %d's memory", ctx->device, pdev);
+    e = cudaDeviceEnablePeerAccess(pdev, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+    else if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_exchange_open_local peer access");
+  }
+  ex->peer[peer] = other->mailbox;
+  ex->opened[peer] = true;
+  ex->ipc[peer] = false;
   ctx->err[0] = 0;
   return Q4K_OK;
 }
@@ -79,7 +107,7 @@ void q4k_exchange_destroy(q4k_exchange* ex) {
   if (!ex) return;
   cudaSetDevice(ex->ctx->device);
   for (uint32_t p = 0; p < ex->world; ++p)
-    if (p != ex->rank && ex->opened[p]) cudaIpcCloseMemHandle(ex->peer[p]);
+    if (p != ex->rank && ex->opened[p] && ex->ipc[p]) cudaIpcCloseMemHandle(ex->peer[p]);
   if (ex->mailbox) cudaFree(ex->mailbox);
   delete ex;
 }
@@ -129,7 +157,7 @@ int q4k_lmhead_select_sharded(q4k_ctx* ctx, q4k_exchange* ex, const void* w, con
   tl.total_cost = tiles_of(V) * item_cost(N, kTaskSelect);
   tl.pairs = pairs_of(N, 0, tile_bytes) ? 1u : 0u;
   for (uint32_t p = 0; p < ex->world; ++p) tl.xc.peer[p] = ex->peer[p];
-  tl.xc.epoch = ex->mailbox + kMaxRanks * kSlotWords;
+  tl.xc.epoch = ex->mailbox + kMailboxEpochWord;
   tl.xc.rank = ex->rank;
   tl.xc.world = ex->world;
   return ctx_cuda(ctx, launch_engine(tl, map, 1, true, ctx->select, ctx->sm_count, s),

@@ -127,6 +127,7 @@ struct GemmArgs {
                            // the B map's box)
   uint32_t parts;          // operand rows per activation row: 2 (exact f16 hi + lo) or 1 (f16 only)
   uint32_t* status;        // bit 0: a bounded wait expired
+  uint32_t spin;           // polls per bounded wait (0: kSpinLimit)
 };
 
 // The raw Q4_K bytes one A-producer thread (one row) needs for one K step:
@@ -166,6 +167,7 @@ __device__ __forceinline__ RowChunks dequant_group(const RawGroup& g, uint32_t j
 
 __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap bmap,
                                                             const __grid_constant__ CUtensorMap amap, const GemmArgs a) {
+  const uint32_t spin = spin_or_default(a.spin);  // polls per bounded wait
   extern __shared__ uint8_t g_smem_raw[];
   // swizzled operand tiles start on 1024-byte boundaries
   uint8_t* smem = g_smem_raw + ((1024u - (smem_u32(g_smem_raw) & 1023u)) & 1023u);
@@ -215,7 +217,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       uint32_t issued = 0;
       for (uint32_t ks = 0; ks < ksteps; ++ks) {
         const uint32_t s = ks % kGStages, use = ks / kGStages;
-        if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u)) {
+        if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u, spin)) {
           failed = true;
           break;
         }
@@ -225,7 +227,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       }
       // every issued copy has landed before the CTA can exit
       for (uint32_t ks = (issued > kGStages ? issued - kGStages : 0); ks < issued; ++ks)
-        if (!mbar_wait(&full_b[ks % kGStages], (ks / kGStages) & 1u)) failed = true;
+        if (!mbar_wait(&full_b[ks % kGStages], (ks / kGStages) & 1u, spin)) failed = true;
     }
   } else if (warp == 1) {
     // MMA issuer: per stage and 16-wide k slice, one 128 x n_mma x 16 MMA per
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       const uint32_t idesc = idesc_f16(n_mma);
       for (uint32_t ks = 0; ks < ksteps; ++ks) {
         const uint32_t s = ks % kGStages, ph = (ks / kGStages) & 1u;
-        if (!mbar_wait(&full_a[s], ph) || !mbar_wait(&full_b[s], ph)) {
+        if (!mbar_wait(&full_a[s], ph, spin) || !mbar_wait(&full_b[s], ph, spin)) {
           failed = true;
           break;
         }
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     const uint32_t rb = r & (kGMmaM - 1), sw = rb & 7u;  // 128-byte swizzle: chunk index ^ row%8
     for (uint32_t ks = 0; ks < ksteps && !failed; ++ks) {
       const uint32_t sb = ks >> 2, j = ks & 3u, rs = sb % kGRawStages;
-      if (j == 0 && !mbar_wait(&raw_full[rs], (sb / kGRawStages) & 1u)) {
+      if (j == 0 && !mbar_wait(&raw_full[rs], (sb / kGRawStages) & 1u, spin)) {
         failed = true;
         break;
       }
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       }
       const RowChunks ch = dequant_group(g, j);
       const uint32_t s = ks % kGStages, use = ks / kGStages;
-      if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u)) {
+      if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u, spin)) {
         failed = true;
         break;
       }
@@ -291,7 +293,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     }
     // epilogue: warp w reads accumulator (w-2)/4 (rows 128*that ..) in its
     // tensor-memory lane quarter w%4
-    if (!mbar_wait(&done_bar, 0)) {
+    if (!mbar_wait(&done_bar, 0, spin)) {
       failed = true;
     } else {
       tc_fence_after();
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     uint32_t issued = 0;
     for (uint32_t sb = 0; sb < nb; ++sb) {
       const uint32_t rs = sb % kGRawStages, use = sb / kGRawStages;
-      if (use > 0 && !mbar_wait(&raw_empty[rs], (use - 1) & 1u)) {
+      if (use > 0 && !mbar_wait(&raw_empty[rs], (use - 1) & 1u, spin)) {
         failed = true;
         break;
       }
@@ -333,10 +335,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     }
     // every issued copy has landed before the CTA can exit
     for (uint32_t sb = (issued > kGRawStages ? issued - kGRawStages : 0); sb < issued; ++sb)
-      if (!mbar_wait(&raw_full[sb % kGRawStages], (sb / kGRawStages) & 1u)) failed = true;
+      if (!mbar_wait(&raw_full[sb % kGRawStages], (sb / kGRawStages) & 1u, spin)) failed = true;
   }
   if (failed) atomicOr(a.status, 1u);
-  if (warp == 1 && lane == 0 && failed) mbar_wait(&done_bar, 0);  // MMAs still running must finish first
+  if (warp == 1 && lane == 0 && failed) mbar_wait(&done_bar, 0, spin);  // MMAs still running must finish first
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -400,11 +402,10 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
   if (parts != 1 && parts != 2) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "parts=%u must be 1 or 2", parts);
   EncodeTiledFn enc = gemm_encode_fn();
   if (!enc) return ctx_fail(ctx, Q4K_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  static int attr_dev = -1;
-  if (attr_dev != ctx->device) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGSmem);
+  static std::atomic<uint8_t> attr_set[kAttrDevices];
+  {
+    const cudaError_t e = smem_attr_once(attr_set, ctx->device, gemm_kernel, (int)kGSmem);
     if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm shared-memory attribute");
-    attr_dev = ctx->device;
   }
   // activation rows per pass: the B operand (4 bytes per element per row)
   // and the per-row scales fit the context scratch
@@ -462,6 +463,7 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     ga.tile_tokens = tile;
     ga.parts = parts;
     ga.status = ctx->select.status;
+    ga.spin = ctx->select.spin_limit;
     const dim3 grid((M + kGRows - 1) / kGRows, (tc + ga.tile_tokens - 1) / ga.tile_tokens);
     gemm_kernel<<<grid, kGThreads, kGSmem, s>>>(bmap, amap, ga);
     e = cudaGetLastError();

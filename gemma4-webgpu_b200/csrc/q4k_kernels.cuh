@@ -5,7 +5,27 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace q4k {
+
+// Raises a kernel's dynamic shared-memory limit once per device.  `done` is
+// the kernel's own per-device flag table; a flag is set only after the call
+// succeeded, and two host threads that both see it unset both make the
+// (idempotent) call, so threads driving different devices never skip it.
+constexpr int kAttrDevices = 64;
+
+// Default polls per bounded wait in the kernels (mbarrier and peer-flag
+// waits); a context may set its own (q4k_set_wait_limit).
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+template <typename K>
+inline cudaError_t smem_attr_once(std::atomic<uint8_t> (&done)[kAttrDevices], int dev, K* kernel, int bytes) {
+  if (dev >= 0 && dev < kAttrDevices && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < kAttrDevices) done[dev].store(1, std::memory_order_release);
+  return e;
+}
 
 // Scratch of the fused LM head: 256 64-bit order keys (one per residue) and a
 // completion counter.  Between calls the keys hold the empty candidate
@@ -14,12 +34,14 @@ struct SelectScratch {
   unsigned long long* slots = nullptr;  // [256]
   uint32_t* counter = nullptr;          // [1]
   uint32_t* status = nullptr;           // [1] nonzero: a kernel gave up a bounded wait
+  uint32_t spin_limit = 0;              // polls per bounded wait (0: kSpinLimit, q4k_ptx.cuh)
 };
 
 constexpr size_t kSelectScratchBytes = 256 * sizeof(unsigned long long) + 256;
 
-// Writes the between-calls state into a fresh scratch.
-cudaError_t init_select_scratch(const SelectScratch& sc, cudaStream_t s);
+// Writes the between-calls state (empty keys, counter 0) into the scratch;
+// clear_status also zeroes the status word (a fresh scratch).
+cudaError_t init_select_scratch(const SelectScratch& sc, cudaStream_t s, bool clear_status = true);
 
 // y[b*ldy + m] = sum_k w16(m,k) * x[b*ldx + k] for b < batch, m < M.
 // The scratch-free CUDA-core kernel (one warp per row); the engine

@@ -83,9 +83,11 @@ extern "C" int q4k_lmhead_select_static(const void* w, const float* x, uint32_t 
   uint32_t tile_bytes = 0;
   if (encode_weight_map(&map, w, V, N, &tile_bytes) != cudaSuccess) return Q4K_ERR_CUDA;
 
-  // The array keeps the previous call's contents: put the selection keys,
-  // counter and status back to their starting values before this call.
-  if (init_select_scratch(sel, s) != cudaSuccess) return Q4K_ERR_CUDA;
+  // The array keeps the previous call's contents: put the selection keys
+  // and the counter back to their starting values before this call.  The
+  // status word is left alone: a bounded wait that expired in an earlier
+  // call stays recorded until q4k_check_static reads and clears it.
+  if (init_select_scratch(sel, s, false) != cudaSuccess) return Q4K_ERR_CUDA;
   JobList jl{};
   jl.n = 1;
   jl.inl.x = x;
@@ -118,4 +120,18 @@ extern "C" int q4k_lmhead_select_static(const void* w, const float* x, uint32_t 
   tl.pairs = pairs_of(N, 0, tile_bytes) ? 1u : 0u;
   if (launch_engine(tl, map, 1, true, sel, sms, s) != cudaSuccess) return Q4K_ERR_CUDA;
   return Q4K_OK;
+}
+
+extern "C" int q4k_check_static(void) {
+  // The status word sits at a fixed offset of the array; it is read and
+  // cleared by symbol, so no device address or allocation is involved.
+  constexpr size_t kStatusOff = kSelBytes + 4;
+  if (cudaDeviceSynchronize() != cudaSuccess) return Q4K_ERR_CUDA;
+  uint32_t status = 0;
+  if (cudaMemcpyFromSymbol(&status, g_static_scratch, sizeof(status), kStatusOff) != cudaSuccess)
+    return Q4K_ERR_CUDA;
+  if (status == 0) return Q4K_OK;
+  const uint32_t zero = 0;
+  if (cudaMemcpyToSymbol(g_static_scratch, &zero, sizeof(zero), kStatusOff) != cudaSuccess) return Q4K_ERR_CUDA;
+  return Q4K_ERR_TIMEOUT;
 }

@@ -5,6 +5,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include "q4k_kernels.cuh"
+
 namespace q4k {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -32,12 +34,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after kSpinLimit polls (each poll may itself block
-// for a short hardware-defined time), so a lost completion cannot hang the GPU.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Bounded wait: gives up after `limit` polls (each poll may itself block for
+// a short hardware-defined time), so a lost completion cannot hang the GPU.
+// kSpinLimit (q4k_kernels.cuh) is the default; a context can change it
+// (q4k_set_wait_limit).
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+__device__ __forceinline__ uint32_t spin_or_default(uint32_t limit) { return limit ? limit : kSpinLimit; }
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }

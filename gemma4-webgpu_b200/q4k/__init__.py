@@ -5,7 +5,7 @@ shaders/matmul_quant*.wgsl, logit_softcap, argmax, topk256, gelu_mul); the
 compute runs in libq4k.so's sm_100a kernels, loaded through ctypes.
 """
 from ._lib import Q4KError, lib  # noqa: F401
-from .ops import Context, Plan, Selection, context, sample_topk256  # noqa: F401
+from .ops import Context, Plan, Selection, context  # noqa: F401
 from . import gguf, synth  # noqa: F401
 
-__all__ = ["Context", "Plan", "Selection", "context", "sample_topk256", "synth", "gguf", "Q4KError", "lib"]
+__all__ = ["Context", "Plan", "Selection", "context", "synth", "gguf", "Q4KError", "lib"]

@@ -27,6 +27,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_destroy": ([_P], None),
     "q4k_last_error": ([_P], ctypes.c_char_p),
     "q4k_check": ([_P], _I),
+    "q4k_set_wait_limit": ([_P, _U32], _I),
     "q4k_matmul_quant": ([_P, _P, _P, _P, _U32, _U32, _P], _I),
     "q4k_gemv": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
     "q4k_gemm": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
@@ -40,8 +41,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_lmhead_select": ([_P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_merge_candidates": ([_P, _P, _P, _U32, _P, _P, _P, _P], _I),
     "q4k_lmhead_select_static": ([_P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
+    "q4k_check_static": ([], _I),
     "q4k_exchange_create": ([_P, _U32, _U32, ctypes.POINTER(_P), _P], _I),
     "q4k_exchange_open": ([_P, _U32, _P], _I),
+    "q4k_exchange_open_local": ([_P, _U32, _P], _I),
     "q4k_exchange_destroy": ([_P], None),
     "q4k_lmhead_select_sharded": ([_P, _P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P], _I),
     "q4k_q6k_device_bytes": ([_U32, _U32], _U64),

@@ -11,8 +11,6 @@ call raises Q4KError.
 from __future__ import annotations
 
 import ctypes
-import math
-import random
 from dataclasses import dataclass
 
 import torch
@@ -99,6 +97,11 @@ class Context:
         """Synchronize and raise Q4KError if a kernel gave up a bounded wait
         since the last check (q4k_check)."""
         self._check(self._L.q4k_check(self._h))
+
+    def set_wait_limit(self, polls: int) -> None:
+        """Polls each bounded wait of this context's kernels makes before it
+        gives up (0: the built-in default; q4k_set_wait_limit)."""
+        self._check(self._L.q4k_set_wait_limit(self._h, polls))
 
     # ---- matmulQuant / matmulQuantMR4 -----------------------------------
 
@@ -435,6 +438,11 @@ class Exchange:
         buf = ctypes.create_string_buffer(handle, self.HANDLE_BYTES)
         self._ctx._check(self._L.q4k_exchange_open(self._h, peer, buf))
 
+    def open_local(self, peer: int, other: "Exchange") -> None:
+        """Map `other`, rank `peer`'s mailbox created in this process
+        (q4k_exchange_open_local)."""
+        self._ctx._check(self._L.q4k_exchange_open_local(self._h, peer, other._h))
+
     def close(self) -> None:
         if self._h:
             self._L.q4k_exchange_destroy(self._h)
@@ -557,45 +565,3 @@ def context(device: int | None = None) -> Context:
         _contexts[device] = Context(device)
     return _contexts[device]
 
-
-# ---- host-side consumer of topk256 (CPU, as in the reference) ---------------
-
-def sample_topk256(result512, temperature: float = 0.0, top_p: float = 1.0, rep_penalty: float = 1.0,
-                   all_tokens=(), rng: random.Random | None = None) -> int:
-    """Pick the next token from the topk256 buffer the way
-    sampleNextTokenSubmit's readback does (src/engine.ts:1792-1837):
-    repetition penalty on seen ids, a stable descending sort by value, then
-    greedy (temperature 0) or temperature + top-p sampling over the 256."""
-    import numpy as np
-
-    buf = np.asarray(result512, dtype=np.float32).reshape(-1)
-    vals = buf[0::2].astype(np.float64)
-    ids = buf[1::2].view(np.uint32).astype(np.int64)
-    cands = [[float(vals[i]), int(ids[i])] for i in range(256)]
-    if rep_penalty > 1.0 and len(all_tokens) > 0:
-        seen = set(all_tokens)
-        for c in cands:
-            if c[1] in seen:
-                c[0] = c[0] / rep_penalty if c[0] > 0 else c[0] * rep_penalty
-    cands.sort(key=lambda c: -c[0])  # Array.prototype.sort is stable, as is list.sort
-    if temperature == 0:
-        return cands[0][1]
-    rng = rng or random.Random()
-    max_logit = cands[0][0]
-    probs = [math.exp((c[0] - max_logit) / temperature) for c in cands]
-    s = sum(probs)
-    cum, cutoff = 0.0, 256
-    for i, p in enumerate(probs):
-        cum += p / s
-        if cum >= top_p:
-            cutoff = i + 1
-            break
-    subset = sum(probs[:cutoff])
-    r = rng.random() * subset
-    picked = cands[cutoff - 1][1]
-    for i in range(cutoff):
-        r -= probs[i]
-        if r <= 0:
-            picked = cands[i][1]
-            break
-    return picked

@@ -80,6 +80,17 @@ Q4K_API const char* q4k_last_error(const q4k_ctx* ctx);
  * (src/engine.ts:385-388, 1677). */
 Q4K_API int q4k_check(q4k_ctx* ctx);
 
+/* Polls each bounded wait of this context's kernels makes before giving up
+ * (the wait on a weight copy, a K-split partner or a peer rank's candidates;
+ * expiry is what q4k_check reports as Q4K_ERR_TIMEOUT).  polls = 0 restores
+ * the built-in default (2^22 polls, seconds).  A smaller limit makes a lost
+ * peer or copy surface sooner; it must stay well above the longest legitimate
+ * wait (microseconds for copies, a peer's whole shard for the sharded head).
+ * Applies to launches made after the call.  No reference counterpart (WebGPU
+ * exposes no timeout; the engine's only failure signal is device loss,
+ * src/engine.ts:385-388). */
+Q4K_API int q4k_set_wait_limit(q4k_ctx* ctx, uint32_t polls);
+
 /* matmul_quant: output[m] = sum_k f32(w[m,k]) * input[k], m < M.
  * Argument order and meaning follow the pipeline's bind group 0
  * {0: input f32[N], 1: weight, 2: output f32[M], 3: {M, N}}
@@ -185,11 +196,22 @@ Q4K_API int q4k_merge_candidates(q4k_ctx* ctx, const float* vals, const uint32_t
  * device current), so make the first call on each device before any stream
  * capture.  Every call shares the one array and resets its selection state
  * first: calls that overlap on the GPU (other streams, other host threads)
- * race and give wrong results; order them on one stream.  Arguments and
- * outputs as q4k_lmhead_select; errors are return codes only. */
+ * race and give wrong results; order them on one stream.  The cached
+ * address does not survive cudaDeviceReset: do not reset a device between
+ * calls.  Arguments and outputs as q4k_lmhead_select; errors are return
+ * codes only: argument and launch errors at the call, and a bounded wait
+ * that expired inside the kernel (outputs invalid) through
+ * q4k_check_static. */
 Q4K_API int q4k_lmhead_select_static(const void* w, const float* x, uint32_t V, uint32_t N, float cap,
                                      uint32_t row_offset, float* logits, float* cand_val, uint32_t* cand_idx,
                                      uint32_t* argmax, void* stream);
+
+/* The q4k_check of q4k_lmhead_select_static, which has no context: on the
+ * current device, synchronize, then report whether any call since the last
+ * check gave up a bounded wait (Q4K_ERR_TIMEOUT; those calls' outputs are
+ * invalid) and clear the record, reading the fixed array's status word
+ * without allocating.  Q4K_OK otherwise.  No counterpart in the reference. */
+Q4K_API int q4k_check_static(void);
 
 /* ---- vocabulary-sharded LM head, exchange fused into the launch -------
  * The reference's LM head runs on one device (sampleNextTokenSubmit,
@@ -209,6 +231,11 @@ typedef struct q4k_exchange q4k_exchange;
 
 Q4K_API int q4k_exchange_create(q4k_ctx* ctx, uint32_t rank, uint32_t world, q4k_exchange** out, void* handle_out);
 Q4K_API int q4k_exchange_open(q4k_exchange* ex, uint32_t peer, const void* handle);
+/* q4k_exchange_open for a peer mailbox created in this same process (ranks
+ * driven as devices of one process, where a CUDA IPC handle cannot be
+ * reopened): maps `other` (rank `peer` of the same world) directly, enabling
+ * peer access when it lives on another device. */
+Q4K_API int q4k_exchange_open_local(q4k_exchange* ex, uint32_t peer, const q4k_exchange* other);
 Q4K_API void q4k_exchange_destroy(q4k_exchange* ex);
 
 /* This rank's shard of the head (rows of `w` are global indices row_offset +

@@ -3,8 +3,9 @@ tests/test_multi_gpu.py through torchrun; not collected by pytest).
 
 Every rank builds the same seeded 262144 x 1536 head, keeps its row shard on
 its GPU, runs q4k.sharded.ShardedLMHead (fused head on the shard, NCCL
-all-gather of the candidates, merge) and compares the merged candidates and
-argmax with the unsharded fused head run on its own GPU.  Prints one line
+all-gather of the candidates, merge; then the exchange fused into the
+launch) on six different inputs back to back and compares each call's merged
+candidates and argmax with the unsharded fused head run on its own GPU.  Prints one line
 "rank R ok" or raises.
 """
 from __future__ import annotations
@@ -33,17 +34,25 @@ def main() -> None:
         V, N = 262144, 1536
         ctx = Context(local)
         w = torch.from_numpy(synth.q4k_matrix(V, N, 777)).cuda()
-        x = torch.from_numpy(synth.activations(1, N, 778)[0]).cuda()
-        ref = ctx.lmhead_select(w, x, V, N, 30.0)
+        # a different input on every call: a merge that read a slot the
+        # next call had already overwritten would show up as a mismatch
+        xs = [torch.from_numpy(synth.activations(1, N, seed)[0]).cuda() for seed in range(778, 784)]
+        refs = [ctx.lmhead_select(w, x, V, N, 30.0) for x in xs]
+        torch.cuda.synchronize()
         for fused in (False, True):
             head = ShardedLMHead(V, N, 30.0, ctx=ctx, fused=fused)
-            for _ in range(3):  # repeated calls: scratch and mailboxes reset between calls
-                merged = head(w[head.row0:head.row0 + head.rows], x)
-                torch.cuda.synchronize()
-                assert torch.equal(merged.cand_idx, ref.cand_idx), f"candidate indices differ (fused={fused})"
-                assert torch.equal(merged.cand_val.view(torch.int32), ref.cand_val.view(torch.int32)), \
-                    f"values differ (fused={fused})"
-                assert torch.equal(merged.argmax, ref.argmax), f"argmax differs (fused={fused})"
+            w_shard = w[head.row0:head.row0 + head.rows]
+            # back to back, no host synchronization between calls
+            merged = []
+            for x in xs:
+                m = head(w_shard, x)
+                merged.append((m.cand_idx.clone(), m.cand_val.clone(), m.argmax.clone()))
+            torch.cuda.synchronize()
+            for i, ((idx, val, am), ref) in enumerate(zip(merged, refs)):
+                assert torch.equal(idx, ref.cand_idx), f"call {i}: candidate indices differ (fused={fused})"
+                assert torch.equal(val.view(torch.int32), ref.cand_val.view(torch.int32)), \
+                    f"call {i}: values differ (fused={fused})"
+                assert torch.equal(am, ref.argmax), f"call {i}: argmax differs (fused={fused})"
             ctx.check()
             dist.barrier()
             head.close()

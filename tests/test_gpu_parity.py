@@ -84,6 +84,18 @@ def test_gemv_large_m_2d_grid_case(ctx, oracle):
     check_gemv(oracle, y, w, x, M, N)
 
 
+def test_gemv_rowwarp_path(ctx, oracle):
+    """Requests whose prepared activation (4 bytes per element per row) would
+    exceed the context's 16 MB scratch take the scratch-free warp-per-row
+    kernel: 16 rows of N = 262400 need 16.8 MB.  batch 19 runs as chunks of
+    16 (warp per row) and 3 (the engine with a separate preparation launch)."""
+    M, N, batch = 24, 262400, 19
+    w = synth.q4k_matrix(M, N, 81)
+    x = synth.activations(batch, N, 82)
+    y = ctx.gemv(to_dev(w), to_dev(x), M, N).cpu().numpy()
+    check_gemv(oracle, y, w, x, M, N)
+
+
 def test_config1_ffn_chain(ctx, oracle):
     I, H = 6144, 1536
     wg = synth.q4k_matrix(I, H, synth.seed_for(1, 0))
@@ -248,20 +260,23 @@ def test_sharded_lmhead_merge_equals_unsharded(ctx, oracle, G):
 
 def test_fused_exchange_one_rank_equals_unsharded(ctx):
     # the fused sharded head with a world of 1: the launch writes its
-    # candidates into its own mailbox, waits for them and merges; repeated
-    # calls advance the mailbox epoch
+    # candidates into its own mailbox, waits for them and merges.  Calls go
+    # back to back with a different input each and no host synchronization
+    # in between, so consecutive calls alternate the mailbox's two slot sets
+    # (epoch parity) while the previous call's data is still fresh.
     V, N = 32768, 1536
     w = to_dev(synth.q4k_matrix(V, N, 71))
+    xs = [to_dev(synth.activations(1, N, seed)[0]) for seed in (72, 73, 74, 75, 76)]
+    refs = [ctx.lmhead_select(w, x, V, N, 30.0) for x in xs]
+    torch.cuda.synchronize()
     ex = ctx.exchange(0, 1)
     try:
-        for seed in (72, 73, 74):
-            x = to_dev(synth.activations(1, N, seed)[0])
-            ref = ctx.lmhead_select(w, x, V, N, 30.0)
-            got = ctx.lmhead_select_sharded(ex, w, x, V, N, 30.0)
-            torch.cuda.synchronize()
-            assert torch.equal(got.cand_idx, ref.cand_idx)
-            assert torch.equal(got.cand_val.view(torch.int32), ref.cand_val.view(torch.int32))
-            assert torch.equal(got.argmax, ref.argmax)
+        got = [ctx.lmhead_select_sharded(ex, w, x, V, N, 30.0) for x in xs]
+        torch.cuda.synchronize()
+        for g, ref in zip(got, refs):
+            assert torch.equal(g.cand_idx, ref.cand_idx)
+            assert torch.equal(g.cand_val.view(torch.int32), ref.cand_val.view(torch.int32))
+            assert torch.equal(g.argmax, ref.argmax)
         ctx.check()
     finally:
         ex.close()

@@ -56,7 +56,32 @@ def _merge_np(vals: np.ndarray, idx: np.ndarray):
     return out_v, out_i, int(ti[0])
 
 
-def _rank_main(rank: int, world: int, port: int, results):
+def planted_logits(oracle, world: int) -> np.ndarray:
+    """The head's softcapped logits with injected hazards: a tie between two
+    shards in one residue class (the lower global index must win), a tie for
+    the global maximum between shards (the argmax tree's rule decides), and
+    a NaN row (never selected)."""
+    from q4k import synth
+
+    w = synth.q4k_matrix(V, N, SEED)
+    x = synth.activations(1, N, SEED + 1)
+    logits = oracle.logit_softcap(oracle.q4k_gemv(w, x, V, N)[0], CAP).copy()
+    last = (world - 1) * (V // world)  # first row of the last shard: same residues as shard 0
+    logits[7] = logits[last + 7] = np.float32(29.5)
+    logits[300] = logits[last + 300] = logits[V // world + 20] = np.float32(29.9)
+    logits[123] = np.float32(np.nan)
+    logits[last + 123] = np.float32(np.nan)
+    return logits
+
+
+def _rank_main(rank: int, world: int, port: int, results, mode: str = "gemv"):
+    """One CPU rank.  mode "gemv": the shard's logits from the oracle GEMV;
+    "planted": the shard of planted_logits; "fail": rank 1 raises before the
+    all-gather, the others must get an error from the collective (bounded by
+    the process group's timeout) instead of hanging.  Each rank records its
+    outcome in `results`."""
+    from datetime import timedelta
+
     _paths()
     import oracle as O
     from q4k import synth
@@ -65,15 +90,21 @@ def _rank_main(rank: int, world: int, port: int, results):
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
     try:
         w = synth.q4k_matrix(V, N, SEED)
         x = synth.activations(1, N, SEED + 1)
+        full = planted_logits(O, world) if mode == "planted" else None
 
         def select(w_shard, x_t, send):
             rows = head.rows
-            logits = O.q4k_gemv(w_shard.numpy(), x_t.numpy()[None, :], rows, N)[0]
-            vals, idx = O.topk256(O.logit_softcap(logits, CAP))
+            if mode == "fail" and rank == 1:
+                raise RuntimeError("injected shard failure")
+            if full is not None:
+                logits = full[head.row0:head.row0 + rows]
+            else:
+                logits = O.logit_softcap(O.q4k_gemv(w_shard.numpy(), x_t.numpy()[None, :], rows, N)[0], CAP)
+            vals, idx = O.topk256(np.ascontiguousarray(logits))
             send[:256] = torch.from_numpy(vals)
             send[256:] = torch.from_numpy((idx.astype(np.int64) + head.row0).astype(np.int32)).view(torch.float32)
 
@@ -84,8 +115,12 @@ def _rank_main(rank: int, world: int, port: int, results):
 
         head = ShardedLMHead(V, N, CAP, select=select, merge=merge)
         w_shard = torch.from_numpy(np.ascontiguousarray(w[head.row0:head.row0 + head.rows]))  # [rows, N/256*144]
-        sel = head(w_shard, torch.from_numpy(x[0]))
-        results[rank] = (sel.cand_val.numpy().copy(), sel.cand_idx.numpy().copy(), int(sel.argmax[0]),
+        try:
+            sel = head(w_shard, torch.from_numpy(x[0]))
+        except Exception as e:  # noqa: BLE001 -- the outcome is the test's subject
+            results[rank] = ("error", f"{type(e).__name__}: {e}")
+            return
+        results[rank] = ("ok", sel.cand_val.numpy().copy(), sel.cand_idx.numpy().copy(), int(sel.argmax[0]),
                          head.row0, head.rows)
     finally:
         dist.destroy_process_group()
@@ -97,27 +132,61 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _run_ranks(world: int, mode: str) -> dict:
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    mp.start_processes(_rank_main, args=(world, _free_port(), results, mode), nprocs=world, join=True,
+                       start_method="spawn")
+    return dict(results)
+
+
+def _assert_all_equal_reference(results, world, ref_v, ref_i, ref_am):
+    rows = sorted((results[r][4], results[r][5]) for r in range(world))
+    assert rows == [(r * V // world, V // world) for r in range(world)]
+    for r in range(world):
+        status, v, i, am, _, _ = results[r]
+        assert status == "ok", r
+        assert np.array_equal(i.astype(np.uint32), ref_i), r
+        assert np.array_equal(v.view(np.uint32), ref_v.view(np.uint32)), r
+        assert am == ref_am, r
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_sharded_head_equals_unsharded_on_cpu_ranks(oracle, world):
     from q4k import synth
 
-    ctx = mp.get_context("spawn")
-    manager = ctx.Manager()
-    results = manager.dict()
-    mp.start_processes(_rank_main, args=(world, _free_port(), results), nprocs=world, join=True,
-                       start_method="spawn")
+    results = _run_ranks(world, "gemv")
     w = synth.q4k_matrix(V, N, SEED)
     x = synth.activations(1, N, SEED + 1)
     logits = oracle.logit_softcap(oracle.q4k_gemv(w, x, V, N)[0], CAP)
     ref_v, ref_i = oracle.topk256(logits)
+    _assert_all_equal_reference(results, world, ref_v, ref_i, oracle.argmax(logits))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_head_injected_ties_and_nan(oracle, world):
+    """Ties across shards (in one residue class, and for the global maximum)
+    and NaN rows: the merged candidates and argmax equal the unsharded
+    selection of shaders/topk256.wgsl / argmax.wgsl over the whole vector."""
+    logits = planted_logits(oracle, world)
+    ref_v, ref_i = oracle.topk256(logits)
     ref_am = oracle.argmax(logits)
-    rows = sorted((results[r][3], results[r][4]) for r in range(world))
-    assert rows == [(r * V // world, V // world) for r in range(world)]
-    for r in range(world):
-        v, i, am, _, _ = results[r]
-        assert np.array_equal(i.astype(np.uint32), ref_i), r
-        assert np.array_equal(v.view(np.uint32), ref_v.view(np.uint32)), r
-        assert am == ref_am, r
+    assert ref_i[7] == 7  # the lower index of the cross-shard tie
+    assert not np.isnan(logits[ref_am])
+    results = _run_ranks(world, "planted")
+    _assert_all_equal_reference(results, world, ref_v, ref_i, ref_am)
+
+
+def test_sharded_head_rank_failure_surfaces_as_error():
+    """Rank 1 raises before the all-gather: every other rank's collective
+    ends with an error (peer gone, or the process group's timeout) and none
+    reports a result."""
+    world = 4
+    results = _run_ranks(world, "fail")
+    assert results[1][0] == "error" and "injected shard failure" in results[1][1]
+    for r in (0, 2, 3):
+        assert results[r][0] == "error", (r, results[r][:1])
 
 
 def test_shard_range_rejects_split_residue_classes():

@@ -9,9 +9,6 @@ in a fresh process, where its first call does the per-device set-up.
 """
 from __future__ import annotations
 
-import ctypes
-
-import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
@@ -47,9 +44,12 @@ def test_static_lmhead_matches_context_entry_point(ctx):
         val, idx, am, logits = _run_static(L, w, x, V, N, 30.0)
         assert torch.equal(idx, ref.cand_idx), call
         assert torch.equal(am, ref.argmax), call
-        # same kernels on the same inputs: bit-identical, well inside the 1e-3 tolerance
-        np.testing.assert_allclose(val.cpu().numpy(), ref.cand_val.cpu().numpy(), rtol=1e-3, atol=0)
-        np.testing.assert_allclose(logits.cpu().numpy(), ref.logits.cpu().numpy(), rtol=1e-3, atol=1e-6)
+        # the same kernel on the same inputs: bit-identical values and logits
+        # (the contract's 1e-3 tolerance is therefore met with zero error)
+        assert torch.equal(val.view(torch.int32), ref.cand_val.view(torch.int32)), call
+        assert torch.equal(logits.view(torch.int32), ref.logits.view(torch.int32)), call
+        # no bounded wait expired in either call (read from the fixed array, no allocation)
+        assert L.q4k_check_static() == 0, call
 
 
 def test_static_lmhead_rejects_rows_past_its_scratch():
