@@ -1,0 +1,834 @@
+// The chained decode step: every GEMV of every layer of one token in ONE
+// persistent launch, each layer reading the previous layer's output.
+//
+// The reference encodes one token as a chain of passes per layer
+// (encodeTransformerPass, src/engine.ts:1538-1619):
+//   attn.rmsNorm -> q/k/v -> v norm -> attention -> linearOut -> postNormAdd
+//   -> ffn.rmsNorm -> gate/up -> geluMul -> linearDown -> postNormAdd
+// and then final.rmsNorm + the LM head (:1620-1626, 1686-1741).  The
+// matmul_quant dispatches are this repository's path; the elementwise passes
+// between them are restated here only so that the data really chains, with
+// the reference shaders' formulas and all norm weights 1 (synthetic weights
+// have none):
+//   rms_norm.wgsl        x / sqrt(sum(x^2)/N + eps)
+//   fused_norm_add.wgsl  residual + x / sqrt(sum(x^2)/N + eps)
+//   per_head_rms_norm_no_weight.wgsl on v, then the attention of a token at
+//   position 0: one cached key, softmax of one score = 1, so every query head
+//   outputs the (normalized) cached v of its KV head
+//   gelu_mul.wgsl        gelu_tanh(gate) * up
+// q and k are computed and stored (the reference caches k; at position 0
+// neither changes the attention output).
+//
+// Launch structure: one cooperative launch, one 16-warp CTA per SM.  The
+// step is a list of dependent stages (per layer: {q,k,v}, {o}, {gate,up},
+// {down}, then a final norm); a stage's GEMVs read one input vector that
+// every CTA prepares for itself in shared memory (the elementwise pass above
+// plus the engine's exact f16 hi/lo split) once the previous stage is
+// complete grid-wide.  Completion is a per-stage arrival counter in global
+// memory (release by the last thread of each CTA, bounded acquire polls by
+// every CTA).  The weights do not depend on the activations, so each warp's
+// TMA copy ring runs ahead across stage boundaries: while a CTA waits for the
+// previous stage, the weights of its next stage are already landing.
+//
+// Work split: a stage's 16-row tiles are spread over the CTAs in equal
+// contiguous ranges; inside a CTA, groups of ks warps take the range's tiles
+// in turn, each warp one 1/ks slice of the row's super-blocks (two per copy
+// stage), and the group's first warp adds the slices in order (ks chosen per
+// stage so every warp slice is a whole number of two-super-block stages).
+//
+// Every wait is bounded.  On expiry a CTA records it in the status word and
+// keeps walking the same control flow without waiting or computing, so every
+// hardware barrier is still met and every CTA exits; the last CTA to exit
+// puts the counters back to zero for the next run.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "q4k_ctx.cuh"
+#include "q4k_dequant.cuh"
+#include "q4k_device.cuh"
+#include "q4k_engine.cuh"
+#include "q4k_engine_math.cuh"
+#include "q4k_ptx.cuh"
+
+namespace q4k {
+namespace {
+
+constexpr uint32_t kChainWarps = 16;
+constexpr uint32_t kChainThreads = kChainWarps * 32;
+constexpr uint32_t kChainSlots = 2;                        // copy stages in flight per warp
+constexpr uint32_t kSlotBytes = kTileRows * kPairTileBytes;  // 16 rows x 2 super-blocks (+16 B)
+constexpr uint32_t kChainMaxN = 8192;                      // longest stage input
+constexpr uint32_t kGroupsPerThread = kChainMaxN / 8 / kChainThreads;  // 8-element groups per thread
+constexpr uint32_t kChainMaxLayers = 64;   // the stage and task tables fit shared memory
+// The kernel's dynamic shared-memory limit: the SM's 227 KB per CTA less
+// room for the kernel's static shared memory (about 1.2 KB).
+constexpr int kChainSmemMax = 225 * 1024;
+
+enum ChainPrep : uint32_t {
+  kPrepNorm = 0,           // x = rms_norm(a)
+  kPrepNormAddNorm = 1,    // v = a + rms_norm(b) (stored), x = rms_norm(v)
+  kPrepHeadNormBcast = 2,  // x[j] = rms_norm(a[0..hd))[j mod hd]
+  kPrepGelu = 3,           // x = gelu_tanh(a) * b (stored)
+};
+
+// One dependent stage of the chain.
+struct alignas(16) ChainStage {
+  uint32_t task0, ntasks;  // its GEMVs: tasks [task0, task0 + ntasks), all of input length N
+  uint32_t tiles;          // 16-row tiles over those tasks
+  uint32_t ks;             // warps per tile (K split)
+  uint32_t N;              // input length
+  uint32_t prep;           // ChainPrep
+  uint32_t hd;             // kPrepHeadNormBcast: elements of a (one head)
+  uint32_t pad;
+  const float* a;
+  const float* b;
+  float* store;       // the vector the prep stores (v, or gelu_mul's output), or null
+  float* store_norm;  // the prepared input itself, stored (the final norm: the LM head's input), or null
+};
+
+struct ChainArgs {
+  const EngineTask* tasks;
+  const ChainStage* stages;
+  uint32_t nstages, ntasks;
+  uint32_t* counters;  // [nstages + 1]: arrivals per stage, then exits
+  uint32_t* status;
+  uint32_t spin;
+  float eps;
+};
+
+// ---- small helpers -------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// A K-split group's hardware barrier (named barrier 1 + group).
+__device__ __forceinline__ void group_sync(uint32_t grp, uint32_t ks) {
+  asm volatile("bar.sync %0, %1;" ::"r"(grp + 1), "r"(ks * 32) : "memory");
+}
+
+// Sum, and sum + max, over the CTA in a fixed order (every CTA, given the
+// same data, gets the same bits).  red: 2 * kChainWarps floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = red[0];
+#pragma unroll
+  for (int i = 1; i < (int)kChainWarps; ++i) s += red[i];
+  return s;
+}
+
+__device__ __forceinline__ float2 block_sum_max(float v, float m, float* red) {
+  for (int o = 16; o > 0; o >>= 1) {
+    v += __shfl_xor_sync(0xffffffffu, v, o);
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    red[threadIdx.x >> 5] = v;
+    red[kChainWarps + (threadIdx.x >> 5)] = m;
+  }
+  __syncthreads();
+  float s = red[0], x = red[kChainWarps];
+#pragma unroll
+  for (int i = 1; i < (int)kChainWarps; ++i) {
+    s += red[i];
+    x = fmaxf(x, red[kChainWarps + i]);
+  }
+  return make_float2(s, x);
+}
+
+// Elements of 8-element group idx: k0..k0+3 and k0+32..k0+35 (the lane
+// order of the engine's activation fragments).
+__device__ __forceinline__ uint32_t group_k0(uint32_t idx) {
+  const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+  return 256u * b + 64u * c + 4u * w;
+}
+
+__device__ __forceinline__ void load8(const float* p, uint32_t k0, float (&v)[8]) {
+  const float4 lo = __ldcg(reinterpret_cast<const float4*>(p + k0));
+  const float4 hi = __ldcg(reinterpret_cast<const float4*>(p + k0 + 32));
+  v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+  v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+}
+
+__device__ __forceinline__ void store8(float* p, uint32_t k0, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p + k0) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + k0 + 32) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// The stage's input vector into the CTA's activation cache (batch 1: hi/lo
+// columns of the m16n8k16 B fragments, q4k_engine.cuh) and its 1/scale.
+// `owner`: this CTA stores the prep's vectors.  Every CTA computes the same
+// values in the same order.
+__device__ __noinline__ float chain_prep(const ChainStage& S, float eps, bool owner, uint4* frags, float* red) {
+  const uint32_t N = S.N, groups = N >> 3;
+  float v[kGroupsPerThread][8];
+  float ss = 0.0f, mx = 0.0f, n = (float)N;
+  if (S.prep == kPrepNormAddNorm) {
+    // v = a + b / rms(b)  (fused_norm_add.wgsl, weight 1), stored; a and b
+    // are loaded together so their latencies overlap
+    float b[kGroupsPerThread][8];
+#pragma unroll
+    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
+      const uint32_t idx = threadIdx.x + i * kChainThreads;
+      if (idx < groups) {
+        const uint32_t k0 = group_k0(idx);
+        load8(S.a, k0, v[i]);
+        load8(S.b, k0, b[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += b[i][j] * b[i][j];
+      }
+    }
+    const float rms_b = sqrtf(block_sum(ss, red) / n + eps);
+    ss = 0.0f;
+#pragma unroll
+    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
+      const uint32_t idx = threadIdx.x + i * kChainThreads;
+      if (idx < groups) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[i][j] = v[i][j] + b[i][j] / rms_b;
+          ss += v[i][j] * v[i][j];
+          mx = fmaxf(mx, fabsf(v[i][j]));
+        }
+        if (owner && S.store) store8(S.store, group_k0(idx), v[i]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
+      const uint32_t idx = threadIdx.x + i * kChainThreads;
+      if (idx < groups) {
+        const uint32_t k0 = group_k0(idx);
+        if (S.prep == kPrepGelu) {
+          float g[8], u[8];
+          load8(S.a, k0, g);
+          load8(S.b, k0, u);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = gelu_mul_value(g[j], u[j]);
+          if (owner && S.store) store8(S.store, k0, v[i]);
+        } else {
+          // kPrepNorm: a; kPrepHeadNormBcast: a[j mod hd] (a head dim that is
+          // a multiple of 256: a group never straddles a head)
+          load8(S.a, S.prep == kPrepHeadNormBcast ? k0 % S.hd : k0, v[i]);
+        }
+        // the norm's sum of squares: over a once (the first head copy)
+        if (S.prep == kPrepNorm || (S.prep == kPrepHeadNormBcast && k0 < S.hd))
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[i][j]));
+      }
+    }
+    if (S.prep == kPrepHeadNormBcast) n = (float)S.hd;
+  }
+  // one reduction for the norm's sum of squares and the largest |value|
+  const float2 red2 = block_sum_max(ss, mx, red);
+  float xmax = red2.y;
+  if (S.prep != kPrepGelu) {
+    // rms_norm.wgsl (weight 1): x / sqrt(sum(x^2)/n + eps); the largest |x|
+    // is the largest |v| divided the same way (division rounds monotonically)
+    const float rms = sqrtf(red2.x / n + eps);
+    xmax = xmax / rms;
+#pragma unroll
+    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
+      const uint32_t idx = threadIdx.x + i * kChainThreads;
+      if (idx < groups) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] / rms;
+        if (owner && S.store_norm) store8(S.store_norm, group_k0(idx), v[i]);
+      }
+    }
+  }
+  const float2 sc = token_scale(xmax);
+  // the scaled hi/lo split in the fragment order (batch 1: columns hi, lo)
+#pragma unroll
+  for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
+    const uint32_t idx = threadIdx.x + i * kChainThreads;
+    if (idx < groups) {
+      const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+      uint16_t hh[8], hl[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float x = v[i][j] * sc.x;
+        const __half h = __float2half_rn(x);
+        hh[j] = __half_as_ushort(h);
+        hl[j] = __half_as_ushort(__float2half_rn(x - __half2float(h)));
+      }
+      uint4* dst = frags + (size_t)(b * 8 + w) * 8;
+      dst[c] = make_uint4(hh[0] | ((uint32_t)hh[2] << 16), hh[1] | ((uint32_t)hh[3] << 16),
+                          hh[4] | ((uint32_t)hh[6] << 16), hh[5] | ((uint32_t)hh[7] << 16));
+      dst[4 + c] = make_uint4(hl[0] | ((uint32_t)hl[2] << 16), hl[1] | ((uint32_t)hl[3] << 16),
+                              hl[4] | ((uint32_t)hl[6] << 16), hl[5] | ((uint32_t)hl[7] << 16));
+    }
+  }
+  return sc.y;
+}
+
+// The stage and task tables as every CTA keeps them in shared memory (the
+// copy walk consults them at every copy stage).
+struct alignas(16) StageRec {
+  uint32_t task0, ntasks, tiles, ks, N, pad[3];
+};
+struct alignas(16) TaskRec {
+  const CUtensorMap* tmap;
+  float* y;
+  uint32_t M, item_begin, item_end, pad;
+};
+
+struct Tables {
+  const StageRec* st;
+  const TaskRec* tk;
+  uint32_t nstages;
+};
+
+// A warp's walk over its copy stages: stage s, tile, super-block; the same
+// order the warp's math consumes them.
+struct Walk {
+  uint32_t s, tile, sb;              // position
+  uint32_t c1, ngrp_step, sb0, sb1;  // current stage: range end, tile step, slice bounds
+  uint32_t issued;                   // copy stages issued so far
+  bool done;
+};
+
+__device__ __forceinline__ bool stage_slice(const StageRec& S, uint32_t warp, uint32_t& grp, uint32_t& q,
+                                            uint32_t& ngrp) {
+  if (S.ntasks == 0) return false;
+  ngrp = kChainWarps / S.ks;
+  if (warp >= ngrp * S.ks) return false;
+  grp = warp / S.ks;
+  q = warp % S.ks;
+  return true;
+}
+
+__device__ __forceinline__ void tile_range(const StageRec& S, uint32_t& c0, uint32_t& c1) {
+  c0 = (uint32_t)(((uint64_t)blockIdx.x * S.tiles) / gridDim.x);
+  c1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * S.tiles) / gridDim.x);
+}
+
+// Position the walk at the first copy stage of stage >= s.
+__device__ void walk_seek(Walk& W, const Tables& tb, uint32_t warp, uint32_t s) {
+  for (; s < tb.nstages; ++s) {
+    const StageRec& S = tb.st[s];
+    uint32_t grp, q, ngrp, c0, c1;
+    if (!stage_slice(S, warp, grp, q, ngrp)) continue;
+    tile_range(S, c0, c1);
+    if (c0 + grp >= c1) continue;
+    const uint32_t nbs = (S.N >> 8) / S.ks;
+    W.s = s;
+    W.tile = c0 + grp;
+    W.c1 = c1;
+    W.ngrp_step = ngrp;
+    W.sb0 = q * nbs;
+    W.sb1 = W.sb0 + nbs;
+    W.sb = W.sb0;
+    W.done = false;
+    return;
+  }
+  W.done = true;
+}
+
+__device__ __forceinline__ void walk_next(Walk& W, const Tables& tb, uint32_t warp) {
+  W.sb += 2;
+  if (W.sb < W.sb1) return;
+  W.tile += W.ngrp_step;
+  if (W.tile < W.c1) {
+    W.sb = W.sb0;
+    return;
+  }
+  walk_seek(W, tb, warp, W.s + 1);
+}
+
+// The task of stage tile `tile` (tasks of one stage are few) and the tile's first row.
+__device__ __forceinline__ const TaskRec& tile_task(const Tables& tb, const StageRec& S, uint32_t tile,
+                                                    uint32_t& row0) {
+  uint32_t t = S.task0;
+  while (t + 1 < S.task0 + S.ntasks && tile >= tb.tk[t].item_end) ++t;
+  const TaskRec& T = tb.tk[t];
+  row0 = (tile - T.item_begin) * kTileRows;
+  return T;
+}
+
+// Lane 0: copy the walk's current stage into `slot`, then advance the walk.
+__device__ __forceinline__ void walk_issue(Walk& W, const Tables& tb, uint32_t warp, uint8_t* slot_mem,
+                                           uint64_t* bar) {
+  uint32_t row0;
+  const TaskRec& T = tile_task(tb, tb.st[W.s], W.tile, row0);
+  mbar_arrive_expect_tx(bar, kSlotBytes);
+  tma_tile_g2s(slot_mem, T.tmap, W.sb * (kBlockBytes / 4), row0, bar);
+  walk_next(W, tb, warp);
+}
+
+// Shared-memory layout of the chain kernel (after 128-byte alignment).
+constexpr size_t kRingBytes = (size_t)kChainWarps * kChainSlots * kSlotBytes;
+constexpr size_t kXcacheBytes = 4 * (size_t)kChainMaxN;  // batch 1: 4 bytes per element
+constexpr size_t kPartBytes = (size_t)2 * kChainWarps * kTileRows * 4;
+constexpr size_t kTablesOff = kRingBytes + kXcacheBytes + kPartBytes;
+
+__global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainArgs A) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  __shared__ uint64_t s_bar[kChainWarps][kChainSlots];
+  __shared__ float s_red[2 * kChainWarps];
+  __shared__ uint32_t s_fail;
+  __shared__ ChainStage s_stage;  // the record of the stage being prepared
+  __shared__ Walk s_walk[kChainWarps];  // each warp's copy walk (lane 0's; kept out of registers)
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t g = lane >> 2, c = lane & 3u;
+  const uint32_t bsel = scale_sel(c);
+  const uint32_t spin = spin_or_default(A.spin);
+  uint8_t* ring = smem + warp * (kChainSlots * kSlotBytes);
+  uint4* xsm = reinterpret_cast<uint4*>(smem + kRingBytes);
+  float* s_part = reinterpret_cast<float*>(smem + kRingBytes + kXcacheBytes);
+  StageRec* s_st = reinterpret_cast<StageRec*>(smem + kTablesOff);
+  TaskRec* s_tk = reinterpret_cast<TaskRec*>(smem + kTablesOff + sizeof(StageRec) * A.nstages);
+  uint64_t* bars = s_bar[warp];
+
+  // the stage and task tables into shared memory
+  for (uint32_t i = threadIdx.x; i < A.nstages; i += kChainThreads) {
+    const ChainStage& G = A.stages[i];
+    s_st[i] = StageRec{G.task0, G.ntasks, G.tiles, G.ks, G.N, {0, 0, 0}};
+  }
+  for (uint32_t i = threadIdx.x; i < A.ntasks; i += kChainThreads) {
+    const EngineTask& G = A.tasks[i];
+    s_tk[i] = TaskRec{G.tmap, G.y, G.M, G.item_begin, G.item_end, 0};
+  }
+  if (lane == 0)
+    for (uint32_t i = 0; i < kChainSlots; ++i) mbar_init(&bars[i], 1);
+  if (threadIdx.x == 0) {
+    s_fail = 0;
+    s_stage = A.stages[0];
+  }
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncthreads();
+  const Tables tb{s_st, s_tk, A.nstages};
+
+  // lane 0: start this warp's copy walk (the first two copy stages)
+  if (lane == 0) {
+    Walk W;
+    W.issued = 0;
+    walk_seek(W, tb, warp, 0);
+    for (uint32_t i = 0; i < kChainSlots && !W.done; ++i) {
+      walk_issue(W, tb, warp, ring + i * kSlotBytes, &bars[i]);
+      ++W.issued;
+    }
+    s_walk[warp] = W;
+  }
+  // B-fragment column of this lane (batch 1: hi, lo stored; any stored column serves)
+  const uint32_t lane_off = ((g & 1u) * 4u + c) * 16u;
+  uint32_t consumed = 0;  // copy stages this warp has waited for (and consumed)
+  bool failed = false;    // this warp gave up a wait: walk on without waiting or computing
+
+  for (uint32_t s = 0; s < A.nstages; ++s) {
+    // the previous stage is complete grid-wide (bounded), then this CTA prepares the input
+    if (s > 0) {
+      if (threadIdx.x == 0 && !s_fail) {
+        bool ok = false;
+        for (uint32_t i = 0; i < spin && !ok; ++i) ok = ld_acquire_gpu(&A.counters[s - 1]) >= gridDim.x;
+        if (!ok) s_fail = 1;
+      }
+      __syncthreads();
+    }
+    const bool owner = blockIdx.x == s % gridDim.x;
+    const float inv = chain_prep(s_stage, A.eps, owner, xsm, s_red);
+    __syncthreads();
+    // the next stage's record, loaded while this stage computes
+    if (threadIdx.x == 0 && s + 1 < A.nstages) s_stage = A.stages[s + 1];
+    const StageRec& R = tb.st[s];
+    if (R.ntasks == 0) break;  // the final norm: nothing to multiply
+    if (s_fail) failed = true;
+
+    uint32_t grp, q, ngrp, c0, c1;
+    if (stage_slice(R, warp, grp, q, ngrp)) {
+      tile_range(R, c0, c1);
+      const uint32_t nbs = (R.N >> 8) / R.ks;
+      // tile_iter: the group's tile count in this stage (the same in all its
+      // warps), whose parity picks the partial-sum buffer
+      uint32_t tile_iter = 0;
+      for (uint32_t tile = c0 + grp; tile < c1; tile += ngrp, ++tile_iter) {
+        float acc[1][2][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) acc[0][h][0] = acc[0][h][1] = acc[0][h][2] = acc[0][h][3] = 0.0f;
+        for (uint32_t b = q * nbs; b < (q + 1) * nbs; b += 2) {
+          if (failed) continue;
+          const uint32_t slot = consumed % kChainSlots;
+          // the whole warp agrees on the outcome of the (bounded) wait
+          if (!__all_sync(0xffffffffu, mbar_wait(&bars[slot], (consumed / kChainSlots) & 1u, spin))) {
+            failed = true;
+            continue;
+          }
+          ++consumed;
+          const uint8_t* stg = ring + slot * kSlotBytes;
+          const uint32_t wstep[1] = {128u};
+#pragma unroll
+          for (uint32_t j = 0; j < 2; ++j) {
+            const BlockRegs R = read_block(stg + g * kPairTileBytes + j * kBlockBytes,
+                                           stg + (g + 8) * kPairTileBytes + j * kBlockBytes, c);
+            if (j == 1) {
+              // the whole slot is in registers: hand it back to the copy walk
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0 && !s_walk[warp].done) {
+                Walk W = s_walk[warp];
+                walk_issue(W, tb, warp, ring + slot * kSlotBytes, &bars[slot]);
+                ++W.issued;
+                s_walk[warp] = W;
+              }
+            }
+            const uint8_t* base[1] = {reinterpret_cast<const uint8_t*>(xsm) + (b + j) * 1024u + lane_off};
+            block_math<1, 2, true>(acc, R, c, bsel, base, wstep);
+          }
+        }
+        // row g / g+8 of the tile: (hi, lo) columns of token 0 sit in the c == 0 lanes
+        const float pa = (acc[0][0][0] + acc[0][1][0]) + (acc[0][0][1] + acc[0][1][1]);
+        const float pb = (acc[0][0][2] + acc[0][1][2]) + (acc[0][0][3] + acc[0][1][3]);
+        uint32_t row0;
+        const TaskRec& T = tile_task(tb, R, tile, row0);
+        const uint32_t ra = row0 + g, rb = ra + 8;
+        if (R.ks > 1) {
+          // the group's slices, added in slice order by its first warp
+          float* part = s_part + (((tile_iter & 1u) * kChainWarps + warp) * kTileRows);
+          if (c == 0) {
+            part[g] = pa;
+            part[g + 8] = pb;
+          }
+          group_sync(grp, R.ks);
+          if (q == 0 && c == 0) {
+            const float* all = s_part + (((tile_iter & 1u) * kChainWarps + grp * R.ks) * kTileRows);
+            float sa = all[g], sb = all[g + 8];
+            for (uint32_t k = 1; k < R.ks; ++k) {
+              sa += all[k * kTileRows + g];
+              sb += all[k * kTileRows + g + 8];
+            }
+            if (!failed) {
+              if (ra < T.M) T.y[ra] = sa * inv;
+              if (rb < T.M) T.y[rb] = sb * inv;
+            }
+          }
+        } else if (c == 0 && !failed) {
+          if (ra < T.M) T.y[ra] = pa * inv;
+          if (rb < T.M) T.y[rb] = pb * inv;
+        }
+      }
+    }
+    // this CTA's part of stage s is stored: arrive
+    __syncthreads();
+    if (failed) atomicOr(&s_fail, 1u);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(&A.counters[s], 1u);
+    }
+  }
+
+  // drain: every copy issued and not consumed lands before the CTA exits (bounded)
+  if (lane == 0)
+    for (uint32_t j = consumed; j < s_walk[warp].issued; ++j)
+      mbar_wait(&bars[j % kChainSlots], (j / kChainSlots) & 1u, spin);
+  if (failed) atomicOr(&s_fail, 1u);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (s_fail) atomicOr(A.status, 1u);
+    // the last CTA out puts every counter back to zero for the next run
+    __threadfence();
+    if (atomicAdd(&A.counters[A.nstages], 1u) == gridDim.x - 1) {
+      for (uint32_t i = 0; i <= A.nstages; ++i) A.counters[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+// Dynamic shared memory of a chain of `nstages` stages and `ntasks` GEMVs.
+size_t chain_smem(uint32_t nstages, uint32_t ntasks) {
+  return 128 + kTablesOff + sizeof(StageRec) * nstages + sizeof(TaskRec) * ntasks;
+}
+
+
+// Warps per tile for rows of nb super-blocks: the most that still gives each
+// warp a whole number of two-super-block copy stages (largest parallelism:
+// the chain's stages are latency-bound).
+uint32_t choose_ks(uint32_t nb) {
+  uint32_t best = 0;
+  for (uint32_t ks = 1; ks <= kChainWarps; ++ks)
+    if (nb % ks == 0 && (nb / ks) % 2 == 0) best = ks;
+  return best;
+}
+
+}  // namespace
+}  // namespace q4k
+
+using namespace q4k;
+
+struct q4k_chain {
+  q4k_ctx* ctx = nullptr;
+  void* mem = nullptr;  // tasks, maps, stages, counters
+  const EngineTask* tasks = nullptr;
+  const ChainStage* stages = nullptr;
+  uint32_t* counters = nullptr;
+  uint32_t nstages = 0, ntasks = 0, grid = 0;
+  size_t smem = 0;  // dynamic shared memory of the launch
+  float eps = 1e-6f;
+  // optional LM head on the final norm
+  bool has_head = false;
+  const void* head_w = nullptr;
+  CUtensorMap head_map;
+  uint32_t head_tile_bytes = 0, V = 0, hidden = 0;
+  float cap = 0.0f;
+  float* normed = nullptr;
+  float* cand_val = nullptr;
+  uint32_t* cand_idx = nullptr;
+  uint32_t* argmax = nullptr;
+};
+
+extern "C" {
+
+int q4k_chain_create(q4k_ctx* ctx, uint32_t layers, uint32_t hidden, uint32_t q_dim, uint32_t kv_dim, uint32_t ffn,
+                     float eps, const q4k_chain_layer* per_layer, const float* h_in, float* normed_out,
+                     q4k_chain** out) {
+  if (!ctx || !out || !per_layer || !h_in || !normed_out) return Q4K_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (layers == 0 || layers > kChainMaxLayers)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "layers=%u outside 1..%u", layers, kChainMaxLayers);
+  const uint32_t dims[4] = {hidden, q_dim, kv_dim, ffn};
+  for (uint32_t d : dims)
+    if (d == 0 || d % 256 != 0 || d > kChainMaxN)
+      return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "dimension %u is not a multiple of 256 in [256, %u]", d, kChainMaxN);
+  if (q_dim % kv_dim != 0)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "q_dim %u is not a multiple of the head dim %u", q_dim, kv_dim);
+  for (uint32_t n : {hidden, q_dim, ffn})
+    if (!choose_ks(n / 256))
+      return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "rows of %u super-blocks do not split into whole copy stages", n / 256);
+  if (!aligned16(h_in) || !aligned16(normed_out)) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "unaligned vector");
+  for (uint32_t l = 0; l < layers; ++l) {
+    const q4k_chain_layer& L = per_layer[l];
+    const void* ptrs[] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd, L.q,      L.k,
+                          L.v,  L.o,  L.g,  L.u,  L.act, L.d, L.h_attn, L.h_out};
+    for (const void* p : ptrs)
+      if (!p || !aligned16(p)) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "layer %u: null or unaligned pointer", l);
+  }
+  // stages and tasks, layer by layer
+  std::vector<ChainStage> st;
+  std::vector<EngineTask> tasks;
+  struct Mat {
+    const void* w;
+    float* y;
+    uint32_t M, N;
+  };
+  auto add_stage = [&](std::initializer_list<Mat> mats, uint32_t N, uint32_t prep, const float* a, const float* b,
+                       float* store, float* store_norm, uint32_t hd) {
+    ChainStage S{};
+    S.task0 = (uint32_t)tasks.size();
+    S.N = N;
+    S.prep = prep;
+    S.hd = hd;
+    S.a = a;
+    S.b = b;
+    S.store = store;
+    S.store_norm = store_norm;
+    S.ks = choose_ks(N / 256);
+    for (const Mat& m : mats) {
+      EngineTask t{};
+      t.w = static_cast<const uint8_t*>(m.w);
+      t.y = m.y;
+      t.M = m.M;
+      t.N = m.N;
+      t.item_begin = S.tiles;
+      S.tiles += tiles_of(m.M);
+      t.item_end = S.tiles;
+      tasks.push_back(t);
+    }
+    S.ntasks = (uint32_t)mats.size();
+    st.push_back(S);
+  };
+  for (uint32_t l = 0; l < layers; ++l) {
+    const q4k_chain_layer& L = per_layer[l];
+    // attn.rmsNorm (layer 0), or the previous layer's ffn.postNormAdd + this layer's attn.rmsNorm
+    if (l == 0)
+      add_stage({{L.wq, L.q, q_dim, hidden}, {L.wk, L.k, kv_dim, hidden}, {L.wv, L.v, kv_dim, hidden}}, hidden,
+                kPrepNorm, h_in, nullptr, nullptr, nullptr, 0);
+    else
+      add_stage({{L.wq, L.q, q_dim, hidden}, {L.wk, L.k, kv_dim, hidden}, {L.wv, L.v, kv_dim, hidden}}, hidden,
+                kPrepNormAddNorm, per_layer[l - 1].h_attn, per_layer[l - 1].d, per_layer[l - 1].h_out, nullptr, 0);
+    // v norm + attention at position 0 -> linearOut
+    add_stage({{L.wo, L.o, hidden, q_dim}}, q_dim, kPrepHeadNormBcast, L.v, nullptr, nullptr, nullptr, kv_dim);
+    // attn.postNormAdd + ffn.rmsNorm -> gate, up
+    add_stage({{L.wg, L.g, ffn, hidden}, {L.wu, L.u, ffn, hidden}}, hidden, kPrepNormAddNorm,
+              l == 0 ? h_in : per_layer[l - 1].h_out, L.o, L.h_attn, nullptr, 0);
+    // geluMul -> linearDown
+    add_stage({{L.wd, L.d, hidden, ffn}}, ffn, kPrepGelu, L.g, L.u, L.act, nullptr, 0);
+  }
+  // the last ffn.postNormAdd + final.rmsNorm: the LM head's input
+  add_stage({}, hidden, kPrepNormAddNorm, per_layer[layers - 1].h_attn, per_layer[layers - 1].d,
+            per_layer[layers - 1].h_out, normed_out, 0);
+
+  q4k_chain* ch = new q4k_chain();
+  ch->ctx = ctx;
+  ch->eps = eps;
+  ch->nstages = (uint32_t)st.size();
+  ch->grid = (uint32_t)ctx->sm_count;
+  ch->normed = normed_out;
+  ch->hidden = hidden;
+  const size_t maps_bytes = sizeof(CUtensorMap) * tasks.size();
+  const size_t tasks_off = (maps_bytes + 255) / 256 * 256;
+  const size_t stages_off = tasks_off + (sizeof(EngineTask) * tasks.size() + 255) / 256 * 256;
+  const size_t counters_off = stages_off + (sizeof(ChainStage) * st.size() + 255) / 256 * 256;
+  const size_t total = counters_off + 4 * (st.size() + 1);
+  cudaError_t e = cudaSetDevice(ctx->device);
+  if (e == cudaSuccess) e = cudaMalloc(&ch->mem, total);
+  if (e != cudaSuccess) {
+    delete ch;
+    return ctx_cuda(ctx, e, "q4k_chain_create allocation");
+  }
+  char* base = static_cast<char*>(ch->mem);
+  CUtensorMap* maps_dev = reinterpret_cast<CUtensorMap*>(base);
+  std::vector<CUtensorMap> maps(tasks.size());
+  for (size_t i = 0; i < tasks.size(); ++i) {
+    e = encode_weight_map(&maps[i], tasks[i].w, tasks[i].M, tasks[i].N, &tasks[i].tile_bytes);
+    if (e == cudaSuccess && tasks[i].tile_bytes != kPairTileBytes) e = cudaErrorInvalidValue;
+    if (e != cudaSuccess) {
+      cudaFree(ch->mem);
+      delete ch;
+      return ctx_cuda(ctx, e, "q4k_chain_create weight tensor map");
+    }
+    tasks[i].tmap = maps_dev + i;
+  }
+  ch->tasks = reinterpret_cast<const EngineTask*>(base + tasks_off);
+  ch->stages = reinterpret_cast<const ChainStage*>(base + stages_off);
+  ch->counters = reinterpret_cast<uint32_t*>(base + counters_off);
+  e = cudaMemcpy(maps_dev, maps.data(), maps_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(base + tasks_off, tasks.data(), sizeof(EngineTask) * tasks.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(base + stages_off, st.data(), sizeof(ChainStage) * st.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(ch->counters, 0, 4 * (st.size() + 1));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(ch->mem);
+    delete ch;
+    return ctx_cuda(ctx, e, "q4k_chain_create upload");
+  }
+  // the launch must fit one CTA per SM for every CTA to be resident (cooperative launch)
+  static std::atomic<uint8_t> attr_set[kAttrDevices];
+  ch->ntasks = (uint32_t)tasks.size();
+  ch->smem = chain_smem(ch->nstages, ch->ntasks);
+  if (ch->smem > (size_t)kChainSmemMax) {
+    const size_t need = ch->smem;
+    cudaFree(ch->mem);
+    delete ch;
+    return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "the chain's tables need %zu bytes of shared memory", need);
+  }
+  e = smem_attr_once(attr_set, ctx->device, chain_kernel, (int)kChainSmemMax);
+  int per_sm = 0;
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kChainThreads, ch->smem);
+  if (e != cudaSuccess || per_sm < 1) {
+    cudaFree(ch->mem);
+    delete ch;
+    return e != cudaSuccess ? ctx_cuda(ctx, e, "q4k_chain_create occupancy")
+                            : ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "the chain kernel does not fit an SM");
+  }
+  *out = ch;
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
+int q4k_chain_lmhead(q4k_chain* ch, const void* w, uint32_t V, float cap, float* cand_val, uint32_t* cand_idx,
+                     uint32_t* argmax) {
+  if (!ch) return Q4K_ERR_INVALID_ARG;
+  q4k_ctx* ctx = ch->ctx;
+  if (!w || !cand_val || !cand_idx || !argmax) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "null pointer");
+  if (V == 0 || V >= (1u << 31)) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "V=%u out of range", V);
+  if (!aligned16(w)) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "LM head weights must be 16-byte aligned");
+  if (xfrag_bytes(ch->hidden, 1) > engine_xcache_bytes(true))
+    return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "hidden=%u exceeds the engine's activation cache", ch->hidden);
+  cudaError_t e = encode_weight_map(&ch->head_map, w, V, ch->hidden, &ch->head_tile_bytes);
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_chain_lmhead weight tensor map");
+  ch->has_head = true;
+  ch->head_w = w;
+  ch->V = V;
+  ch->cap = cap;
+  ch->cand_val = cand_val;
+  ch->cand_idx = cand_idx;
+  ch->argmax = argmax;
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
+int q4k_chain_run(q4k_chain* ch, void* stream) {
+  if (!ch) return Q4K_ERR_INVALID_ARG;
+  q4k_ctx* ctx = ch->ctx;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ChainArgs A;
+  A.tasks = ch->tasks;
+  A.stages = ch->stages;
+  A.nstages = ch->nstages;
+  A.ntasks = ch->ntasks;
+  A.counters = ch->counters;
+  A.status = ctx->select.status;
+  A.spin = ctx->select.spin_limit;
+  A.eps = ch->eps;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ch->grid);
+  cfg.blockDim = dim3(kChainThreads);
+  cfg.dynamicSmemBytes = ch->smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, chain_kernel, A);
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_chain_run launch");
+  if (ch->has_head) {
+    // the fused LM head (q4k_lmhead_select's launch) on the final norm
+    TaskList tl{};
+    tl.n = 1;
+    tl.prep = 1;
+    tl.inl_job.x = ch->normed;
+    tl.inl_job.xfrag = ctx->xfrag;
+    tl.inl_job.inv_scale = ctx->inv_scale;
+    tl.inl_job.N = ch->hidden;
+    tl.inl.w = static_cast<const uint8_t*>(ch->head_w);
+    tl.inl.xfrag = ctx->xfrag;
+    tl.inl.inv_scale = ctx->inv_scale;
+    tl.inl.cand_val = ch->cand_val;
+    tl.inl.cand_idx = ch->cand_idx;
+    tl.inl.argmax = ch->argmax;
+    tl.inl.M = ch->V;
+    tl.inl.N = ch->hidden;
+    tl.inl.item_begin = 0;
+    tl.inl.item_end = tiles_of(ch->V);
+    tl.inl.kind = kTaskSelect;
+    tl.inl.cap = ch->cap;
+    tl.inl.tile_bytes = ch->head_tile_bytes;
+    tl.total_items = tiles_of(ch->V);
+    tl.total_cost = tiles_of(ch->V) * item_cost(ch->hidden, kTaskSelect);
+    tl.pairs = pairs_of(ch->hidden, 0, ch->head_tile_bytes) ? 1u : 0u;
+    e = launch_engine(tl, ch->head_map, 1, true, ctx->select, ctx->sm_count, s);
+    if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_chain_run LM head launch");
+  }
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
+int q4k_chain_launches(const q4k_chain* ch) { return ch ? 1 + (ch->has_head ? 1 : 0) : -1; }
+
+void q4k_chain_destroy(q4k_chain* ch) {
+  if (!ch) return;
+  if (ch->mem) {
+    cudaSetDevice(ch->ctx->device);
+    cudaFree(ch->mem);
+  }
+  delete ch;
+}
+
+}  // extern "C"

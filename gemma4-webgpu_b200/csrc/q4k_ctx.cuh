@@ -63,4 +63,43 @@ constexpr uint32_t kGemmMinRows = 64;
 int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
              cudaStream_t s, uint32_t parts = 2);
 
+// ---- multi-matrix GEMM launches (plans with batch >= kGemmMinRows) ------------
+// Every matrix of a plan stage runs in ONE gemm_kernel launch whose CTAs each
+// take one tile (256 weight rows x a token tile) from a host-made tile table,
+// after one preparation launch has turned every distinct activation of the
+// stage (x, or gelu_mul(gate, up)) into its B operand.
+
+// One matrix: y[t][m] = sum_k w16[m][k] x[t][k] for t < T, m < M.
+struct alignas(16) GemmTask {
+  const CUtensorMap* amap;  // the raw Q4_K matrix (gemm_weight_map), device memory
+  const CUtensorMap* bmap;  // its activation operand (gemm_operand_map), device memory
+  float* y;                 // [T][M]
+  const float* inv_scale;   // [T]: 1/scale of each activation row (the operand's)
+  uint32_t M, N, T;
+  uint32_t tile_tokens;     // activation rows per tile (gemm_tile_tokens)
+};
+
+// One activation operand: mode 0 from x [T][N]; mode 1 gelu_mul(gate, up)
+// [T][N] (shaders/gelu_mul.wgsl), stored to act when act != null.
+struct alignas(16) GemmJob {
+  const float* x;
+  const float* gate;
+  const float* up;
+  float* act;
+  void* operand;     // f16 [parts*T][N] in the weight tiles' K order
+  float* inv_scale;  // [T]
+  uint32_t N, mode;
+};
+
+// Activation rows per token tile of a multi-matrix launch (full 256-operand-row tiles).
+uint32_t gemm_tile_tokens(uint32_t parts);
+// Rows of the weight-row tile (the A operand's M per CTA).
+uint32_t gemm_tile_rows();
+size_t gemm_operand_bytes(uint32_t N, uint32_t T, uint32_t parts);
+cudaError_t gemm_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N);
+cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, uint32_t T, uint32_t parts);
+cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, cudaStream_t s);
+cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts, int device,
+                              uint32_t* status, uint32_t spin, cudaStream_t s);
+
 }  // namespace q4k

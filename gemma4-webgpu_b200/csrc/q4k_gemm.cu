@@ -128,6 +128,8 @@ struct GemmArgs {
   uint32_t parts;          // operand rows per activation row: 2 (exact f16 hi + lo) or 1 (f16 only)
   uint32_t* status;        // bit 0: a bounded wait expired
   uint32_t spin;           // polls per bounded wait (0: kSpinLimit)
+  const GemmTask* tasks;   // multi-matrix launch: task table (null: the single matrix above)
+  const uint2* tiles;      // multi-matrix launch: CTA b's tile = (task, row tile | token tile << 16)
 };
 
 // The raw Q4_K bytes one A-producer thread (one row) needs for one K step:
@@ -179,12 +181,35 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   __shared__ uint32_t s_tmem;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  const uint32_t row0 = blockIdx.x * kGRows, tok0 = blockIdx.y * a.tile_tokens;
-  const uint32_t ntok = min(a.tile_tokens, a.T - tok0);
-  const uint32_t b_bytes = a.parts * a.tile_tokens * kGK * 2;  // one B box
+  // This CTA's tile: of the single matrix (grid = row tiles x token tiles),
+  // or one entry of a multi-matrix launch's tile table.
+  const CUtensorMap* pamap = &amap;
+  const CUtensorMap* pbmap = &bmap;
+  float* y = a.y;
+  const float* inv_scale = a.inv_scale;
+  uint32_t M = a.M, N = a.N, T = a.T, tile_tokens = a.tile_tokens, row0, tok0;
+  if (a.tiles) {
+    const uint2 tl = a.tiles[blockIdx.x];
+    const GemmTask& tk = a.tasks[tl.x];
+    pamap = tk.amap;
+    pbmap = tk.bmap;
+    y = tk.y;
+    inv_scale = tk.inv_scale;
+    M = tk.M;
+    N = tk.N;
+    T = tk.T;
+    tile_tokens = tk.tile_tokens;
+    row0 = (tl.y & 0xffffu) * kGRows;
+    tok0 = (tl.y >> 16) * tile_tokens;
+  } else {
+    row0 = blockIdx.x * kGRows;
+    tok0 = blockIdx.y * tile_tokens;
+  }
+  const uint32_t ntok = min(tile_tokens, T - tok0);
+  const uint32_t b_bytes = a.parts * tile_tokens * kGK * 2;  // one B box
   // MMA N: the tile's operand rows, a multiple of 16
   const uint32_t n_mma = a.parts == 2 ? 2u * ((ntok + 7u) & ~7u) : ((ntok + 15u) & ~15u);
-  const uint32_t ksteps = a.N / kGK;
+  const uint32_t ksteps = N / kGK;
   bool failed = false;
 
   if (threadIdx.x == 0) {
@@ -222,7 +247,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
           break;
         }
         mbar_arrive_expect_tx(&full_b[s], b_bytes);
-        tma_tile_g2s(sB + s * kGBBytes, &bmap, ks * kGK, a.parts * tok0, &full_b[s]);
+        tma_tile_g2s(sB + s * kGBBytes, pbmap, ks * kGK, a.parts * tok0, &full_b[s]);
         ++issued;
       }
       // every issued copy has landed before the CTA can exit
@@ -306,13 +331,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
 #pragma unroll
           for (uint32_t t = 0; t < 16; ++t) {
             const uint32_t tok = tok0 + c0 / 2 + t;
-            if (tok < a.T && erow < a.M) a.y[(size_t)tok * a.M + erow] = (v[2 * t] + v[2 * t + 1]) * a.inv_scale[tok];
+            if (tok < T && erow < M) y[(size_t)tok * M + erow] = (v[2 * t] + v[2 * t + 1]) * inv_scale[tok];
           }
         } else {
 #pragma unroll
           for (uint32_t t = 0; t < 32; ++t) {
             const uint32_t tok = tok0 + c0 + t;
-            if (tok < a.T && erow < a.M) a.y[(size_t)tok * a.M + erow] = v[t] * a.inv_scale[tok];
+            if (tok < T && erow < M) y[(size_t)tok * M + erow] = v[t] * inv_scale[tok];
           }
         }
       }
@@ -321,7 +346,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     // raw-weight copy warp: super-block column sb of the tile's 256 rows (one
     // 144-byte box per row) into raw stage sb % 2, once the producers have
     // taken the column that stage held
-    const uint32_t nb = a.N >> 8;
+    const uint32_t nb = N >> 8;
     uint32_t issued = 0;
     for (uint32_t sb = 0; sb < nb; ++sb) {
       const uint32_t rs = sb % kGRawStages, use = sb / kGRawStages;
@@ -330,7 +355,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         break;
       }
       mbar_arrive_expect_tx(&raw_full[rs], kGRawBytes);
-      tma_tile_g2s(sRaw + rs * kGRawBytes, &amap, sb * (kBlockBytes / 4), row0, &raw_full[rs]);
+      tma_tile_g2s(sRaw + rs * kGRawBytes, pamap, sb * (kBlockBytes / 4), row0, &raw_full[rs]);
       ++issued;
     }
     // every issued copy has landed before the CTA can exit
@@ -375,6 +400,43 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const float* x, __half*
   __half* lo = hi + N;
   for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) {
     const float v = xr[(k & ~7u) | chunk_elem(k & 7u)] * s;  // the A tiles' K order
+    const __half hv = __float2half_rn(v);
+    hi[k] = hv;
+    if (parts == 2) lo[k] = __float2half_rn(v - __half2float(hv));
+  }
+}
+
+// The same for the jobs of a multi-matrix launch: CTA j*T + t prepares
+// token t of job j (x, or gelu_mul of gate and up, stored to act on the way).
+__global__ void __launch_bounds__(256) gemm_prep_kernel(const GemmJob* jobs, uint32_t T, uint32_t parts) {
+  __shared__ float s_red[8];
+  const GemmJob J = jobs[blockIdx.x / T];
+  const uint32_t t = blockIdx.x % T, N = J.N;
+  const size_t base = (size_t)t * N;
+  auto value = [&](size_t i) { return J.mode ? gelu_mul_value(J.gate[i], J.up[i]) : J.x[i]; };
+  float mx = 0.0f;
+  for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) {
+    const float v = value(base + k);
+    if (J.mode && J.act) J.act[base + k] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = s_red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, s_red[i]);
+  int e = 0, sexp = 0;
+  if (mx > 0.0f && mx <= 3.402823466e38f) {
+    frexpf(mx, &e);
+    sexp = 15 - e;
+    sexp = sexp > 100 ? 100 : (sexp < -100 ? -100 : sexp);
+  }
+  const float sc = ldexpf(1.0f, sexp);
+  if (threadIdx.x == 0) J.inv_scale[t] = ldexpf(1.0f, -sexp);
+  __half* hi = static_cast<__half*>(J.operand) + (size_t)(parts * t) * N;
+  __half* lo = hi + N;
+  for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) {
+    const float v = value(base + ((k & ~7u) | chunk_elem(k & 7u))) * sc;  // the A tiles' K order
     const __half hv = __float2half_rn(v);
     hi[k] = hv;
     if (parts == 2) lo[k] = __float2half_rn(v - __half2float(hv));
@@ -464,6 +526,8 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     ga.parts = parts;
     ga.status = ctx->select.status;
     ga.spin = ctx->select.spin_limit;
+    ga.tasks = nullptr;
+    ga.tiles = nullptr;
     const dim3 grid((M + kGRows - 1) / kGRows, (tc + ga.tile_tokens - 1) / ga.tile_tokens);
     gemm_kernel<<<grid, kGThreads, kGSmem, s>>>(bmap, amap, ga);
     e = cudaGetLastError();
@@ -472,6 +536,63 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
   }
   ctx->err[0] = 0;
   return Q4K_OK;
+}
+
+uint32_t gemm_tile_tokens(uint32_t parts) { return 2 * kGTokens / parts; }
+
+uint32_t gemm_tile_rows() { return kGRows; }
+
+size_t gemm_operand_bytes(uint32_t N, uint32_t T, uint32_t parts) { return (size_t)2 * parts * T * N; }
+
+cudaError_t gemm_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N) {
+  EncodeTiledFn enc = gemm_encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {(cuuint64_t)(N / 256) * (kBlockBytes / 4), M};
+  const cuuint64_t strides[1] = {(cuuint64_t)(N / 256) * kBlockBytes};
+  const cuuint32_t box[2] = {kBlockBytes / 4, kGRows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? cudaSuccess
+             : cudaErrorInvalidValue;
+}
+
+cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, uint32_t T, uint32_t parts) {
+  EncodeTiledFn enc = gemm_encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {N, (cuuint64_t)parts * T};
+  const cuuint64_t strides[1] = {2ull * N};
+  const cuuint32_t box[2] = {kGK, parts * gemm_tile_tokens(parts)};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(operand), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? cudaSuccess
+             : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, cudaStream_t s) {
+  if (n_jobs == 0) return cudaSuccess;
+  gemm_prep_kernel<<<n_jobs * T, 256, 0, s>>>(jobs, T, parts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts, int device,
+                              uint32_t* status, uint32_t spin, cudaStream_t s) {
+  if (n_tiles == 0) return cudaSuccess;
+  static std::atomic<uint8_t> attr_set[kAttrDevices];
+  cudaError_t e = smem_attr_once(attr_set, device, gemm_kernel, (int)kGSmem);
+  if (e != cudaSuccess) return e;
+  GemmArgs ga{};
+  ga.parts = parts;
+  ga.status = status;
+  ga.spin = spin;
+  ga.tasks = tasks;
+  ga.tiles = tiles;
+  const CUtensorMap unused{};
+  gemm_kernel<<<n_tiles, kGThreads, kGSmem, s>>>(unused, unused, ga);
+  return cudaGetLastError();
 }
 
 }  // namespace q4k

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "q4k_ctx.cuh"
@@ -63,6 +64,12 @@ struct Stage {
   uint32_t ksplit = 0;  // warps sharing each tile (long rows only; see TaskList::ksplit)
   uint32_t fmt = kFmtQ4K;  // after commit: the weight format of every task of this launch unit
   bool pairs = false;      // after commit: every task fills both super-blocks of its stages (TaskList::pairs)
+  // GEMM plans (batch >= kGemmMinRows): one preparation launch over the
+  // stage's activation jobs, one multi-matrix GEMM launch over its tiles
+  GemmJob* gjobs_dev = nullptr;
+  GemmTask* gtasks_dev = nullptr;
+  uint2* tiles_dev = nullptr;
+  uint32_t n_gjobs = 0, n_tiles = 0;
 };
 
 // Commit splits each recorded stage into launch units of one weight format
@@ -96,6 +103,8 @@ std::vector<Stage> split_by_format(const std::vector<Stage>& stages) {
 struct q4k_plan {
   q4k_ctx* ctx = nullptr;
   uint32_t batch = 1;
+  bool gemm = false;   // batch >= kGemmMinRows: stages run on the tcgen05 GEMM
+  uint32_t parts = 1;  // GEMM plans: operand rows per activation row (1: f16, 2: exact f16 hi + lo)
   std::vector<Stage> stages;
   bool committed = false;
   void* mem = nullptr;  // one allocation: descriptors + prepared activations
@@ -118,6 +127,9 @@ int check_plan(q4k_plan* p) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Largest batch of a GEMM plan (16-bit token-tile indices in the tile table).
+constexpr uint32_t kPlanMaxGemmRows = 8192;
+
 // Plan tasks carry their own maps; the launch parameter is unused.
 const CUtensorMap kNoMap{};
 
@@ -128,12 +140,22 @@ extern "C" {
 int q4k_plan_create(q4k_ctx* ctx, uint32_t batch, q4k_plan** out) {
   if (!ctx || !out) return Q4K_ERR_INVALID_ARG;
   *out = nullptr;
-  if (batch == 0 || batch > (uint32_t)kMaxTokens)
-    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan batch=%u outside [1, %d]", batch, kMaxTokens);
+  if (batch == 0 || (batch > (uint32_t)kMaxTokens && batch < kGemmMinRows) || batch > kPlanMaxGemmRows)
+    return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan batch=%u outside [1, %d] and [%u, %u]", batch, kMaxTokens,
+                    kGemmMinRows, kPlanMaxGemmRows);
   q4k_plan* p = new q4k_plan();
   p->ctx = ctx;
   p->batch = batch;
+  p->gemm = batch >= kGemmMinRows;
   *out = p;
+  return Q4K_OK;
+}
+
+int q4k_plan_gemm_exact(q4k_plan* p, int exact) {
+  int rc = check_plan(p);
+  if (rc != Q4K_OK) return rc;
+  if (!p->gemm) return ctx_fail(p->ctx, Q4K_ERR_INVALID_ARG, "batch-%u plans run on the GEMV engine", p->batch);
+  p->parts = exact ? 2u : 1u;
   return Q4K_OK;
 }
 
@@ -153,6 +175,8 @@ static int plan_gemv(q4k_plan* p, uint32_t stage, const void* w, const float* x,
     return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "bad shape M=%u N=%u (N must be a multiple of 256)", M, N);
   if (!aligned16(w) || !aligned16(x) || !aligned16(y))
     return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  if (p->gemm && fmt != kFmtQ4K)
+    return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "batch-%u plans take Q4_K matrices only", p->batch);
   Stage* st = stage_of(p, stage);
   if (!st) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "stage %u out of range", stage);
   st->gemvs.push_back({static_cast<const uint8_t*>(w), x, y, M, N, fmt});
@@ -215,9 +239,12 @@ int q4k_plan_lmhead_q6k(q4k_plan* p, uint32_t stage, const void* w_dev, const fl
   return plan_lmhead(p, stage, w_dev, x, V, N, cap, row_offset, logits, cand_val, cand_idx, argmax, kFmtQ6K);
 }
 
+static int commit_gemm(q4k_plan* p);
+
 int q4k_plan_commit(q4k_plan* p) {
   int rc = check_plan(p);
   if (rc != Q4K_OK) return rc;
+  if (p->gemm) return commit_gemm(p);
   q4k_ctx* ctx = p->ctx;
   const uint32_t B = p->batch;
   p->stages = split_by_format(p->stages);
@@ -410,11 +437,149 @@ int q4k_plan_commit(q4k_plan* p) {
   return Q4K_OK;
 }
 
+// GEMM plans: per stage, one job per distinct activation (x, or a gelu_mul
+// output that a GEMM of the stage reads), its B operand in the plan's
+// memory, one task per matrix, and the tile table of the stage's single
+// GEMM launch: every (weight-row tile, token tile) of every matrix, longest
+// rows first so the last wave holds the short tiles.
+static int commit_gemm(q4k_plan* p) {
+  q4k_ctx* ctx = p->ctx;
+  const uint32_t T = p->batch, parts = p->parts, tt = gemm_tile_tokens(parts), tr = gemm_tile_rows();
+  struct Key {
+    const float* x;
+    uint32_t N;
+    int gelu;
+  };
+  std::vector<std::vector<Key>> keys(p->stages.size());
+  std::vector<std::vector<uint32_t>> task_job(p->stages.size());
+  size_t desc = 0, ops = 0;
+  for (size_t s = 0; s < p->stages.size(); ++s) {
+    Stage& st = p->stages[s];
+    if (!st.selects.empty()) return ctx_fail(ctx, Q4K_ERR_UNSUPPORTED, "GEMM plans have no fused LM head");
+    auto job_for = [&](const float* x, uint32_t N) -> int {
+      for (size_t j = 0; j < keys[s].size(); ++j)
+        if (keys[s][j].x == x && keys[s][j].N == N) return (int)j;
+      int gelu = -1;
+      for (size_t g = 0; g < st.gelus.size(); ++g)
+        if (st.gelus[g].act == x) {
+          if (st.gelus[g].n != N) return -2;
+          gelu = (int)g;
+        }
+      keys[s].push_back({x, N, gelu});
+      return (int)keys[s].size() - 1;
+    };
+    for (const PlanGemv& g : st.gemvs) {
+      const int j = job_for(g.x, g.N);
+      if (j < 0) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "gelu_mul output size differs from a GEMV's N");
+      task_job[s].push_back((uint32_t)j);
+      st.n_tiles += ((g.M + tr - 1) / tr) * ((T + tt - 1) / tt);
+    }
+    for (size_t g = 0; g < st.gelus.size(); ++g) {
+      bool used = false;
+      for (const Key& k : keys[s]) used |= (k.gelu == (int)g);
+      if (!used) keys[s].push_back({st.gelus[g].act, st.gelus[g].n, (int)g});
+    }
+    st.n_tasks = (uint32_t)st.gemvs.size();
+    st.n_gjobs = (uint32_t)keys[s].size();
+    desc += align_up(sizeof(GemmTask) * st.n_tasks, 256) + align_up(sizeof(GemmJob) * st.n_gjobs, 256) +
+            align_up(sizeof(CUtensorMap) * (st.n_tasks + st.n_gjobs), 256) + align_up(sizeof(uint2) * st.n_tiles, 256);
+    for (const Key& k : keys[s]) ops += align_up(gemm_operand_bytes(k.N, T, parts), 256) + align_up(4ull * T, 256);
+  }
+  p->bytes = desc + ops;
+  if (p->bytes == 0) {
+    p->committed = true;
+    return Q4K_OK;
+  }
+  cudaError_t e = cudaMalloc(&p->mem, p->bytes);
+  if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit allocation");
+  char* cur = static_cast<char*>(p->mem);
+  char* ocur = cur + desc;
+  for (size_t s = 0; s < p->stages.size(); ++s) {
+    Stage& st = p->stages[s];
+    CUtensorMap* maps_dev = reinterpret_cast<CUtensorMap*>(cur);
+    cur += align_up(sizeof(CUtensorMap) * (st.n_tasks + st.n_gjobs), 256);
+    st.gtasks_dev = reinterpret_cast<GemmTask*>(cur);
+    cur += align_up(sizeof(GemmTask) * st.n_tasks, 256);
+    st.gjobs_dev = reinterpret_cast<GemmJob*>(cur);
+    cur += align_up(sizeof(GemmJob) * st.n_gjobs, 256);
+    st.tiles_dev = reinterpret_cast<uint2*>(cur);
+    cur += align_up(sizeof(uint2) * st.n_tiles, 256);
+    std::vector<CUtensorMap> maps(st.n_tasks + st.n_gjobs);
+    std::vector<GemmJob> jobs(st.n_gjobs);
+    for (uint32_t j = 0; j < st.n_gjobs; ++j) {
+      const Key& k = keys[s][j];
+      GemmJob& J = jobs[j];
+      J = GemmJob{};
+      J.N = k.N;
+      if (k.gelu >= 0) {
+        const PlanGelu& g = st.gelus[k.gelu];
+        J.mode = 1;
+        J.gate = g.gate;
+        J.up = g.up;
+        J.act = g.act;
+      } else {
+        J.x = k.x;
+      }
+      J.operand = ocur;
+      ocur += align_up(gemm_operand_bytes(k.N, T, parts), 256);
+      J.inv_scale = reinterpret_cast<float*>(ocur);
+      ocur += align_up(4ull * T, 256);
+      e = gemm_operand_map(&maps[st.n_tasks + j], J.operand, k.N, T, parts);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit activation tensor map");
+    }
+    std::vector<GemmTask> tasks(st.n_tasks);
+    std::vector<uint2> tiles;
+    tiles.reserve(st.n_tiles);
+    for (uint32_t i = 0; i < st.n_tasks; ++i) {
+      const PlanGemv& g = st.gemvs[i];
+      const uint32_t j = task_job[s][i];
+      e = gemm_weight_map(&maps[i], g.w, g.M, g.N);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit weight tensor map");
+      GemmTask& t = tasks[i];
+      t.amap = maps_dev + i;
+      t.bmap = maps_dev + st.n_tasks + j;
+      t.y = g.y;
+      t.inv_scale = jobs[j].inv_scale;
+      t.M = g.M;
+      t.N = g.N;
+      t.T = T;
+      t.tile_tokens = tt;
+      for (uint32_t r = 0; r < (g.M + tr - 1) / tr; ++r)
+        for (uint32_t q = 0; q < (T + tt - 1) / tt; ++q) tiles.push_back(make_uint2(i, r | (q << 16)));
+    }
+    std::stable_sort(tiles.begin(), tiles.end(),
+                     [&](const uint2& a, const uint2& b) { return tasks[a.x].N > tasks[b.x].N; });
+    if (!maps.empty())
+      e = cudaMemcpy(maps_dev, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && st.n_tasks)
+      e = cudaMemcpy(st.gtasks_dev, tasks.data(), sizeof(GemmTask) * st.n_tasks, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && st.n_gjobs)
+      e = cudaMemcpy(st.gjobs_dev, jobs.data(), sizeof(GemmJob) * st.n_gjobs, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && st.n_tiles)
+      e = cudaMemcpy(st.tiles_dev, tiles.data(), sizeof(uint2) * st.n_tiles, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit upload");
+  }
+  p->committed = true;
+  ctx->err[0] = 0;
+  return Q4K_OK;
+}
+
 int q4k_plan_run(q4k_plan* p, void* stream) {
   if (!p) return Q4K_ERR_INVALID_ARG;
   q4k_ctx* ctx = p->ctx;
   if (!p->committed) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "plan not committed");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->gemm) {
+    for (const Stage& st : p->stages) {
+      cudaError_t e = launch_gemm_prep(st.gjobs_dev, st.n_gjobs, p->batch, p->parts, s);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run GEMM activation prep launch");
+      e = launch_gemm_tasks(st.gtasks_dev, st.tiles_dev, st.n_tiles, p->parts, ctx->device, ctx->select.status,
+                            ctx->select.spin_limit, s);
+      if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run GEMM launch");
+    }
+    ctx->err[0] = 0;
+    return Q4K_OK;
+  }
   for (const Stage& st : p->stages) {
     if (st.n_jobs && !st.prep) {
       JobList jl{};
@@ -448,6 +613,10 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
 int q4k_plan_launches(const q4k_plan* p) {
   if (!p || !p->committed) return -1;
   int n = 0;
+  if (p->gemm) {
+    for (const Stage& st : p->stages) n += (st.n_gjobs ? 1 : 0) + (st.n_tiles ? 1 : 0);
+    return n;
+  }
   for (const Stage& st : p->stages) n += (st.n_jobs && !st.prep ? 1 : 0) + (st.total_items ? 1 : 0);
   return n;
 }

@@ -54,7 +54,13 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "q4k_q6k_lmhead_select": ([_P, _P, _P, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P], _I),
     "q4k_q5k_dequant_f16": ([_P, _P, _P, _U64, _P], _I),
     "q4k_ple_stage1": ([_P, _P, _P, _U32, _U32, _U32, _P, _P, _F, _P, _P], _I),
+    "q4k_chain_create": ([_P, _U32, _U32, _U32, _U32, _U32, _F, _P, _P, _P, ctypes.POINTER(_P)], _I),
+    "q4k_chain_lmhead": ([_P, _P, _U32, _F, _P, _P, _P], _I),
+    "q4k_chain_run": ([_P, _P], _I),
+    "q4k_chain_launches": ([_P], _I),
+    "q4k_chain_destroy": ([_P], None),
     "q4k_plan_create": ([_P, _U32, ctypes.POINTER(_P)], _I),
+    "q4k_plan_gemm_exact": ([_P, _I], _I),
     "q4k_plan_destroy": ([_P], None),
     "q4k_plan_gemv": ([_P, _U32, _P, _P, _P, _U32, _U32], _I),
     "q4k_plan_gelu_mul": ([_P, _U32, _P, _P, _P, _U32], _I),

@@ -26,6 +26,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -290,18 +292,22 @@ class StepGraph:
 class BatchedSweep:
     """Config 4: the 35 layers' seven matrices at T activation rows per step
     (prefill, or T independent sequences sharing the weights), without the
-    LM head.  T <= 16 runs as a two-stage Plan on the GEMV engine (one weight
-    stream per matrix for all T rows); T >= 64 runs each matrix through the
-    tcgen05 GEMM (q4k_gemm via Context.gemm), with gelu_mul between up and
-    down as in src/engine.ts:1589-1605.  The layers are independent, so the
-    GEMM path spreads them over `streams` CUDA streams (one library context
-    each: a GEMM call prepares its activation operand in its context's
-    scratch), letting the launches of small matrices share the SMs.  f16x
-    (T >= 64 only): activations rounded once to f16 in the GEMM
-    (q4k_gemm_f16x, the 2e-3 prefill tolerance) instead of exact hi + lo."""
+    LM head, as a two-stage Plan: stage 0 = every q/k/v/o/gate/up, stage 1 =
+    gelu_mul + every down (src/engine.ts:1589-1605).  T <= 16 runs on the
+    GEMV engine (one weight stream per matrix for all T rows); T >= 64 runs
+    each stage as ONE tcgen05 GEMM launch over all of its matrices (after one
+    activation-preparation launch), activations rounded once to f16 (the
+    2e-3 prefill tolerance) unless exact=True asks for the exact f16 hi + lo
+    split.  mode="streams" (T >= 64) instead calls q4k_gemm per matrix,
+    spreading the independent layers over `streams` CUDA streams with a
+    library context each -- the earlier form, kept for comparison."""
 
-    def __init__(self, step: DecodeStep, T: int, streams: int = 18, f16x: bool = False):
-        self.step, self.T, self.f16x = step, T, f16x
+    def __init__(self, step: DecodeStep, T: int, streams: int = 18, f16x: bool | None = None,
+                 exact: bool | None = None, mode: str = "plan"):
+        if exact is None:
+            exact = not f16x if f16x is not None else False
+        self.step, self.T, self.exact, self.mode = step, T, exact, mode
+        self.f16x = not exact
         ctx, s = step.ctx, step.shape
         dev = ctx.device
         shapes = layer_shapes(s)
@@ -312,8 +318,8 @@ class BatchedSweep:
                     for layer in range(s.layers) for name in LAYER_MATS}
         self.act = [torch.empty((T, s.ffn), **f32) for _ in range(s.layers)]
         self.plan = None
-        if T <= 16:
-            p = Plan(ctx, batch=T)
+        if T <= 16 or mode == "plan":
+            p = Plan(ctx, batch=T, exact=exact)
             for layer in range(s.layers):
                 for name in ("q", "k", "v", "o", "gate", "up"):
                     M, N = shapes[name]
@@ -327,6 +333,13 @@ class BatchedSweep:
         else:
             self.ctxs = [Context(dev) for _ in range(streams)]
             self.streams = [torch.cuda.Stream(device=dev) for _ in range(streams)]
+
+    def launches(self) -> int:
+        """Kernel launches per step."""
+        if self.plan is not None:
+            return self.plan.launches()
+        shapes = layer_shapes(self.step.shape)
+        return self.step.shape.layers * (2 * len(shapes) + 1)  # (prep + GEMM) per matrix + gelu_mul
 
     def _layer(self, c: Context, layer: int, stream) -> None:
         s, W, O = self.step.shape, self.step.weights, self.out
@@ -358,6 +371,9 @@ class BatchedSweep:
             main.wait_event(e)
 
     def close(self) -> None:
+        if self.plan is not None:
+            self.plan.close()
+            self.plan = None
         for c in getattr(self, "ctxs", []):
             c.close()
         self.ctxs = []
@@ -368,3 +384,89 @@ class BatchedSweep:
 
     def flops(self) -> int:
         return 2 * self.T * self.weights()
+
+
+CHAIN_BUFFERS = ("q", "k", "v", "o", "g", "u", "act", "d", "h_attn", "h_out")
+
+
+class ChainLayer(ctypes.Structure):
+    """q4k_chain_layer of include/q4k.h: one layer's weights and outputs."""
+
+    _fields_ = [(name, ctypes.c_void_p) for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd") + CHAIN_BUFFERS]
+
+
+class ChainedStep:
+    """Config 3 as a true dependency chain: layer l+1 reads layer l's output,
+    the way encodeTransformerPass runs (src/engine.ts:1538-1619), with the
+    reference's norms, residual adds, v norm and position-0 attention between
+    the GEMVs (all norm weights 1; see q4k_chain_create in include/q4k.h),
+    then final.rmsNorm and the fused LM head.  One persistent launch for all
+    layers plus the LM head launch.  Uses the seeded weights of `step`
+    (the same matrices as the sweep); h_in = the step's x_h row 0."""
+
+    def __init__(self, step: DecodeStep, layers: int | None = None, with_head: bool = True, eps: float = 1e-6):
+        if step.batch != 1:
+            raise ValueError("the chained step is one token (batch 1)")
+        self.step = step
+        ctx, s = step.ctx, step.shape
+        self.ctx = ctx
+        self.layers = layers or s.layers
+        self.eps = eps
+        dev = ctx.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        sizes = {"q": s.q, "k": s.kv, "v": s.kv, "o": s.hidden, "g": s.ffn, "u": s.ffn, "act": s.ffn,
+                 "d": s.hidden, "h_attn": s.hidden, "h_out": s.hidden}
+        self.out = [{name: torch.empty(sizes[name], **f32) for name in CHAIN_BUFFERS} for _ in range(self.layers)]
+        # inputs and results each in one buffer: one copy each way per token
+        self.inputs = torch.empty(s.hidden, **f32)
+        self.inputs.copy_(step.x_h[0])
+        self.h_in = self.inputs
+        self.normed = torch.empty(s.hidden, **f32)
+        self.results = torch.empty(513, dtype=torch.int32, device=dev)
+        self.sel = Selection(cand_val=self.results[:256].view(torch.float32), cand_idx=self.results[256:512],
+                             argmax=self.results[512:], logits=None)
+        arr = (ChainLayer * self.layers)()
+        for layer in range(self.layers):
+            W = {n: step.weights[(layer, n)] for n in LAYER_MATS}
+            o = self.out[layer]
+            arr[layer] = ChainLayer(W["q"].data_ptr(), W["k"].data_ptr(), W["v"].data_ptr(), W["o"].data_ptr(),
+                                    W["gate"].data_ptr(), W["up"].data_ptr(), W["down"].data_ptr(),
+                                    *[o[n].data_ptr() for n in CHAIN_BUFFERS])
+        self._L = ctx._L
+        h = ctypes.c_void_p()
+        ctx._check(self._L.q4k_chain_create(ctx._h, self.layers, s.hidden, s.q, s.kv, s.ffn, eps,
+                                            ctypes.cast(arr, ctypes.c_void_p), self.h_in.data_ptr(),
+                                            self.normed.data_ptr(), ctypes.byref(h)))
+        self._h = h.value
+        self._arr = arr
+        self.with_head = with_head
+        if with_head:
+            ctx._check(self._L.q4k_chain_lmhead(self._h, step.lm_head.data_ptr(), s.vocab, s.softcap,
+                                                self.sel.cand_val.data_ptr(), self.sel.cand_idx.data_ptr(),
+                                                self.sel.argmax.data_ptr()))
+
+    def run(self, stream: torch.cuda.Stream | None = None) -> None:
+        st = stream if stream is not None else torch.cuda.current_stream(self.ctx.device)
+        self.ctx._check(self._L.q4k_chain_run(self._h, st.cuda_stream))
+
+    def launches(self) -> int:
+        return self._L.q4k_chain_launches(self._h)
+
+    def result_tensors(self) -> list[torch.Tensor]:
+        return [self.results]
+
+    def weight_bytes(self) -> int:
+        s = self.step.shape
+        per_layer = sum(synth.q4k_bytes(M, N) for M, N in layer_shapes(s).values())
+        return self.layers * per_layer + (synth.q4k_bytes(s.vocab, s.hidden) if self.with_head else 0)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.q4k_chain_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -461,9 +461,15 @@ class Plan:
     (encodeTransformerPass + queue.submit, src/engine.ts:1466-1626, 1748).
     Tensors are bound at record time, like bind groups, and kept alive by the
     plan.  Operations in one stage must not depend on each other, except that
-    a GEMV may read the `act` of a gelu_mul recorded in the same stage."""
+    a GEMV may read the `act` of a gelu_mul recorded in the same stage.
 
-    def __init__(self, ctx: Context, batch: int = 1):
+    batch 1..16 runs on the GEMV engine; batch >= 64 (prefill, or many
+    sequences sharing the weights) runs each stage as one tcgen05 GEMM launch
+    over all its matrices, with activations rounded once to f16 (the 2e-3
+    prefill tolerance) unless `exact` asks for the exact f16 hi + lo split
+    (the GEMV tolerance, twice the tensor-core work)."""
+
+    def __init__(self, ctx: Context, batch: int = 1, exact: bool = False):
         self.ctx = ctx
         self.batch = batch
         self._L = ctx._L
@@ -472,6 +478,9 @@ class Plan:
         self._h = h.value
         self._keep: list[torch.Tensor] = []
         self.committed = False
+        self.exact = exact
+        if batch > 16 and exact:
+            ctx._check(self._L.q4k_plan_gemm_exact(self._h, 1))
 
     def _bind(self, *ts):
         for t in ts:

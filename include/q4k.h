@@ -320,6 +320,77 @@ Q4K_API int q4k_ple_stage1(q4k_ctx* ctx, const void* table_q5k, const uint32_t* 
                            uint32_t vocab, uint32_t layers, const float* projected, const uint16_t* norm_w,
                            float eps, float* out, void* stream);
 
+/* ---- the chained decode step -------------------------------------------
+ * One token's layers as a true chain, each layer reading the previous
+ * layer's output, in ONE persistent launch (plus the fused LM head): the
+ * matmul_quant dispatches of encodeTransformerPass (src/engine.ts:1538-1619)
+ * with the reference's elementwise passes between them restated so the data
+ * flows as it does there (norm weights 1):
+ *   n1 = rms_norm(h)                      attn.rmsNorm     (rms_norm.wgsl)
+ *   q, k, v = Wq n1, Wk n1, Wv n1         linearQKV
+ *   a = per-head rms_norm(v) for every    vNorm + attention at position 0
+ *       query head (one cached key:       (per_head_rms_norm_no_weight.wgsl;
+ *       softmax of one score is 1)         attn_score/softmax/attn_output)
+ *   o = Wo a                              linearOut
+ *   h_attn = h + rms_norm(o)              attn.postNormAdd (fused_norm_add.wgsl)
+ *   n2 = rms_norm(h_attn)                 ffn.rmsNorm
+ *   g, u = Wg n2, Wu n2; act = gelu(g)*u  linearGateUp, geluMul
+ *   d = Wd act                            linearDown
+ *   h_out = h_attn + rms_norm(d)          ffn.postNormAdd: the next layer's h
+ * and after the last layer normed_out = rms_norm(h_out) (final.rmsNorm,
+ * src/engine.ts:1620-1626), the LM head's input.  rms_norm(x) = x /
+ * sqrt(sum(x^2)/n + eps).  One KV head of kv_dim elements (q_dim a multiple
+ * of it).  Every dimension a multiple of 256, at most 8192.  All buffers are
+ * the caller's device memory, 16-byte aligned; every per-layer output is
+ * written each run.  q4k_chain_create allocates the step's descriptors once;
+ * q4k_chain_run allocates nothing and is graph-capturable.  The launch waits
+ * on grid-wide stage counters with bounded polls (q4k_set_wait_limit); an
+ * expired wait is reported by q4k_check. */
+typedef struct q4k_chain q4k_chain;
+
+typedef struct {
+  const void* wq;  /* Q4_K [q_dim][hidden] */
+  const void* wk;  /* Q4_K [kv_dim][hidden] */
+  const void* wv;  /* Q4_K [kv_dim][hidden] */
+  const void* wo;  /* Q4_K [hidden][q_dim] */
+  const void* wg;  /* Q4_K [ffn][hidden] */
+  const void* wu;  /* Q4_K [ffn][hidden] */
+  const void* wd;  /* Q4_K [hidden][ffn] */
+  float* q;        /* [q_dim] */
+  float* k;        /* [kv_dim] */
+  float* v;        /* [kv_dim] (before its norm) */
+  float* o;        /* [hidden] */
+  float* g;        /* [ffn] */
+  float* u;        /* [ffn] */
+  float* act;      /* [ffn] gelu(g)*u */
+  float* d;        /* [hidden] */
+  float* h_attn;   /* [hidden] residual after the attention block */
+  float* h_out;    /* [hidden] residual after the FFN block */
+} q4k_chain_layer;
+
+/* Record the chain over `layers` layers: per_layer[layers], h_in [hidden]
+ * the first layer's input, normed_out [hidden] the final norm.  No
+ * reference counterpart as one call: it is the per-token layer loop of
+ * encodeTransformerPass, recorded once like the engine's bind groups. */
+Q4K_API int q4k_chain_create(q4k_ctx* ctx, uint32_t layers, uint32_t hidden, uint32_t q_dim, uint32_t kv_dim,
+                             uint32_t ffn, float eps, const q4k_chain_layer* per_layer, const float* h_in,
+                             float* normed_out, q4k_chain** out);
+
+/* Add the fused LM head (q4k_lmhead_select with softcap `cap`) on
+ * normed_out to every run: sampleNextTokenSubmit's lmHead + logitSoftcap +
+ * topk256/argmax (src/engine.ts:1686-1741).  w: Q4_K [V][hidden]. */
+Q4K_API int q4k_chain_lmhead(q4k_chain* chain, const void* w, uint32_t V, float cap, float* cand_val,
+                             uint32_t* cand_idx, uint32_t* argmax);
+
+/* Run the step on `stream`: one persistent launch (+ the LM head launch). */
+Q4K_API int q4k_chain_run(q4k_chain* chain, void* stream);
+
+/* Kernel launches one q4k_chain_run issues. */
+Q4K_API int q4k_chain_launches(const q4k_chain* chain);
+
+/* Free the chain's descriptors.  NULL is ignored. */
+Q4K_API void q4k_chain_destroy(q4k_chain* chain);
+
 /* ---- plans ------------------------------------------------------------
  * A plan records a decode step's matmul-path operations once and replays
  * them with two launches per stage, the way the engine records a token's
@@ -333,8 +404,21 @@ Q4K_API int q4k_ple_stage1(q4k_ctx* ctx, const void* table_q5k, const uint32_t* 
  * allocates the plan's device memory once; q4k_plan_run allocates nothing. */
 typedef struct q4k_plan q4k_plan;
 
-/* New empty plan whose GEMVs all take `batch` activation rows (1..16). */
+/* New empty plan whose GEMVs all take `batch` activation rows: 1..16 on
+ * the GEMV engine, or 64..8192 (prefill, or that many sequences sharing the
+ * weights) on the tcgen05 GEMM, where each stage runs as one preparation
+ * launch over its distinct activations plus ONE GEMM launch over every
+ * matrix of the stage (no per-matrix launches).  GEMM plans take Q4_K
+ * GEMVs and gelu_mul ops, no LM head; their activations are rounded once to
+ * f16 after a power-of-two row scale (q4k_gemm_f16x's 2e-3 prefill
+ * tolerance) unless q4k_plan_gemm_exact asks for the exact form. */
 Q4K_API int q4k_plan_create(q4k_ctx* ctx, uint32_t batch, q4k_plan** out);
+
+/* GEMM plans only, before commit: exact != 0 feeds each activation row as
+ * exact f16 hi + lo parts (q4k_gemm's GEMV tolerance; twice the tensor-core
+ * work), 0 restores the f16 default.  The reference runs every prompt token
+ * through the one-row matmul_quant (src/engine.ts:1932-1934). */
+Q4K_API int q4k_plan_gemm_exact(q4k_plan* plan, int exact);
 
 /* Free a plan and its device memory.  NULL is ignored. */
 Q4K_API void q4k_plan_destroy(q4k_plan* plan);

@@ -115,7 +115,7 @@ def test_batched_sweep_streams_match_single_calls(ctx):
     from q4k.decode import BatchedSweep, DecodeStep, E2BShape, layer_shapes
 
     step = DecodeStep(ctx, E2BShape(layers=3, vocab=1024))
-    bs = BatchedSweep(step, 64, streams=2)
+    bs = BatchedSweep(step, 64, streams=2, exact=True, mode="streams")
     bs.run()
     torch.cuda.synchronize()
     shapes = layer_shapes(step.shape)
@@ -132,7 +132,7 @@ def test_batched_sweep_f16x_matches_single_calls(ctx):
     from q4k.decode import BatchedSweep, DecodeStep, E2BShape, layer_shapes
 
     step = DecodeStep(ctx, E2BShape(layers=2, vocab=1024))
-    bs = BatchedSweep(step, 300, streams=2, f16x=True)
+    bs = BatchedSweep(step, 300, streams=2, f16x=True, mode="streams")
     bs.run()
     torch.cuda.synchronize()
     shapes = layer_shapes(step.shape)
@@ -143,3 +143,35 @@ def test_batched_sweep_f16x_matches_single_calls(ctx):
             torch.cuda.synchronize()
             assert torch.equal(ref.view(torch.int32), bs.out[(layer, name)].view(torch.int32)), (layer, name)
     bs.close()
+
+
+@pytest.mark.parametrize("T,exact", [(64, True), (300, False), (512, False), (65, True)])
+def test_gemm_plan_one_launch_per_stage_matches_oracle(ctx, oracle, T, exact):
+    """A batch >= 64 plan runs each stage as one preparation launch plus ONE
+    GEMM launch over all its matrices (two layers' q/k/v/o/gate/up, then
+    gelu_mul + both downs): every output matches the oracle -- exact plans
+    on the f32 activations, f16 plans on the f16-rounded activations -- within
+    the GEMV tolerance, and the stored gelu_mul output is the oracle's."""
+    from q4k.decode import BatchedSweep, DecodeStep, E2BShape, LAYER_MATS, layer_shapes, matrix_seed
+
+    shape = E2BShape(layers=2, vocab=1024)
+    step = DecodeStep(ctx, shape)
+    bs = BatchedSweep(step, T, exact=exact)
+    assert bs.plan is not None and bs.plan.launches() == 4
+    bs.run()
+    torch.cuda.synchronize()
+    ctx.check()
+    shapes = layer_shapes(shape)
+    x_h, x_attn = bs.x_h.cpu().numpy(), bs.x_attn.cpu().numpy()
+    feed = (lambda a: a) if exact else f16_rounded
+    for layer in range(2):
+        W = {name: synth.q4k_matrix(*shapes[name], matrix_seed(layer, name)) for name in LAYER_MATS}
+        out = {name: bs.out[(layer, name)].cpu().numpy() for name in LAYER_MATS}
+        for name in ("q", "k", "v", "o", "gate", "up"):
+            M, N = shapes[name]
+            check(oracle, out[name], W[name], feed(x_attn if name == "o" else x_h), M, N)
+        act = bs.act[layer].cpu().numpy()
+        act_ref = oracle.gelu_mul(out["gate"], out["up"])
+        assert np.all(np.abs(act - act_ref) <= 1e-6 * np.abs(out["gate"] * out["up"]) + 1e-6 * np.abs(act_ref))
+        M, N = shapes["down"]
+        check(oracle, out["down"], W["down"], feed(act), M, N)
