@@ -412,6 +412,49 @@ def run_ours(args) -> None:
         fhead.close()
         sharded["fused_exchange"] = {"ms": round(fs_ms, 4), "GB/s": round(lm_bytes / (fs_ms / 1e3) / 1e9, 1),
                                      "launches_per_call": 1, "matches_unsharded": fsame}
+        # where the fused head's time goes: the same shard's fused head
+        # without any exchange (its GEMV + softcap + per-residue selection),
+        # timed the same way; the rest is the candidate exchange (peer
+        # stores, flag wait) and the merge
+        barrier(world)
+        a.record()
+        for _ in range(reps):
+            ctx.lmhead_select(w_shard, x0, head.rows, 1536, 30.0, row_offset=head.row0)
+        b.record()
+        torch.cuda.synchronize()
+        shard_ms = max_over_ranks(a.elapsed_time(b) / reps, world, dev)
+        barrier(world)
+        shard_bytes = lm_bytes // world
+        sharded["breakdown"] = {
+            "shard_head_alone_ms": round(shard_ms, 4),
+            "shard_head_alone_GB/s": round(shard_bytes / (shard_ms / 1e3) / 1e9, 1),
+            "exchange_and_merge_ms": round(fs_ms - shard_ms, 4),
+            "shard_bytes": shard_bytes,
+            "what": "fused sharded head = this rank's shard head (GEMV + softcap + per-residue keys + last-CTA "
+                    "merge) + peer stores of 2 KB to every rank + bounded flag wait + G-way merge"}
+
+    # the step as a true dependency chain (layer l+1 reads layer l's output,
+    # with the reference's norms between the GEMVs): one persistent launch for
+    # the 35 layers + the LM head launch
+    chained = None
+    if args.batch == 1 and not args.no_chain:
+        from q4k.decode import ChainedStep
+
+        ch = ChainedStep(step)
+        c_ms, c_graph = time_body(ch.run, reps)
+        c_ms = max_over_ranks(c_ms, world, dev)
+        ch_nohead = ChainedStep(step, with_head=False)
+        cl_ms, cl_graph = time_body(ch_nohead.run, reps)
+        cl_ms = max_over_ranks(cl_ms, world, dev)
+        chained = {"ms": round(c_ms, 4), "tokens_per_s": round(world / (c_ms / 1e3), 1),
+                   "GB/s": round(ch.weight_bytes() / (c_ms / 1e3) / 1e9, 1), "launches": ch.launches(),
+                   "layers_only_ms": round(cl_ms, 4), "per_layer_us": round(cl_ms * 1e3 / ch.layers, 2),
+                   "what": "35 layers chained (rms_norm -> q/k/v -> v norm + position-0 attention -> o -> "
+                           "fused_norm_add -> rms_norm -> gate/up -> gelu_mul -> down -> fused_norm_add), "
+                           "140 dependent stages in one cooperative launch, then final rms_norm + fused LM head"}
+        del c_graph, cl_graph
+        ch.close()
+        ch_nohead.close()
 
     # end to end through the public API: pinned host inputs in, results out
     # the step's inputs (x_h | x_attn) and results (candidates | argmax) each
@@ -475,6 +518,8 @@ def run_ours(args) -> None:
     if real:
         real["lmhead_q6k"]["frac_of_peak"] = round(real["lmhead_q6k"]["GB/s"] / pk["hbm_gbs"], 4)
         kernels["e2b_real_q4km"] = real
+    if chained:
+        kernels["chained_step"] = chained
     if sharded:
         sharded["frac_of_peak"] = round(sharded["GB/s"] / (world * pk["hbm_gbs"]), 4)
         kernels["lmhead_sharded"] = sharded
@@ -689,6 +734,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-real", action="store_true", help="skip the real-E2B-shape (Q4_K + Q6_K) sweep")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 batched sweeps")
+    ap.add_argument("--no-chain", action="store_true", help="skip the chained (layer-dependent) decode step")
     ap.add_argument("--case", choices=CASES, default=None,
                     help="run one kernel's small profiler case instead of the benchmark (see run_case)")
     ap.add_argument("--reps", type=int, default=40, help="--case: launches to run")

@@ -62,7 +62,7 @@ constexpr uint32_t kChainThreads = kChainWarps * 32;
 constexpr uint32_t kChainSlots = 2;                        // copy stages in flight per warp
 constexpr uint32_t kSlotBytes = kTileRows * kPairTileBytes;  // 16 rows x 2 super-blocks (+16 B)
 constexpr uint32_t kChainMaxN = 8192;                      // longest stage input
-constexpr uint32_t kGroupsPerThread = kChainMaxN / 8 / kChainThreads;  // 8-element groups per thread
+constexpr uint32_t kChainStageBuf = 512;  // floats of the shared staging buffer (head vectors)
 constexpr uint32_t kChainMaxLayers = 64;   // the stage and task tables fit shared memory
 // The kernel's dynamic shared-memory limit: the SM's 227 KB per CTA less
 // room for the kernel's static shared memory (about 1.2 KB).
@@ -113,165 +113,181 @@ __device__ __forceinline__ void group_sync(uint32_t grp, uint32_t ks) {
   asm volatile("bar.sync %0, %1;" ::"r"(grp + 1), "r"(ks * 32) : "memory");
 }
 
-// Sum, and sum + max, over the CTA in a fixed order (every CTA, given the
-// same data, gets the same bits).  red: 2 * kChainWarps floats.
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+// Element quad j (0 .. N/4-1) of the activation: elements k..k+3 with
+// k = k0 + 32 * (j & 1), k0 the first element of 8-element fragment group
+// j >> 1 (elements k0..k0+3 and k0+32..k0+35, the lane order of the
+// engine's activation fragments).
+__device__ __forceinline__ uint32_t quad_k(uint32_t j) {
+  const uint32_t idx = j >> 1, b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+  return 256u * b + 64u * c + 4u * w + 32u * (j & 1u);
+}
+
+__device__ __forceinline__ float4 ld4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// Quads per thread of the longest input.
+constexpr uint32_t kQuadsPerThread = kChainMaxN / 4 / kChainThreads;
+
+// Power-of-two activation scale of a normalized vector: |x| <= sqrt(n) <=
+// 90.6 for n <= 8192, so x * 2^8 < 2^15 always (the split's range).
+constexpr float kNormScale = 256.0f, kNormInvScale = 1.0f / 256.0f;
+
+// Fixed-order sums over the CTA (every CTA, given the same data, gets the
+// same bits).  red: 3 * kChainWarps floats.
+template <int K>
+__device__ __forceinline__ void block_sums(float (&v)[K], float* red) {
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+    for (int o = 16; o > 0; o >>= 1) v[k] += __shfl_xor_sync(0xffffffffu, v[k], o);
   __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  if ((threadIdx.x & 31) == 0)
+#pragma unroll
+    for (int k = 0; k < K; ++k) red[k * kChainWarps + (threadIdx.x >> 5)] = v[k];
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    float s = red[k * kChainWarps];
+#pragma unroll
+    for (int i = 1; i < (int)kChainWarps; ++i) s += red[k * kChainWarps + i];
+    v[k] = s;
+  }
+}
+
+__device__ __forceinline__ float block_max(float m, float* red) {
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   float s = red[0];
 #pragma unroll
-  for (int i = 1; i < (int)kChainWarps; ++i) s += red[i];
+  for (int i = 1; i < (int)kChainWarps; ++i) s = fmaxf(s, red[i]);
   return s;
 }
 
-__device__ __forceinline__ float2 block_sum_max(float v, float m, float* red) {
-  for (int o = 16; o > 0; o >>= 1) {
-    v += __shfl_xor_sync(0xffffffffu, v, o);
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  }
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) {
-    red[threadIdx.x >> 5] = v;
-    red[kChainWarps + (threadIdx.x >> 5)] = m;
-  }
-  __syncthreads();
-  float s = red[0], x = red[kChainWarps];
+// Quad j's scaled hi/lo f16 split into the fragment cache (batch 1: columns
+// hi, lo; half j & 1 of the lane's 16-byte fragments).
+__device__ __forceinline__ void write_quad(uint4* frags, uint32_t j, float4 x, float s) {
+  const uint32_t idx = j >> 1, b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
+  const float e[4] = {x.x * s, x.y * s, x.z * s, x.w * s};
+  uint16_t hh[4], hl[4];
 #pragma unroll
-  for (int i = 1; i < (int)kChainWarps; ++i) {
-    s += red[i];
-    x = fmaxf(x, red[kChainWarps + i]);
+  for (int i = 0; i < 4; ++i) {
+    const __half h = __float2half_rn(e[i]);
+    hh[i] = __half_as_ushort(h);
+    hl[i] = __half_as_ushort(__float2half_rn(e[i] - __half2float(h)));
   }
-  return make_float2(s, x);
+  uint2* dst = reinterpret_cast<uint2*>(frags + (size_t)(b * 8 + w) * 8);
+  // per k-step: (x[k], x[k+2]), (x[k+1], x[k+3])
+  dst[2 * c + (j & 1u)] = make_uint2(hh[0] | ((uint32_t)hh[2] << 16), hh[1] | ((uint32_t)hh[3] << 16));
+  dst[8 + 2 * c + (j & 1u)] = make_uint2(hl[0] | ((uint32_t)hl[2] << 16), hl[1] | ((uint32_t)hl[3] << 16));
 }
 
-// Elements of 8-element group idx: k0..k0+3 and k0+32..k0+35 (the lane
-// order of the engine's activation fragments).
-__device__ __forceinline__ uint32_t group_k0(uint32_t idx) {
-  const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
-  return 256u * b + 64u * c + 4u * w;
-}
+__device__ __forceinline__ void store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
-__device__ __forceinline__ void load8(const float* p, uint32_t k0, float (&v)[8]) {
-  const float4 lo = __ldcg(reinterpret_cast<const float4*>(p + k0));
-  const float4 hi = __ldcg(reinterpret_cast<const float4*>(p + k0 + 32));
-  v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
-  v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
-}
-
-__device__ __forceinline__ void store8(float* p, uint32_t k0, const float (&v)[8]) {
-  *reinterpret_cast<float4*>(p + k0) = make_float4(v[0], v[1], v[2], v[3]);
-  *reinterpret_cast<float4*>(p + k0 + 32) = make_float4(v[4], v[5], v[6], v[7]);
-}
-
-// The stage's input vector into the CTA's activation cache (batch 1: hi/lo
-// columns of the m16n8k16 B fragments, q4k_engine.cuh) and its 1/scale.
-// `owner`: this CTA stores the prep's vectors.  Every CTA computes the same
-// values in the same order.
-__device__ __noinline__ float chain_prep(const ChainStage& S, float eps, bool owner, uint4* frags, float* red) {
-  const uint32_t N = S.N, groups = N >> 3;
-  float v[kGroupsPerThread][8];
-  float ss = 0.0f, mx = 0.0f, n = (float)N;
+// The stage's input vector into the CTA's activation cache and its 1/scale.
+// Each thread takes element quads j = threadIdx.x + i * 512.  `owner`: this
+// CTA stores the prep's vectors.  `stage_buf`: kChainStageBuf floats of
+// shared memory for the head vector of kPrepHeadNormBcast.  Every CTA
+// computes the same values in the same order.  Norms multiply by the
+// reciprocal of the rms (the reference divides; WGSL allows 2.5 ulp for
+// division, and the two differ by at most an ulp).
+__device__ __noinline__ float chain_prep(const ChainStage& S, float eps, bool owner, uint4* frags, float* red,
+                                         float* stage_buf) {
+  const uint32_t N = S.N, quads = N >> 2;
+  float4 v[kQuadsPerThread];
   if (S.prep == kPrepNormAddNorm) {
-    // v = a + b / rms(b)  (fused_norm_add.wgsl, weight 1), stored; a and b
-    // are loaded together so their latencies overlap
-    float b[kGroupsPerThread][8];
+    // v = a + b / rms(b) (fused_norm_add.wgsl, weight 1), then x = v / rms(v):
+    // sum(v^2) = sum(a^2) + 2 sum(ab) / rms(b) + sum(b^2) / rms(b)^2, so one
+    // reduction gives both norms
+    float4 b[kQuadsPerThread];
+    float sums[3] = {0.0f, 0.0f, 0.0f};  // a.a, a.b, b.b
 #pragma unroll
-    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
-      const uint32_t idx = threadIdx.x + i * kChainThreads;
-      if (idx < groups) {
-        const uint32_t k0 = group_k0(idx);
-        load8(S.a, k0, v[i]);
-        load8(S.b, k0, b[i]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ss += b[i][j] * b[i][j];
+    for (uint32_t i = 0; i < kQuadsPerThread; ++i) {
+      const uint32_t j = threadIdx.x + i * kChainThreads;
+      if (j < quads) {
+        const uint32_t k = quad_k(j);
+        v[i] = ld4(S.a + k);
+        b[i] = ld4(S.b + k);
+        sums[0] += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        sums[1] += v[i].x * b[i].x + v[i].y * b[i].y + v[i].z * b[i].z + v[i].w * b[i].w;
+        sums[2] += b[i].x * b[i].x + b[i].y * b[i].y + b[i].z * b[i].z + b[i].w * b[i].w;
       }
     }
-    const float rms_b = sqrtf(block_sum(ss, red) / n + eps);
-    ss = 0.0f;
+    block_sums<3>(sums, red);
+    const float n = (float)N;
+    const float ib = 1.0f / sqrtf(sums[2] / n + eps);
+    const float vv = sums[0] + 2.0f * ib * sums[1] + ib * ib * sums[2];
+    const float iv = 1.0f / sqrtf(fmaxf(vv, 0.0f) / n + eps);
 #pragma unroll
-    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
-      const uint32_t idx = threadIdx.x + i * kChainThreads;
-      if (idx < groups) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          v[i][j] = v[i][j] + b[i][j] / rms_b;
-          ss += v[i][j] * v[i][j];
-          mx = fmaxf(mx, fabsf(v[i][j]));
-        }
-        if (owner && S.store) store8(S.store, group_k0(idx), v[i]);
+    for (uint32_t i = 0; i < kQuadsPerThread; ++i) {
+      const uint32_t j = threadIdx.x + i * kChainThreads;
+      if (j < quads) {
+        const uint32_t k = quad_k(j);
+        const float4 h = make_float4(v[i].x + b[i].x * ib, v[i].y + b[i].y * ib, v[i].z + b[i].z * ib,
+                                     v[i].w + b[i].w * ib);
+        if (owner && S.store) store4(S.store + k, h);
+        const float4 x = make_float4(h.x * iv, h.y * iv, h.z * iv, h.w * iv);
+        if (owner && S.store_norm) store4(S.store_norm + k, x);
+        write_quad(frags, j, x, kNormScale);
       }
     }
-  } else {
-#pragma unroll
-    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
-      const uint32_t idx = threadIdx.x + i * kChainThreads;
-      if (idx < groups) {
-        const uint32_t k0 = group_k0(idx);
-        if (S.prep == kPrepGelu) {
-          float g[8], u[8];
-          load8(S.a, k0, g);
-          load8(S.b, k0, u);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) v[i][j] = gelu_mul_value(g[j], u[j]);
-          if (owner && S.store) store8(S.store, k0, v[i]);
-        } else {
-          // kPrepNorm: a; kPrepHeadNormBcast: a[j mod hd] (a head dim that is
-          // a multiple of 256: a group never straddles a head)
-          load8(S.a, S.prep == kPrepHeadNormBcast ? k0 % S.hd : k0, v[i]);
-        }
-        // the norm's sum of squares: over a once (the first head copy)
-        if (S.prep == kPrepNorm || (S.prep == kPrepHeadNormBcast && k0 < S.hd))
-#pragma unroll
-          for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[i][j]));
-      }
-    }
-    if (S.prep == kPrepHeadNormBcast) n = (float)S.hd;
+    return kNormInvScale;
   }
-  // one reduction for the norm's sum of squares and the largest |value|
-  const float2 red2 = block_sum_max(ss, mx, red);
-  float xmax = red2.y;
-  if (S.prep != kPrepGelu) {
-    // rms_norm.wgsl (weight 1): x / sqrt(sum(x^2)/n + eps); the largest |x|
-    // is the largest |v| divided the same way (division rounds monotonically)
-    const float rms = sqrtf(red2.x / n + eps);
-    xmax = xmax / rms;
+  if (S.prep == kPrepGelu) {
+    // gelu_mul.wgsl: x = gelu_tanh(a) * b, stored; the largest |x| sets the scale
+    float mx = 0.0f;
 #pragma unroll
-    for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
-      const uint32_t idx = threadIdx.x + i * kChainThreads;
-      if (idx < groups) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] / rms;
-        if (owner && S.store_norm) store8(S.store_norm, group_k0(idx), v[i]);
+    for (uint32_t i = 0; i < kQuadsPerThread; ++i) {
+      const uint32_t j = threadIdx.x + i * kChainThreads;
+      if (j < quads) {
+        const uint32_t k = quad_k(j);
+        const float4 g = ld4(S.a + k), u = ld4(S.b + k);
+        v[i] = make_float4(gelu_mul_value(g.x, u.x), gelu_mul_value(g.y, u.y), gelu_mul_value(g.z, u.z),
+                           gelu_mul_value(g.w, u.w));
+        if (owner && S.store) store4(S.store + k, v[i]);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
       }
     }
+    const float2 sc = token_scale(block_max(mx, red));
+#pragma unroll
+    for (uint32_t i = 0; i < kQuadsPerThread; ++i) {
+      const uint32_t j = threadIdx.x + i * kChainThreads;
+      if (j < quads) write_quad(frags, j, v[i], sc.x);
+    }
+    return sc.y;
   }
-  const float2 sc = token_scale(xmax);
-  // the scaled hi/lo split in the fragment order (batch 1: columns hi, lo)
+  // kPrepNorm: x = a / rms(a).  kPrepHeadNormBcast: x[k] = a[k mod hd] /
+  // rms(a[0..hd)); the head is staged in shared memory once (every quad of
+  // every head copy reads it), its sum over the first copy only.
+  const bool bcast = S.prep == kPrepHeadNormBcast;
+  const float* src = S.a;
+  if (bcast && S.hd <= kChainStageBuf) {
+    for (uint32_t j = threadIdx.x; j < S.hd / 4; j += kChainThreads)
+      reinterpret_cast<float4*>(stage_buf)[j] = ld4(S.a + 4 * j);
+    __syncthreads();
+    src = stage_buf;
+  }
+  float ss[1] = {0.0f};
 #pragma unroll
-  for (uint32_t i = 0; i < kGroupsPerThread; ++i) {
-    const uint32_t idx = threadIdx.x + i * kChainThreads;
-    if (idx < groups) {
-      const uint32_t b = idx >> 5, w = (idx >> 2) & 7u, c = idx & 3u;
-      uint16_t hh[8], hl[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float x = v[i][j] * sc.x;
-        const __half h = __float2half_rn(x);
-        hh[j] = __half_as_ushort(h);
-        hl[j] = __half_as_ushort(__float2half_rn(x - __half2float(h)));
-      }
-      uint4* dst = frags + (size_t)(b * 8 + w) * 8;
-      dst[c] = make_uint4(hh[0] | ((uint32_t)hh[2] << 16), hh[1] | ((uint32_t)hh[3] << 16),
-                          hh[4] | ((uint32_t)hh[6] << 16), hh[5] | ((uint32_t)hh[7] << 16));
-      dst[4 + c] = make_uint4(hl[0] | ((uint32_t)hl[2] << 16), hl[1] | ((uint32_t)hl[3] << 16),
-                              hl[4] | ((uint32_t)hl[6] << 16), hl[5] | ((uint32_t)hl[7] << 16));
+  for (uint32_t i = 0; i < kQuadsPerThread; ++i) {
+    const uint32_t j = threadIdx.x + i * kChainThreads;
+    if (j < quads) {
+      const uint32_t k = quad_k(j);
+      v[i] = bcast ? *reinterpret_cast<const float4*>(src + k % S.hd) : ld4(src + k);
+      if (!bcast || k < S.hd) ss[0] += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
     }
   }
-  return sc.y;
+  block_sums<1>(ss, red);
+  const float iv = 1.0f / sqrtf(ss[0] / (float)(bcast ? S.hd : N) + eps);
+#pragma unroll
+  for (uint32_t i = 0; i < kQuadsPerThread; ++i) {
+    const uint32_t j = threadIdx.x + i * kChainThreads;
+    if (j < quads) {
+      const float4 x = make_float4(v[i].x * iv, v[i].y * iv, v[i].z * iv, v[i].w * iv);
+      if (owner && S.store_norm) store4(S.store_norm + quad_k(j), x);
+      write_quad(frags, j, x, kNormScale);
+    }
+  }
+  return kNormInvScale;
 }
 
 // The stage and task tables as every CTA keeps them in shared memory (the
@@ -378,7 +394,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainArgs
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
   __shared__ uint64_t s_bar[kChainWarps][kChainSlots];
-  __shared__ float s_red[2 * kChainWarps];
+  __shared__ float s_red[3 * kChainWarps];
   __shared__ uint32_t s_fail;
   __shared__ ChainStage s_stage;  // the record of the stage being prepared
   __shared__ Walk s_walk[kChainWarps];  // each warp's copy walk (lane 0's; kept out of registers)
@@ -440,7 +456,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const ChainArgs
       __syncthreads();
     }
     const bool owner = blockIdx.x == s % gridDim.x;
-    const float inv = chain_prep(s_stage, A.eps, owner, xsm, s_red);
+    const float inv = chain_prep(s_stage, A.eps, owner, xsm, s_red, s_part);
     __syncthreads();
     // the next stage's record, loaded while this stage computes
     if (threadIdx.x == 0 && s + 1 < A.nstages) s_stage = A.stages[s + 1];
