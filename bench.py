@@ -582,7 +582,7 @@ def run_ours(args) -> None:
 
 # ---- profiler cases ---------------------------------------------------------------------------
 
-CASES = ("gemv", "lmhead", "sweep", "gemm", "q6head", "ple", "downs")
+CASES = ("gemv", "lmhead", "sweep", "gemm", "q6head", "ple", "downs", "gemmplan", "chain")
 
 
 def run_case(args) -> None:
@@ -603,6 +603,9 @@ def run_case(args) -> None:
               token each rep
       downs   the decode step's second plan stage alone (gelu_mul + the 35 down
               projections 1536x6144, 186 MB, 4 warps per tile)
+      gemmplan  config 4's GEMM plan on --layers layers (default 8: 159 MB) at --batch
+              activation rows (default 512), f16 activations (--exact: hi + lo)
+      chain   the chained decode step over --layers layers (default 8), no LM head
     """
     import torch
 
@@ -631,6 +634,24 @@ def run_case(args) -> None:
         step = DecodeStep(ctx, E2BShape(layers=args.layers, vocab=16384), batch=args.batch)
         for _ in range(args.reps):
             step.run()
+    elif args.case == "gemmplan":
+        from q4k.decode import BatchedSweep, DecodeStep, E2BShape
+
+        step = DecodeStep(ctx, E2BShape(layers=args.layers, vocab=256), batch=1)
+        bs = BatchedSweep(step, args.batch if args.batch > 1 else 512, exact=args.exact)
+        for _ in range(args.reps):
+            bs.run()
+        torch.cuda.synchronize()
+        bs.close()
+    elif args.case == "chain":
+        from q4k.decode import ChainedStep, DecodeStep, E2BShape
+
+        step = DecodeStep(ctx, E2BShape(layers=args.layers, vocab=256), batch=1)
+        ch = ChainedStep(step, with_head=False)
+        for _ in range(args.reps):
+            ch.run()
+        torch.cuda.synchronize()
+        ch.close()
     elif args.case == "downs":
         from q4k.decode import DecodeStep, E2BShape
 
@@ -740,6 +761,7 @@ def main():
     ap.add_argument("--reps", type=int, default=40, help="--case: launches to run")
     ap.add_argument("--layers", type=int, default=8, help="--case sweep: layers of the plan")
     ap.add_argument("--f16x", action="store_true", help="--case gemm: activations rounded to f16 (q4k_gemm_f16x)")
+    ap.add_argument("--exact", action="store_true", help="--case gemmplan: exact f16 hi + lo activations")
     args = ap.parse_args()
     if args.case is not None:
         run_case(args)

@@ -15,15 +15,17 @@
 //   * the B operand, x split exactly into f16 hi + lo parts (two operand rows
 //     per activation row, scaled per row by a power of two), arrives by one
 //     TMA tensor copy in the 128-byte swizzled K-major layout;
-//   * the A operand, the 256 x 64 f16 weights, is dequantized by 8 warps
+//   * the A operand, the 256 x 64 f16 weights, is dequantized by 16 warps
+//     (two groups of 8, one per K-step parity, each filling its own stage)
 //     into the same swizzled layout, computed before the stage is free and
 //     stored once it is; the raw Q4_K super-blocks reach shared memory by
 //     TMA, one 144-byte box per tile row per super-block column (four K
 //     steps), two columns in flight (a copy warp of its own);
 //   * one thread issues the 8 MMAs and commits them to the stage's "empty"
 //     barrier, which frees the stage for the producers.
-// Two operand stages are in flight.  The epilogue (8 warps: per accumulator one per
-// 32-lane quarter of tensor memory) reads the accumulators, adds each activation
+// Two operand stages are in flight.  The epilogue (the 16 producer warps: per
+// accumulator one per 32-lane quarter of tensor memory and column half) reads
+// the accumulators, adds each activation
 // row's hi and lo columns, undoes the scale and stores Y.  f16 x f16
 // products are exact and the hi/lo split carries x to ~2^-22, so the result
 // is the f32 dot product of the reference's f16 weights with x, up to fp32
@@ -53,7 +55,8 @@ constexpr uint32_t kGStages = 2;
 constexpr uint32_t kGASub = kGMmaM * kGK * 2;           // 16 KB: one 128-row A block
 constexpr uint32_t kGABytes = kGHalves * kGASub;        // 32 KB
 constexpr uint32_t kGBBytes = 2 * kGTokens * kGK * 2;   // 32 KB
-constexpr uint32_t kGDqWarps = 8;                       // dequantizing warps, also the epilogue
+constexpr uint32_t kGDqGroups = 2;                      // producer groups: group p takes the K steps = p (mod 2)
+constexpr uint32_t kGDqWarps = 8 * kGDqGroups;          // dequantizing warps (8 per group), also the epilogue
 constexpr uint32_t kGRawWarp = 2 + kGDqWarps;            // the raw-weight copy warp
 constexpr uint32_t kGThreads = (3 + kGDqWarps) * 32;    // + B-copy warp + MMA warp + raw-copy warp
 constexpr uint32_t kGRawStages = 2;                     // raw super-block columns in flight
@@ -214,14 +217,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kGStages; ++s) {
-      mbar_init(&full_a[s], kGDqWarps);
+      mbar_init(&full_a[s], kGDqWarps / kGDqGroups);  // filled by one group (K-step parity = stage)
       mbar_init(&full_b[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&done_bar, 1);
     for (uint32_t s = 0; s < kGRawStages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kGDqWarps);
+      mbar_init(&raw_empty[s], kGDqWarps);  // every producer warp takes some K steps of each column
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -279,27 +282,31 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       umma_commit(&done_bar);  // the accumulators are final once every MMA above completes
     }
   } else if (warp < kGRawWarp) {
-    // A producers: thread r (0..255) dequantizes tile row r's 64 weights of
-    // each K step (its 32-byte qs group, both nibbles: low -> local k 0..31
-    // of sub-block 2j, high -> local k 32..63 of sub-block 2j+1) into row
-    // r%128 of A block r/128.  The raw super-blocks arrive by TMA, one
-    // column of the tile's 256 rows per raw stage (four K steps); a step's
-    // weights are computed before waiting for its A stage to be free, so
-    // only the stores sit between the tensor core releasing a stage and
+    // A producers, two groups of 8 warps: thread r (0..255) of group p
+    // dequantizes tile row r's 64 weights of the K steps = p (mod 2) (its
+    // 32-byte qs group, both nibbles: low -> local k 0..31 of sub-block 2j,
+    // high -> local k 32..63 of sub-block 2j+1) into row r%128 of A block
+    // r/128 of stage p.  The raw super-blocks arrive by TMA, one column of
+    // the tile's 256 rows per raw stage (four K steps, two per group); a
+    // step's weights are computed before waiting for its A stage to be free,
+    // so only the stores sit between the tensor core releasing a stage and
     // refilling it.  A warp covers 32 consecutive rows: the 8 lanes of each
     // 16-byte store phase hit 8 different swizzled chunks.  Rows past M
     // arrive as zeros; their accumulator rows are never stored.
-    const uint32_t r = threadIdx.x - 64;
+    static_assert(kGStages == kGDqGroups, "group p fills A stage p");
+    const uint32_t pt = threadIdx.x - 64;
+    const uint32_t r = pt % kGRows, grp = pt / kGRows;
     const uint32_t rb = r & (kGMmaM - 1), sw = rb & 7u;  // 128-byte swizzle: chunk index ^ row%8
-    for (uint32_t ks = 0; ks < ksteps && !failed; ++ks) {
+    for (uint32_t ks = grp; ks < ksteps && !failed; ks += kGDqGroups) {
       const uint32_t sb = ks >> 2, j = ks & 3u, rs = sb % kGRawStages;
-      if (j == 0 && !mbar_wait(&raw_full[rs], (sb / kGRawStages) & 1u, spin)) {
+      // the group's first K step of this column waits for the column
+      if (j == grp && !mbar_wait(&raw_full[rs], (sb / kGRawStages) & 1u, spin)) {
         failed = true;
         break;
       }
       const RawGroup g = raw_group(sRaw + rs * kGRawBytes + r * kBlockBytes, j);
-      if (j == 3) {
-        // the column is in registers: hand the raw stage back
+      if (j + kGDqGroups >= 4) {
+        // the group's last K step of this column is in registers: hand it back
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
       }
@@ -316,15 +323,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(&full_a[s]);
     }
-    // epilogue: warp w reads accumulator (w-2)/4 (rows 128*that ..) in its
-    // tensor-memory lane quarter w%4
+    // epilogue: producer warp e = w-2 reads accumulator (e/4)%2 (rows
+    // 128*that ..) in its tensor-memory lane quarter w%4, the 32-column
+    // chunks of parity e/8
     if (!mbar_wait(&done_bar, 0, spin)) {
       failed = true;
     } else {
       tc_fence_after();
-      const uint32_t q = warp & 3u, hb = (warp - 2) >> 2;
+      const uint32_t e = warp - 2, q = warp & 3u, hb = (e >> 2) & 1u, half = e >> 3;
       const uint32_t erow = row0 + hb * kGMmaM + 32 * q + lane;
-      for (uint32_t c0 = 0; c0 < n_mma; c0 += 32) {
+      for (uint32_t c0 = 32 * half; c0 < n_mma; c0 += 32 * (kGDqWarps / 8)) {
         float v[32];
         tmem_ld32(tmem + ((32u * q) << 16) + hb * kGAccCols + c0, v);
         if (a.parts == 2) {
