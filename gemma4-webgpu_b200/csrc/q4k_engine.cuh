@@ -166,10 +166,13 @@ cudaError_t encode_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint3
 cudaError_t encode_q6k_maps(CUtensorMap* maps, const void* w, uint32_t M, uint32_t N, uint32_t* tile_bytes);
 
 // Schedule cost of one work item (16 rows) of a task: its super-blocks per
-// row, in units of 1/20; LM-head items (softcap + per-residue selection in
-// the epilogue) count 5 % more.
+// row.  LM-head items (softcap + per-residue selection in the epilogue) cost
+// the same: with them weighted 5 % above plain items, a per-CTA trace of
+// the decode step's first launch showed the CTAs holding LM-head items
+// finishing ~5 % before the others.
 __host__ __device__ inline uint32_t item_cost(uint32_t N, uint32_t kind) {
-  return (N >> 8) * (kind == kTaskSelect ? 21u : 20u);
+  (void)kind;
+  return N >> 8;
 }
 
 // Engine launch geometry: CTAs for a work list, and the shared-memory
