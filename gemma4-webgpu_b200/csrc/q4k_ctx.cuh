@@ -91,15 +91,17 @@ struct alignas(16) GemmJob {
   uint32_t N, mode;
 };
 
-// Activation rows per token tile of a multi-matrix launch (full 256-operand-row tiles).
-uint32_t gemm_tile_tokens(uint32_t parts);
+// Activation rows per token tile of a T-row launch: all of them when they
+// make at most 128 operand rows (parts per activation row; the tensor-memory
+// A form), else 256 operand rows.
+uint32_t gemm_tile_tokens(uint32_t parts, uint32_t T);
 // Rows of the weight-row tile (the A operand's M per CTA).
 uint32_t gemm_tile_rows();
 size_t gemm_operand_bytes(uint32_t N, uint32_t T, uint32_t parts);
 cudaError_t gemm_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N);
 cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, uint32_t T, uint32_t parts);
 cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, cudaStream_t s);
-cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts, int device,
-                              uint32_t* status, uint32_t spin, cudaStream_t s);
+cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts,
+                              uint32_t tile_tokens, int device, uint32_t* status, uint32_t spin, cudaStream_t s);
 
 }  // namespace q4k

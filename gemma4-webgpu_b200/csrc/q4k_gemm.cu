@@ -22,8 +22,12 @@
 //     TMA, one 144-byte box per tile row per super-block column (four K
 //     steps), two columns in flight (a copy warp of its own);
 //   * one thread issues the 8 MMAs and commits them to the stage's "empty"
-//     barrier, which frees the stage for the producers.
-// Two operand stages are in flight.  The epilogue (the 16 producer warps: per
+//     barrier, which frees the stage for the producers; it waits on one
+//     barrier per step, the producers' plus a relay arrival once B landed.
+// Two operand stages are in flight.  Tiles of at most 128 operand rows (a
+// batch of up to 128 f16 or 64 exact activation rows) run the TS form
+// instead (GemmForm below): the weights go straight into tensor memory, four
+// stages in flight.  The epilogue (the 16 producer warps: per
 // accumulator one per 32-lane quarter of tensor memory and column half) reads
 // the accumulators, adds each activation
 // row's hi and lo columns, undoes the scale and stores Y.  f16 x f16
@@ -59,11 +63,37 @@ constexpr uint32_t kGDqGroups = 2;                      // producer groups: grou
 constexpr uint32_t kGDqWarps = 8 * kGDqGroups;          // dequantizing warps (8 per group), also the epilogue
 constexpr uint32_t kGRawWarp = 2 + kGDqWarps;            // the raw-weight copy warp
 constexpr uint32_t kGThreads = (3 + kGDqWarps) * 32;    // + B-copy warp + MMA warp + raw-copy warp
-constexpr uint32_t kGRawStages = 2;                     // raw super-block columns in flight
+constexpr uint32_t kGRawStages = 2;                     // raw super-block columns in flight (SS form)
 constexpr uint32_t kGRawBytes = kGRows * kBlockBytes;   // 36 KB: one super-block of each of the 256 rows
 constexpr uint32_t kGAccCols = 2 * kGTokens;            // fp32 columns of one accumulator
 constexpr uint32_t kGTmemCols = kGHalves * kGAccCols;   // 512: all of tensor memory
-constexpr size_t kGSmem = 1024 + (size_t)kGStages * (kGABytes + kGBBytes) + (size_t)kGRawStages * kGRawBytes;
+
+// The two forms of the kernel.  SS: both operands in shared memory, tiles of
+// up to 256 operand rows (MMA N <= 256), two stages.  TS (tiles of at most
+// 128 operand rows): the producers store the weights straight into tensor
+// memory (tcgen05.st) and the MMA reads A from there.  A single-thread
+// stream of M = 128 kind::f16 MMAs measured on B200 costs ~89 cycles per
+// instruction for any N <= 128 with A in shared memory (N = 256: 128 cycles,
+// the full rate), but 54 cycles at N = 64 and 64 cycles at N = 128 (the full
+// rate) with A in tensor memory; the A stores, their proxy fence and the
+// tensor core's A reads also leave shared memory.  Tensor memory then holds
+// the two 128-column accumulators and four A stages of 2 x 32 columns (a
+// row's 64 weights of a K step, two f16 per column, lane = row); the freed
+// shared memory holds four B stages and four raw super-block columns.
+template <bool kTA>
+struct GemmForm {
+  static constexpr uint32_t kStages = kTA ? 4 : kGStages;
+  static constexpr uint32_t kABytes = kTA ? 0 : kGABytes;                // smem A stage
+  static constexpr uint32_t kBBytes = kTA ? 128 * kGK * 2 : kGBBytes;   // smem B stage (largest box)
+  static constexpr uint32_t kAccCols = kTA ? 128 : kGAccCols;          // tensor-memory columns per accumulator
+  static constexpr uint32_t kACol = kGHalves * kAccCols;               // first A column (TS)
+  static constexpr uint32_t kAStageCols = kGHalves * (kGK / 2);        // A columns per stage (TS)
+  static constexpr uint32_t kRawStages = kTA ? 4 : kGRawStages;        // raw super-block columns in flight
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * (kABytes + kBBytes) + (size_t)kRawStages * kGRawBytes;
+  static_assert(!kTA || kACol + kStages * kAStageCols <= kGTmemCols, "TS tensor-memory layout");
+  static_assert(kStages % kGDqGroups == 0, "each stage is filled by one producer group");
+};
+constexpr uint32_t kGMaxTsRows = 128;  // operand rows per tile up to which the TS form runs
 
 // UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzled
 // layout: 128-byte rows, 8-row groups 1024 bytes apart (stride offset), the
@@ -85,6 +115,34 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
+}
+
+// The same with A in tensor memory: `a_tmem` addresses the 128 lanes x 8
+// columns (two f16 per column, the lower K index in the low half) of one
+// 16-wide k slice.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this warp's 32 tensor-memory lanes from
+// the 8 chunks of each lane's row (chunk c -> columns 4c..4c+3), then waits
+// until the stores are complete.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint4 (&c)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(c[0].x), "r"(c[0].y), "r"(c[0].z), "r"(c[0].w), "r"(c[1].x), "r"(c[1].y), "r"(c[1].z), "r"(c[1].w),
+      "r"(c[2].x), "r"(c[2].y), "r"(c[2].z), "r"(c[2].w), "r"(c[3].x), "r"(c[3].y), "r"(c[3].z), "r"(c[3].w),
+      "r"(c[4].x), "r"(c[4].y), "r"(c[4].z), "r"(c[4].w), "r"(c[5].x), "r"(c[5].y), "r"(c[5].z), "r"(c[5].w),
+      "r"(c[6].x), "r"(c[6].y), "r"(c[6].z), "r"(c[6].w), "r"(c[7].x), "r"(c[7].y), "r"(c[7].z), "r"(c[7].w)
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Arrives on `bar` once every MMA this thread issued before has completed.
@@ -170,17 +228,19 @@ __device__ __forceinline__ RowChunks dequant_group(const RawGroup& g, uint32_t j
   return o;
 }
 
+template <bool kTA>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap bmap,
                                                             const __grid_constant__ CUtensorMap amap, const GemmArgs a) {
+  using F = GemmForm<kTA>;
   const uint32_t spin = spin_or_default(a.spin);  // polls per bounded wait
   extern __shared__ uint8_t g_smem_raw[];
   // swizzled operand tiles start on 1024-byte boundaries
   uint8_t* smem = g_smem_raw + ((1024u - (smem_u32(g_smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + kGStages * kGABytes;
-  uint8_t* sRaw = sB + kGStages * kGBBytes;
-  __shared__ uint64_t full_a[kGStages], full_b[kGStages], empty_bar[kGStages], done_bar;
-  __shared__ uint64_t raw_full[kGRawStages], raw_empty[kGRawStages];
+  uint8_t* sB = smem + F::kStages * F::kABytes;
+  uint8_t* sRaw = sB + F::kStages * F::kBBytes;
+  __shared__ uint64_t full_a[F::kStages], full_b[F::kStages], empty_bar[F::kStages], done_bar;
+  __shared__ uint64_t raw_full[F::kRawStages], raw_empty[F::kRawStages];
   __shared__ uint32_t s_tmem;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -216,13 +276,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   bool failed = false;
 
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < kGStages; ++s) {
-      mbar_init(&full_a[s], kGDqWarps / kGDqGroups);  // filled by one group (K-step parity = stage)
+    for (uint32_t s = 0; s < F::kStages; ++s) {
+      mbar_init(&full_a[s], kGDqWarps / kGDqGroups + 1);  // one producer group + the B-landed relay
       mbar_init(&full_b[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&done_bar, 1);
-    for (uint32_t s = 0; s < kGRawStages; ++s) {
+    for (uint32_t s = 0; s < F::kRawStages; ++s) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], kGDqWarps);  // every producer warp takes some K steps of each column
     }
@@ -244,63 +304,93 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     if (lane == 0) {
       uint32_t issued = 0;
       for (uint32_t ks = 0; ks < ksteps; ++ks) {
-        const uint32_t s = ks % kGStages, use = ks / kGStages;
+        const uint32_t s = ks % F::kStages, use = ks / F::kStages;
         if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u, spin)) {
           failed = true;
           break;
         }
         mbar_arrive_expect_tx(&full_b[s], b_bytes);
-        tma_tile_g2s(sB + s * kGBBytes, pbmap, ks * kGK, a.parts * tok0, &full_b[s]);
+        tma_tile_g2s(sB + s * F::kBBytes, pbmap, ks * kGK, a.parts * tok0, &full_b[s]);
         ++issued;
       }
       // every issued copy has landed before the CTA can exit
-      for (uint32_t ks = (issued > kGStages ? issued - kGStages : 0); ks < issued; ++ks)
-        if (!mbar_wait(&full_b[ks % kGStages], (ks / kGStages) & 1u, spin)) failed = true;
+      for (uint32_t ks = (issued > F::kStages ? issued - F::kStages : 0); ks < issued; ++ks)
+        if (!mbar_wait(&full_b[ks % F::kStages], (ks / F::kStages) & 1u, spin)) failed = true;
+    } else if (lane == 1) {
+      // relay: once a step's B copy has landed, one more arrival on the
+      // stage's A barrier, so the MMA thread waits on one barrier per step
+      // (each wait on an already completed barrier cost it ~0.2 us inside
+      // the busy kernel).  It cannot fall two phases behind: the copy of step
+      // ks + kStages needs the MMAs of step ks, which need this arrival.
+      for (uint32_t ks = 0; ks < ksteps; ++ks) {
+        const uint32_t s = ks % F::kStages;
+        if (!mbar_wait(&full_b[s], (ks / F::kStages) & 1u, spin)) {
+          failed = true;
+          break;
+        }
+        mbar_arrive(&full_a[s]);
+      }
     }
   } else if (warp == 1) {
     // MMA issuer: per stage and 16-wide k slice, one 128 x n_mma x 16 MMA per
     // row block, both reading the same B tile
     if (lane == 0) {
+      // The ring is unrolled, so each stage's operand addresses are a base
+      // plus constants (descriptor address fields count 16-byte units): the
+      // single issuing thread paces the pipeline at small N, and per-MMA
+      // address arithmetic on its dependency chain cost ~9% at T = 64.
       const uint32_t idesc = idesc_f16(n_mma);
-      for (uint32_t ks = 0; ks < ksteps; ++ks) {
-        const uint32_t s = ks % kGStages, ph = (ks / kGStages) & 1u;
-        if (!mbar_wait(&full_a[s], ph, spin) || !mbar_wait(&full_b[s], ph, spin)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * kGABytes), b0 = smem_u32(sB + s * kGBBytes);
+      const uint64_t db = smem_desc_sw128(smem_u32(sB));
+      const uint64_t da = smem_desc_sw128(smem_u32(sA));
+      for (uint32_t ks0 = 0; ks0 < ksteps && !failed; ks0 += F::kStages) {  // ksteps % kStages == 0
+        const uint32_t ph = (ks0 / F::kStages) & 1u;
 #pragma unroll
-        for (uint32_t kk = 0; kk < kGK / 16; ++kk) {
-          const uint64_t bd = smem_desc_sw128(b0 + 32 * kk);
+        for (uint32_t s = 0; s < F::kStages; ++s) {
+          if (!mbar_wait(&full_a[s], ph, spin)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t first = ks0 + s == 0;
 #pragma unroll
-          for (uint32_t hb = 0; hb < kGHalves; ++hb)
-            umma_f16(tmem + hb * kGAccCols, smem_desc_sw128(a0 + hb * kGASub + 32 * kk), bd, idesc, (ks | kk) != 0);
+          for (uint32_t kk = 0; kk < kGK / 16; ++kk) {
+            const uint64_t bd = db + (s * F::kBBytes + 32 * kk) / 16;
+            const uint32_t acc = kk != 0 || !first;
+#pragma unroll
+            for (uint32_t hb = 0; hb < kGHalves; ++hb) {
+              if constexpr (kTA)
+                umma_f16_ts(tmem + hb * F::kAccCols, tmem + F::kACol + s * F::kAStageCols + hb * (kGK / 2) + kk * 8,
+                            bd, idesc, acc);
+              else
+                umma_f16(tmem + hb * F::kAccCols, da + (s * F::kABytes + hb * kGASub + 32 * kk) / 16, bd, idesc, acc);
+            }
+          }
+          umma_commit(&empty_bar[s]);
         }
-        umma_commit(&empty_bar[s]);
       }
       umma_commit(&done_bar);  // the accumulators are final once every MMA above completes
     }
   } else if (warp < kGRawWarp) {
-    // A producers, two groups of 8 warps: thread r (0..255) of group p
-    // dequantizes tile row r's 64 weights of the K steps = p (mod 2) (its
-    // 32-byte qs group, both nibbles: low -> local k 0..31 of sub-block 2j,
-    // high -> local k 32..63 of sub-block 2j+1) into row r%128 of A block
-    // r/128 of stage p.  The raw super-blocks arrive by TMA, one column of
-    // the tile's 256 rows per raw stage (four K steps, two per group); a
-    // step's weights are computed before waiting for its A stage to be free,
-    // so only the stores sit between the tensor core releasing a stage and
-    // refilling it.  A warp covers 32 consecutive rows: the 8 lanes of each
-    // 16-byte store phase hit 8 different swizzled chunks.  Rows past M
-    // arrive as zeros; their accumulator rows are never stored.
-    static_assert(kGStages == kGDqGroups, "group p fills A stage p");
-    const uint32_t pt = threadIdx.x - 64;
-    const uint32_t r = pt % kGRows, grp = pt / kGRows;
-    const uint32_t rb = r & (kGMmaM - 1), sw = rb & 7u;  // 128-byte swizzle: chunk index ^ row%8
+    // A producers, two groups of 8 warps: group p dequantizes the K steps
+    // = p (mod 2), thread (warp w, lane l) tile row r = 128 b + 32 (w % 4) + l
+    // with b = ((w - 2) / 4) % 2 (so that the row's lane of tensor memory is
+    // in the warp's lane quarter), its 64 weights of the step (its 32-byte qs
+    // group, both nibbles: low -> local k 0..31 of sub-block 2j, high -> local
+    // k 32..63 of sub-block 2j+1) into row r % 128 of A block b of the
+    // step's stage.  The raw super-blocks arrive by TMA, one column of the
+    // tile's 256 rows per raw stage (four K steps, two per group); a step's
+    // weights are computed before waiting for its A stage to be free, so only
+    // the stores sit between the tensor core releasing a stage and refilling
+    // it.  A warp covers 32 consecutive rows: the 8 lanes of each 16-byte
+    // shared-memory store phase hit 8 different swizzled chunks.  Rows past M
+    // arrive as zeros; their accumulator rows are never stored.  Waits are
+    // warp-uniform (a vote), as the tensor-memory accesses are warp-wide.
+    const uint32_t e = warp - 2, grp = e >> 3, q = warp & 3u, blk = (e >> 2) & 1u;
+    const uint32_t rb = 32 * q + lane, r = blk * kGMmaM + rb, sw = rb & 7u;  // 128-byte swizzle: chunk ^ row%8
     for (uint32_t ks = grp; ks < ksteps && !failed; ks += kGDqGroups) {
-      const uint32_t sb = ks >> 2, j = ks & 3u, rs = sb % kGRawStages;
+      const uint32_t sb = ks >> 2, j = ks & 3u, rs = sb % F::kRawStages;
       // the group's first K step of this column waits for the column
-      if (j == grp && !mbar_wait(&raw_full[rs], (sb / kGRawStages) & 1u, spin)) {
+      if (j == grp && !__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], (sb / F::kRawStages) & 1u, spin))) {
         failed = true;
         break;
       }
@@ -311,30 +401,35 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
       }
       const RowChunks ch = dequant_group(g, j);
-      const uint32_t s = ks % kGStages, use = ks / kGStages;
-      if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u, spin)) {
+      const uint32_t s = ks % F::kStages, use = ks / F::kStages;
+      if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty_bar[s], (use - 1) & 1u, spin))) {
         failed = true;
         break;
       }
-      uint8_t* dst = sA + s * kGABytes + (r / kGMmaM) * kGASub + rb * 128;
+      if constexpr (kTA) {
+        tc_fence_after();  // the MMAs that read this stage have completed
+        tmem_st32(tmem + ((32u * q) << 16) + F::kACol + s * F::kAStageCols + blk * (kGK / 2), ch.c);
+        tc_fence_before();
+      } else {
+        uint8_t* dst = sA + s * F::kABytes + blk * kGASub + rb * 128;
 #pragma unroll
-      for (uint32_t c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = ch.c[c];
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        for (uint32_t c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = ch.c[c];
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&full_a[s]);
     }
-    // epilogue: producer warp e = w-2 reads accumulator (e/4)%2 (rows
-    // 128*that ..) in its tensor-memory lane quarter w%4, the 32-column
-    // chunks of parity e/8
-    if (!mbar_wait(&done_bar, 0, spin)) {
+    // epilogue: producer warp e reads accumulator blk (rows 128 blk ..) in
+    // its tensor-memory lane quarter w % 4, the 32-column chunks of parity e/8
+    if (!__all_sync(0xffffffffu, mbar_wait(&done_bar, 0, spin))) {
       failed = true;
     } else {
       tc_fence_after();
-      const uint32_t e = warp - 2, q = warp & 3u, hb = (e >> 2) & 1u, half = e >> 3;
-      const uint32_t erow = row0 + hb * kGMmaM + 32 * q + lane;
+      const uint32_t half = e >> 3;
+      const uint32_t erow = row0 + blk * kGMmaM + 32 * q + lane;
       for (uint32_t c0 = 32 * half; c0 < n_mma; c0 += 32 * (kGDqWarps / 8)) {
         float v[32];
-        tmem_ld32(tmem + ((32u * q) << 16) + hb * kGAccCols + c0, v);
+        tmem_ld32(tmem + ((32u * q) << 16) + blk * F::kAccCols + c0, v);
         if (a.parts == 2) {
 #pragma unroll
           for (uint32_t t = 0; t < 16; ++t) {
@@ -352,12 +447,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     }
   } else if (lane == 0) {
     // raw-weight copy warp: super-block column sb of the tile's 256 rows (one
-    // 144-byte box per row) into raw stage sb % 2, once the producers have
-    // taken the column that stage held
+    // 144-byte box per row) into raw stage sb % (raw stages), once the
+    // producers have taken the column that stage held
     const uint32_t nb = N >> 8;
     uint32_t issued = 0;
     for (uint32_t sb = 0; sb < nb; ++sb) {
-      const uint32_t rs = sb % kGRawStages, use = sb / kGRawStages;
+      const uint32_t rs = sb % F::kRawStages, use = sb / F::kRawStages;
       if (use > 0 && !mbar_wait(&raw_empty[rs], (use - 1) & 1u, spin)) {
         failed = true;
         break;
@@ -367,8 +462,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       ++issued;
     }
     // every issued copy has landed before the CTA can exit
-    for (uint32_t sb = (issued > kGRawStages ? issued - kGRawStages : 0); sb < issued; ++sb)
-      if (!mbar_wait(&raw_full[sb % kGRawStages], (sb / kGRawStages) & 1u, spin)) failed = true;
+    for (uint32_t sb = (issued > F::kRawStages ? issued - F::kRawStages : 0); sb < issued; ++sb)
+      if (!mbar_wait(&raw_full[sb % F::kRawStages], (sb / F::kRawStages) & 1u, spin)) failed = true;
   }
   if (failed) atomicOr(a.status, 1u);
   if (warp == 1 && lane == 0 && failed) mbar_wait(&done_bar, 0, spin);  // MMAs still running must finish first
@@ -465,6 +560,23 @@ EncodeTiledFn gemm_encode_fn() {
   return fn;
 }
 
+// One launch of the form that a tile of parts x tile_tokens operand rows uses.
+template <bool kTA>
+cudaError_t launch_form(dim3 grid, const CUtensorMap& bmap, const CUtensorMap& amap, const GemmArgs& ga, int device,
+                        cudaStream_t s) {
+  static std::atomic<uint8_t> attr_set[kAttrDevices];
+  const cudaError_t e = smem_attr_once(attr_set, device, gemm_kernel<kTA>, (int)GemmForm<kTA>::kSmem);
+  if (e != cudaSuccess) return e;
+  gemm_kernel<kTA><<<grid, kGThreads, GemmForm<kTA>::kSmem, s>>>(bmap, amap, ga);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_kernel(dim3 grid, const CUtensorMap& bmap, const CUtensorMap& amap, const GemmArgs& ga,
+                               int device, cudaStream_t s) {
+  return ga.parts * ga.tile_tokens <= kGMaxTsRows ? launch_form<true>(grid, bmap, amap, ga, device, s)
+                                                  : launch_form<false>(grid, bmap, amap, ga, device, s);
+}
+
 }  // namespace
 
 int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
@@ -472,11 +584,6 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
   if (parts != 1 && parts != 2) return ctx_fail(ctx, Q4K_ERR_INVALID_ARG, "parts=%u must be 1 or 2", parts);
   EncodeTiledFn enc = gemm_encode_fn();
   if (!enc) return ctx_fail(ctx, Q4K_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  static std::atomic<uint8_t> attr_set[kAttrDevices];
-  {
-    const cudaError_t e = smem_attr_once(attr_set, ctx->device, gemm_kernel, (int)kGSmem);
-    if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm shared-memory attribute");
-  }
   // activation rows per pass: the B operand (4 bytes per element per row)
   // and the per-row scales fit the context scratch
   uint32_t cap = (uint32_t)(ctx->xfrag_cap / (4ull * N));
@@ -511,9 +618,11 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     const uint32_t row_tiles = (M + kGRows - 1) / kGRows;
     const uint32_t sms = (uint32_t)ctx->sm_count;
     const uint32_t full = 2 * kGTokens / parts, half = full / 2;
-    const uint32_t tile =
+    uint32_t tile =
         (row_tiles * ((tc + full - 1) / full) * 4 <= sms && row_tiles * ((tc + half - 1) / half) <= sms) ? half
                                                                                                         : full;
+    // a batch that fits one TS tile runs as one
+    if (tile == full && gemm_tile_tokens(parts, tc) * parts <= kGMaxTsRows) tile = gemm_tile_tokens(parts, tc);
     CUtensorMap bmap;
     const cuuint64_t dims[2] = {N, (cuuint64_t)parts * tc};
     const cuuint64_t strides[1] = {2ull * N};
@@ -537,8 +646,7 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     ga.tasks = nullptr;
     ga.tiles = nullptr;
     const dim3 grid((M + kGRows - 1) / kGRows, (tc + ga.tile_tokens - 1) / ga.tile_tokens);
-    gemm_kernel<<<grid, kGThreads, kGSmem, s>>>(bmap, amap, ga);
-    e = cudaGetLastError();
+    e = launch_gemm_kernel(grid, bmap, amap, ga, ctx->device, s);
     if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm launch");
     done += tc;
   }
@@ -546,7 +654,11 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
   return Q4K_OK;
 }
 
-uint32_t gemm_tile_tokens(uint32_t parts) { return 2 * kGTokens / parts; }
+uint32_t gemm_tile_tokens(uint32_t parts, uint32_t T) {
+  // the MMA's N (parts x activation rows) is a multiple of 16
+  const uint32_t t = parts == 2 ? (T + 7u) & ~7u : (T + 15u) & ~15u;
+  return parts * t <= kGMaxTsRows ? t : 2 * kGTokens / parts;
+}
 
 uint32_t gemm_tile_rows() { return kGRows; }
 
@@ -571,7 +683,7 @@ cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, 
   if (!enc) return cudaErrorNotSupported;
   const cuuint64_t dims[2] = {N, (cuuint64_t)parts * T};
   const cuuint64_t strides[1] = {2ull * N};
-  const cuuint32_t box[2] = {kGK, parts * gemm_tile_tokens(parts)};
+  const cuuint32_t box[2] = {kGK, parts * gemm_tile_tokens(parts, T)};
   const cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(operand), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -586,21 +698,18 @@ cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, u
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts, int device,
-                              uint32_t* status, uint32_t spin, cudaStream_t s) {
+cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts,
+                              uint32_t tile_tokens, int device, uint32_t* status, uint32_t spin, cudaStream_t s) {
   if (n_tiles == 0) return cudaSuccess;
-  static std::atomic<uint8_t> attr_set[kAttrDevices];
-  cudaError_t e = smem_attr_once(attr_set, device, gemm_kernel, (int)kGSmem);
-  if (e != cudaSuccess) return e;
   GemmArgs ga{};
   ga.parts = parts;
+  ga.tile_tokens = tile_tokens;  // selects the form; each task carries its own
   ga.status = status;
   ga.spin = spin;
   ga.tasks = tasks;
   ga.tiles = tiles;
   const CUtensorMap unused{};
-  gemm_kernel<<<n_tiles, kGThreads, kGSmem, s>>>(unused, unused, ga);
-  return cudaGetLastError();
+  return launch_gemm_kernel(dim3(n_tiles), unused, unused, ga, device, s);
 }
 
 }  // namespace q4k

@@ -444,7 +444,7 @@ int q4k_plan_commit(q4k_plan* p) {
 // rows first so the last wave holds the short tiles.
 static int commit_gemm(q4k_plan* p) {
   q4k_ctx* ctx = p->ctx;
-  const uint32_t T = p->batch, parts = p->parts, tt = gemm_tile_tokens(parts), tr = gemm_tile_rows();
+  const uint32_t T = p->batch, parts = p->parts, tt = gemm_tile_tokens(parts, T), tr = gemm_tile_rows();
   struct Key {
     const float* x;
     uint32_t N;
@@ -573,8 +573,8 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
     for (const Stage& st : p->stages) {
       cudaError_t e = launch_gemm_prep(st.gjobs_dev, st.n_gjobs, p->batch, p->parts, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run GEMM activation prep launch");
-      e = launch_gemm_tasks(st.gtasks_dev, st.tiles_dev, st.n_tiles, p->parts, ctx->device, ctx->select.status,
-                            ctx->select.spin_limit, s);
+      e = launch_gemm_tasks(st.gtasks_dev, st.tiles_dev, st.n_tiles, p->parts, gemm_tile_tokens(p->parts, p->batch),
+                            ctx->device, ctx->select.status, ctx->select.spin_limit, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run GEMM launch");
     }
     ctx->err[0] = 0;

@@ -145,7 +145,7 @@ def test_batched_sweep_f16x_matches_single_calls(ctx):
     bs.close()
 
 
-@pytest.mark.parametrize("T,exact", [(64, True), (300, False), (512, False), (65, True)])
+@pytest.mark.parametrize("T,exact", [(64, True), (64, False), (100, False), (128, False), (300, False), (512, False), (65, True)])
 def test_gemm_plan_one_launch_per_stage_matches_oracle(ctx, oracle, T, exact):
     """A batch >= 64 plan runs each stage as one preparation launch plus ONE
     GEMM launch over all its matrices (two layers' q/k/v/o/gate/up, then
