@@ -102,6 +102,7 @@ cudaError_t gemm_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_
 cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, uint32_t T, uint32_t parts);
 cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, cudaStream_t s);
 cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts,
-                              uint32_t tile_tokens, int device, uint32_t* status, uint32_t spin, cudaStream_t s);
+                              uint32_t tile_tokens, uint32_t sms, int device, uint32_t* status, uint32_t spin,
+                              cudaStream_t s);
 
 }  // namespace q4k

@@ -190,7 +190,8 @@ struct GemmArgs {
   uint32_t* status;        // bit 0: a bounded wait expired
   uint32_t spin;           // polls per bounded wait (0: kSpinLimit)
   const GemmTask* tasks;   // multi-matrix launch: task table (null: the single matrix above)
-  const uint2* tiles;      // multi-matrix launch: CTA b's tile = (task, row tile | token tile << 16)
+  const uint2* tiles;      // multi-matrix launch: tile i = (task, row tile | token tile << 16)
+  uint32_t n_tiles;        // tiles of the launch; CTA b takes tiles b, b + gridDim.x, ...
 };
 
 // The raw Q4_K bytes one A-producer thread (one row) needs for one K step:
@@ -228,6 +229,51 @@ __device__ __forceinline__ RowChunks dequant_group(const RawGroup& g, uint32_t j
   return o;
 }
 
+// Tile i of a launch: an entry of the multi-matrix tile table, or of the
+// single matrix's (row tile, token tile) grid, row tiles fastest.
+struct GemmTile {
+  const CUtensorMap* amap;
+  const CUtensorMap* bmap;
+  float* y;
+  const float* inv_scale;
+  uint32_t M, N, T, tile_tokens, row0, tok0, n_mma;
+};
+
+__device__ __forceinline__ GemmTile gemm_tile(const GemmArgs& a, const CUtensorMap* amap, const CUtensorMap* bmap,
+                                              uint32_t i) {
+  GemmTile t;
+  if (a.tiles) {
+    const uint2 tl = a.tiles[i];
+    const GemmTask& tk = a.tasks[tl.x];
+    t.amap = tk.amap;
+    t.bmap = tk.bmap;
+    t.y = tk.y;
+    t.inv_scale = tk.inv_scale;
+    t.M = tk.M;
+    t.N = tk.N;
+    t.T = tk.T;
+    t.tile_tokens = tk.tile_tokens;
+    t.row0 = (tl.y & 0xffffu) * kGRows;
+    t.tok0 = (tl.y >> 16) * t.tile_tokens;
+  } else {
+    const uint32_t row_tiles = (a.M + kGRows - 1) / kGRows;
+    t.amap = amap;
+    t.bmap = bmap;
+    t.y = a.y;
+    t.inv_scale = a.inv_scale;
+    t.M = a.M;
+    t.N = a.N;
+    t.T = a.T;
+    t.tile_tokens = a.tile_tokens;
+    t.row0 = (i % row_tiles) * kGRows;
+    t.tok0 = (i / row_tiles) * a.tile_tokens;
+  }
+  // MMA N: the tile's operand rows, a multiple of 16
+  const uint32_t ntok = min(t.tile_tokens, t.T - t.tok0);
+  t.n_mma = a.parts == 2 ? 2u * ((ntok + 7u) & ~7u) : ((ntok + 15u) & ~15u);
+  return t;
+}
+
 template <bool kTA>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap bmap,
                                                             const __grid_constant__ CUtensorMap amap, const GemmArgs a) {
@@ -239,40 +285,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   uint8_t* sA = smem;
   uint8_t* sB = smem + F::kStages * F::kABytes;
   uint8_t* sRaw = sB + F::kStages * F::kBBytes;
-  __shared__ uint64_t full_a[F::kStages], full_b[F::kStages], empty_bar[F::kStages], done_bar;
+  __shared__ uint64_t full_a[F::kStages], full_b[F::kStages], empty_bar[F::kStages], done_bar, acc_empty, drain_bar;
   __shared__ uint64_t raw_full[F::kRawStages], raw_empty[F::kRawStages];
   __shared__ uint32_t s_tmem;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  // This CTA's tile: of the single matrix (grid = row tiles x token tiles),
-  // or one entry of a multi-matrix launch's tile table.
-  const CUtensorMap* pamap = &amap;
-  const CUtensorMap* pbmap = &bmap;
-  float* y = a.y;
-  const float* inv_scale = a.inv_scale;
-  uint32_t M = a.M, N = a.N, T = a.T, tile_tokens = a.tile_tokens, row0, tok0;
-  if (a.tiles) {
-    const uint2 tl = a.tiles[blockIdx.x];
-    const GemmTask& tk = a.tasks[tl.x];
-    pamap = tk.amap;
-    pbmap = tk.bmap;
-    y = tk.y;
-    inv_scale = tk.inv_scale;
-    M = tk.M;
-    N = tk.N;
-    T = tk.T;
-    tile_tokens = tk.tile_tokens;
-    row0 = (tl.y & 0xffffu) * kGRows;
-    tok0 = (tl.y >> 16) * tile_tokens;
-  } else {
-    row0 = blockIdx.x * kGRows;
-    tok0 = blockIdx.y * tile_tokens;
-  }
-  const uint32_t ntok = min(tile_tokens, T - tok0);
-  const uint32_t b_bytes = a.parts * tile_tokens * kGK * 2;  // one B box
-  // MMA N: the tile's operand rows, a multiple of 16
-  const uint32_t n_mma = a.parts == 2 ? 2u * ((ntok + 7u) & ~7u) : ((ntok + 15u) & ~15u);
-  const uint32_t ksteps = N / kGK;
+  const uint32_t n_tiles = a.n_tiles;
   bool failed = false;
 
   if (threadIdx.x == 0) {
@@ -282,6 +300,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&done_bar, 1);
+    mbar_init(&acc_empty, kGDqWarps);
+    mbar_init(&drain_bar, 1);
     for (uint32_t s = 0; s < F::kRawStages; ++s) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], kGDqWarps);  // every producer warp takes some K steps of each column
@@ -299,36 +319,50 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
+  // Every role walks the same tiles (blockIdx.x, + gridDim.x, ...) and keeps
+  // its ring counters across them: gk counts K steps, gsb raw columns, so the
+  // stage phases continue from tile to tile and the copies of the next tile
+  // start while this one finishes.  A tile's K steps are a multiple of 4, so
+  // every tile starts at stage 0 of both rings' unrolled walks.
   if (warp == 0) {
     // B producer: one TMA box (parts x tile_tokens operand rows x 64 halves) per stage
     if (lane == 0) {
-      uint32_t issued = 0;
-      for (uint32_t ks = 0; ks < ksteps; ++ks) {
-        const uint32_t s = ks % F::kStages, use = ks / F::kStages;
-        if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u, spin)) {
-          failed = true;
-          break;
+      uint32_t gk = 0;
+      for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x) {
+        const GemmTile t = gemm_tile(a, &amap, &bmap, i);
+        const uint32_t b_bytes = a.parts * t.tile_tokens * kGK * 2;  // one B box
+        for (uint32_t ks = 0; ks < t.N / kGK; ++ks, ++gk) {
+          const uint32_t s = gk % F::kStages, use = gk / F::kStages;
+          if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u, spin)) {
+            failed = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_b[s], b_bytes);
+          tma_tile_g2s(sB + s * F::kBBytes, t.bmap, ks * kGK, a.parts * t.tok0, &full_b[s]);
         }
-        mbar_arrive_expect_tx(&full_b[s], b_bytes);
-        tma_tile_g2s(sB + s * F::kBBytes, pbmap, ks * kGK, a.parts * tok0, &full_b[s]);
-        ++issued;
       }
       // every issued copy has landed before the CTA can exit
-      for (uint32_t ks = (issued > F::kStages ? issued - F::kStages : 0); ks < issued; ++ks)
-        if (!mbar_wait(&full_b[ks % F::kStages], (ks / F::kStages) & 1u, spin)) failed = true;
+      for (uint32_t g = (gk > F::kStages ? gk - F::kStages : 0); g < gk; ++g)
+        if (!mbar_wait(&full_b[g % F::kStages], (g / F::kStages) & 1u, spin)) failed = true;
     } else if (lane == 1) {
       // relay: once a step's B copy has landed, one more arrival on the
-      // stage's A barrier, so the MMA thread waits on one barrier per step
-      // (each wait on an already completed barrier cost it ~0.2 us inside
-      // the busy kernel).  It cannot fall two phases behind: the copy of step
-      // ks + kStages needs the MMAs of step ks, which need this arrival.
-      for (uint32_t ks = 0; ks < ksteps; ++ks) {
-        const uint32_t s = ks % F::kStages;
-        if (!mbar_wait(&full_b[s], (ks / F::kStages) & 1u, spin)) {
-          failed = true;
-          break;
+      // stage's A barrier, so the MMA thread waits on one barrier per step.
+      // A wait issued right after MMAs costs that thread about as much as
+      // waiting for those MMAs to complete (measured on B200), so it waits
+      // as rarely as it can.  The relay cannot fall two phases behind: the
+      // copy of step gk + kStages needs the MMAs of step gk, which need this
+      // arrival.
+      uint32_t gk = 0;
+      for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x) {
+        const uint32_t ksteps = gemm_tile(a, &amap, &bmap, i).N / kGK;
+        for (uint32_t ks = 0; ks < ksteps; ++ks, ++gk) {
+          const uint32_t s = gk % F::kStages;
+          if (!mbar_wait(&full_b[s], (gk / F::kStages) & 1u, spin)) {
+            failed = true;
+            break;
+          }
+          mbar_arrive(&full_a[s]);
         }
-        mbar_arrive(&full_a[s]);
       }
     }
   } else if (warp == 1) {
@@ -339,36 +373,53 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       // plus constants (descriptor address fields count 16-byte units): the
       // single issuing thread paces the pipeline at small N, and per-MMA
       // address arithmetic on its dependency chain cost ~9% at T = 64.
-      const uint32_t idesc = idesc_f16(n_mma);
       const uint64_t db = smem_desc_sw128(smem_u32(sB));
       const uint64_t da = smem_desc_sw128(smem_u32(sA));
-      for (uint32_t ks0 = 0; ks0 < ksteps && !failed; ks0 += F::kStages) {  // ksteps % kStages == 0
-        const uint32_t ph = (ks0 / F::kStages) & 1u;
-#pragma unroll
-        for (uint32_t s = 0; s < F::kStages; ++s) {
-          if (!mbar_wait(&full_a[s], ph, spin)) {
+      uint32_t gk0 = 0, tcount = 0;
+      for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x, ++tcount) {
+        const GemmTile t = gemm_tile(a, &amap, &bmap, i);
+        const uint32_t idesc = idesc_f16(t.n_mma), ksteps = t.N / kGK;
+        // the epilogue has read the previous tile's accumulators
+        if (tcount > 0) {
+          if (!mbar_wait(&acc_empty, (tcount - 1) & 1u, spin)) {
             failed = true;
             break;
           }
           tc_fence_after();
-          const uint32_t first = ks0 + s == 0;
-#pragma unroll
-          for (uint32_t kk = 0; kk < kGK / 16; ++kk) {
-            const uint64_t bd = db + (s * F::kBBytes + 32 * kk) / 16;
-            const uint32_t acc = kk != 0 || !first;
-#pragma unroll
-            for (uint32_t hb = 0; hb < kGHalves; ++hb) {
-              if constexpr (kTA)
-                umma_f16_ts(tmem + hb * F::kAccCols, tmem + F::kACol + s * F::kAStageCols + hb * (kGK / 2) + kk * 8,
-                            bd, idesc, acc);
-              else
-                umma_f16(tmem + hb * F::kAccCols, da + (s * F::kABytes + hb * kGASub + 32 * kk) / 16, bd, idesc, acc);
-            }
-          }
-          umma_commit(&empty_bar[s]);
         }
+        for (uint32_t ks0 = 0; ks0 < ksteps && !failed; ks0 += F::kStages) {  // ksteps % kStages == 0
+          const uint32_t ph = ((gk0 + ks0) / F::kStages) & 1u;
+#pragma unroll
+          for (uint32_t s = 0; s < F::kStages; ++s) {
+            if (!mbar_wait(&full_a[s], ph, spin)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t first = ks0 + s == 0;
+#pragma unroll
+            for (uint32_t kk = 0; kk < kGK / 16; ++kk) {
+              const uint64_t bd = db + (s * F::kBBytes + 32 * kk) / 16;
+              const uint32_t acc = kk != 0 || !first;
+#pragma unroll
+              for (uint32_t hb = 0; hb < kGHalves; ++hb) {
+                if constexpr (kTA)
+                  umma_f16_ts(tmem + hb * F::kAccCols,
+                              tmem + F::kACol + s * F::kAStageCols + hb * (kGK / 2) + kk * 8, bd, idesc, acc);
+                else
+                  umma_f16(tmem + hb * F::kAccCols, da + (s * F::kABytes + hb * kGASub + 32 * kk) / 16, bd, idesc,
+                           acc);
+              }
+            }
+            umma_commit(&empty_bar[s]);
+          }
+        }
+        if (!failed) umma_commit(&done_bar);  // the accumulators are final once every MMA above completes
+        gk0 += ksteps;
       }
-      umma_commit(&done_bar);  // the accumulators are final once every MMA above completes
+      // no MMA may still run when tensor memory is freed
+      umma_commit(&drain_bar);
+      if (!mbar_wait(&drain_bar, 0, spin)) failed = true;
     }
   } else if (warp < kGRawWarp) {
     // A producers, two groups of 8 warps: group p dequantizes the K steps
@@ -387,86 +438,106 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     // warp-uniform (a vote), as the tensor-memory accesses are warp-wide.
     const uint32_t e = warp - 2, grp = e >> 3, q = warp & 3u, blk = (e >> 2) & 1u;
     const uint32_t rb = 32 * q + lane, r = blk * kGMmaM + rb, sw = rb & 7u;  // 128-byte swizzle: chunk ^ row%8
-    for (uint32_t ks = grp; ks < ksteps && !failed; ks += kGDqGroups) {
-      const uint32_t sb = ks >> 2, j = ks & 3u, rs = sb % F::kRawStages;
-      // the group's first K step of this column waits for the column
-      if (j == grp && !__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], (sb / F::kRawStages) & 1u, spin))) {
-        failed = true;
-        break;
-      }
-      const RawGroup g = raw_group(sRaw + rs * kGRawBytes + r * kBlockBytes, j);
-      if (j + kGDqGroups >= 4) {
-        // the group's last K step of this column is in registers: hand it back
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
-      }
-      const RowChunks ch = dequant_group(g, j);
-      const uint32_t s = ks % F::kStages, use = ks / F::kStages;
-      if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty_bar[s], (use - 1) & 1u, spin))) {
-        failed = true;
-        break;
-      }
-      if constexpr (kTA) {
-        tc_fence_after();  // the MMAs that read this stage have completed
-        tmem_st32(tmem + ((32u * q) << 16) + F::kACol + s * F::kAStageCols + blk * (kGK / 2), ch.c);
-        tc_fence_before();
-      } else {
-        uint8_t* dst = sA + s * F::kABytes + blk * kGASub + rb * 128;
+    uint32_t gk0 = 0, gsb0 = 0, tcount = 0;
+    for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x, ++tcount) {
+      const GemmTile t = gemm_tile(a, &amap, &bmap, i);
+      const uint32_t ksteps = t.N / kGK;
+      for (uint32_t ks = grp; ks < ksteps; ks += kGDqGroups) {
+        const uint32_t gsb = gsb0 + (ks >> 2), j = ks & 3u, rs = gsb % F::kRawStages;
+        // the group's first K step of this column waits for the column
+        if (j == grp && !__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], (gsb / F::kRawStages) & 1u, spin))) {
+          failed = true;
+          break;
+        }
+        const RawGroup g = raw_group(sRaw + rs * kGRawBytes + r * kBlockBytes, j);
+        if (j + kGDqGroups >= 4) {
+          // the group's last K step of this column is in registers: hand it back
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        }
+        const RowChunks ch = dequant_group(g, j);
+        const uint32_t gk = gk0 + ks, s = gk % F::kStages, use = gk / F::kStages;
+        if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty_bar[s], (use - 1) & 1u, spin))) {
+          failed = true;
+          break;
+        }
+        if constexpr (kTA) {
+          tc_fence_after();  // the MMAs that read this stage have completed
+          tmem_st32(tmem + ((32u * q) << 16) + F::kACol + s * F::kAStageCols + blk * (kGK / 2), ch.c);
+          tc_fence_before();
+        } else {
+          uint8_t* dst = sA + s * F::kABytes + blk * kGASub + rb * 128;
 #pragma unroll
-        for (uint32_t c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = ch.c[c];
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+          for (uint32_t c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = ch.c[c];
+          fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[s]);
-    }
-    // epilogue: producer warp e reads accumulator blk (rows 128 blk ..) in
-    // its tensor-memory lane quarter w % 4, the 32-column chunks of parity e/8
-    if (!__all_sync(0xffffffffu, mbar_wait(&done_bar, 0, spin))) {
-      failed = true;
-    } else {
+      if (failed) break;
+      gk0 += ksteps;
+      gsb0 += ksteps >> 2;
+      // epilogue: producer warp e reads accumulator blk (rows 128 blk ..) in
+      // its tensor-memory lane quarter w % 4, the 32-column chunks of parity
+      // e/8, then hands the accumulators back to the MMA thread
+      if (!__all_sync(0xffffffffu, mbar_wait(&done_bar, tcount & 1u, spin))) {
+        failed = true;
+        break;
+      }
       tc_fence_after();
-      const uint32_t half = e >> 3;
-      const uint32_t erow = row0 + blk * kGMmaM + 32 * q + lane;
-      for (uint32_t c0 = 32 * half; c0 < n_mma; c0 += 32 * (kGDqWarps / 8)) {
+      const uint32_t half = e >> 3, ntok = min(t.tile_tokens, t.T - t.tok0);
+      const uint32_t erow = t.row0 + blk * kGMmaM + 32 * q + lane;
+      for (uint32_t c0 = 32 * half; c0 < t.n_mma; c0 += 32 * (kGDqWarps / 8)) {
         float v[32];
         tmem_ld32(tmem + ((32u * q) << 16) + blk * F::kAccCols + c0, v);
+        if (c0 + 32 * (kGDqWarps / 8) >= t.n_mma) {
+          // this warp's last accumulator chunk is in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty);
+        }
         if (a.parts == 2) {
 #pragma unroll
-          for (uint32_t t = 0; t < 16; ++t) {
-            const uint32_t tok = tok0 + c0 / 2 + t;
-            if (tok < T && erow < M) y[(size_t)tok * M + erow] = (v[2 * t] + v[2 * t + 1]) * inv_scale[tok];
+          for (uint32_t u = 0; u < 16; ++u) {
+            const uint32_t tl = c0 / 2 + u;
+            if (tl < ntok && erow < t.M) t.y[(size_t)(t.tok0 + tl) * t.M + erow] = (v[2 * u] + v[2 * u + 1]) * t.inv_scale[t.tok0 + tl];
           }
         } else {
 #pragma unroll
-          for (uint32_t t = 0; t < 32; ++t) {
-            const uint32_t tok = tok0 + c0 + t;
-            if (tok < T && erow < M) y[(size_t)tok * M + erow] = v[t] * inv_scale[tok];
+          for (uint32_t u = 0; u < 32; ++u) {
+            const uint32_t tl = c0 + u;
+            if (tl < ntok && erow < t.M) t.y[(size_t)(t.tok0 + tl) * t.M + erow] = v[u] * t.inv_scale[t.tok0 + tl];
           }
         }
+      }
+      if (32 * half >= t.n_mma) {
+        // no chunk for this warp (n_mma <= 32): nothing held
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty);
       }
     }
   } else if (lane == 0) {
     // raw-weight copy warp: super-block column sb of the tile's 256 rows (one
-    // 144-byte box per row) into raw stage sb % (raw stages), once the
+    // 144-byte box per row) into raw stage gsb % (raw stages), once the
     // producers have taken the column that stage held
-    const uint32_t nb = N >> 8;
-    uint32_t issued = 0;
-    for (uint32_t sb = 0; sb < nb; ++sb) {
-      const uint32_t rs = sb % F::kRawStages, use = sb / F::kRawStages;
-      if (use > 0 && !mbar_wait(&raw_empty[rs], (use - 1) & 1u, spin)) {
-        failed = true;
-        break;
+    uint32_t gsb = 0;
+    for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x) {
+      const GemmTile t = gemm_tile(a, &amap, &bmap, i);
+      for (uint32_t sb = 0; sb < (t.N >> 8); ++sb, ++gsb) {
+        const uint32_t rs = gsb % F::kRawStages, use = gsb / F::kRawStages;
+        if (use > 0 && !mbar_wait(&raw_empty[rs], (use - 1) & 1u, spin)) {
+          failed = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&raw_full[rs], kGRawBytes);
+        tma_tile_g2s(sRaw + rs * kGRawBytes, t.amap, sb * (kBlockBytes / 4), t.row0, &raw_full[rs]);
       }
-      mbar_arrive_expect_tx(&raw_full[rs], kGRawBytes);
-      tma_tile_g2s(sRaw + rs * kGRawBytes, pamap, sb * (kBlockBytes / 4), row0, &raw_full[rs]);
-      ++issued;
     }
     // every issued copy has landed before the CTA can exit
-    for (uint32_t sb = (issued > F::kRawStages ? issued - F::kRawStages : 0); sb < issued; ++sb)
-      if (!mbar_wait(&raw_full[sb % F::kRawStages], (sb / F::kRawStages) & 1u, spin)) failed = true;
+    for (uint32_t g = (gsb > F::kRawStages ? gsb - F::kRawStages : 0); g < gsb; ++g)
+      if (!mbar_wait(&raw_full[g % F::kRawStages], (g / F::kRawStages) & 1u, spin)) failed = true;
   }
   if (failed) atomicOr(a.status, 1u);
-  if (warp == 1 && lane == 0 && failed) mbar_wait(&done_bar, 0, spin);  // MMAs still running must finish first
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -562,8 +633,8 @@ EncodeTiledFn gemm_encode_fn() {
 
 // One launch of the form that a tile of parts x tile_tokens operand rows uses.
 template <bool kTA>
-cudaError_t launch_form(dim3 grid, const CUtensorMap& bmap, const CUtensorMap& amap, const GemmArgs& ga, int device,
-                        cudaStream_t s) {
+cudaError_t launch_form(uint32_t grid, const CUtensorMap& bmap, const CUtensorMap& amap, const GemmArgs& ga,
+                        int device, cudaStream_t s) {
   static std::atomic<uint8_t> attr_set[kAttrDevices];
   const cudaError_t e = smem_attr_once(attr_set, device, gemm_kernel<kTA>, (int)GemmForm<kTA>::kSmem);
   if (e != cudaSuccess) return e;
@@ -571,8 +642,10 @@ cudaError_t launch_form(dim3 grid, const CUtensorMap& bmap, const CUtensorMap& a
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_kernel(dim3 grid, const CUtensorMap& bmap, const CUtensorMap& amap, const GemmArgs& ga,
+// Persistent: one CTA per SM (at most one per tile), each walking its tiles.
+cudaError_t launch_gemm_kernel(const CUtensorMap& bmap, const CUtensorMap& amap, const GemmArgs& ga, uint32_t sms,
                                int device, cudaStream_t s) {
+  const uint32_t grid = ga.n_tiles < sms ? ga.n_tiles : sms;
   return ga.parts * ga.tile_tokens <= kGMaxTsRows ? launch_form<true>(grid, bmap, amap, ga, device, s)
                                                   : launch_form<false>(grid, bmap, amap, ga, device, s);
 }
@@ -645,8 +718,8 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     ga.spin = ctx->select.spin_limit;
     ga.tasks = nullptr;
     ga.tiles = nullptr;
-    const dim3 grid((M + kGRows - 1) / kGRows, (tc + ga.tile_tokens - 1) / ga.tile_tokens);
-    e = launch_gemm_kernel(grid, bmap, amap, ga, ctx->device, s);
+    ga.n_tiles = row_tiles * ((tc + ga.tile_tokens - 1) / ga.tile_tokens);
+    e = launch_gemm_kernel(bmap, amap, ga, sms, ctx->device, s);
     if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_gemm launch");
     done += tc;
   }
@@ -699,7 +772,8 @@ cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, u
 }
 
 cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts,
-                              uint32_t tile_tokens, int device, uint32_t* status, uint32_t spin, cudaStream_t s) {
+                              uint32_t tile_tokens, uint32_t sms, int device, uint32_t* status, uint32_t spin,
+                              cudaStream_t s) {
   if (n_tiles == 0) return cudaSuccess;
   GemmArgs ga{};
   ga.parts = parts;
@@ -708,8 +782,9 @@ cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_
   ga.spin = spin;
   ga.tasks = tasks;
   ga.tiles = tiles;
+  ga.n_tiles = n_tiles;
   const CUtensorMap unused{};
-  return launch_gemm_kernel(dim3(n_tiles), unused, unused, ga, device, s);
+  return launch_gemm_kernel(unused, unused, ga, sms, device, s);
 }
 
 }  // namespace q4k

@@ -574,7 +574,7 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
       cudaError_t e = launch_gemm_prep(st.gjobs_dev, st.n_gjobs, p->batch, p->parts, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run GEMM activation prep launch");
       e = launch_gemm_tasks(st.gtasks_dev, st.tiles_dev, st.n_tiles, p->parts, gemm_tile_tokens(p->parts, p->batch),
-                            ctx->device, ctx->select.status, ctx->select.spin_limit, s);
+                            (uint32_t)ctx->sm_count, ctx->device, ctx->select.status, ctx->select.spin_limit, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run GEMM launch");
     }
     ctx->err[0] = 0;
