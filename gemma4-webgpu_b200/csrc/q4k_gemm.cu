@@ -496,17 +496,23 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty);
         }
+        // the chunk's per-token scales: one load per lane before any store
+        // (y and the scales could alias, which would order every scale load
+        // after the previous store), then broadcast
+        const uint32_t tl0 = a.parts == 2 ? c0 / 2 : c0;
+        const float my_scale = tl0 + lane < ntok ? t.inv_scale[t.tok0 + tl0 + lane] : 0.0f;
+        float* ycol = t.y + (size_t)(t.tok0 + tl0) * t.M + erow;
         if (a.parts == 2) {
 #pragma unroll
           for (uint32_t u = 0; u < 16; ++u) {
-            const uint32_t tl = c0 / 2 + u;
-            if (tl < ntok && erow < t.M) t.y[(size_t)(t.tok0 + tl) * t.M + erow] = (v[2 * u] + v[2 * u + 1]) * t.inv_scale[t.tok0 + tl];
+            const float sc = __shfl_sync(0xffffffffu, my_scale, u);
+            if (tl0 + u < ntok && erow < t.M) ycol[(size_t)u * t.M] = (v[2 * u] + v[2 * u + 1]) * sc;
           }
         } else {
 #pragma unroll
           for (uint32_t u = 0; u < 32; ++u) {
-            const uint32_t tl = c0 + u;
-            if (tl < ntok && erow < t.M) t.y[(size_t)(t.tok0 + tl) * t.M + erow] = v[u] * t.inv_scale[t.tok0 + tl];
+            const float sc = __shfl_sync(0xffffffffu, my_scale, u);
+            if (tl0 + u < ntok && erow < t.M) ycol[(size_t)u * t.M] = v[u] * sc;
           }
         }
       }
