@@ -13,18 +13,18 @@
 // (2 x 256 columns); both blocks read the same B tile, so the activation
 // operand is fetched once per 256 weight rows.  Per 64-wide K step:
 //   * the B operand, x split exactly into f16 hi + lo parts (two operand rows
-//     per activation row, scaled per row by a power of two), arrives by one
-//     TMA tensor copy in the 128-byte swizzled K-major layout;
+//     per activation row, scaled per row by a power of two), arrives by TMA
+//     tensor copies in a swizzled K-major layout (two K = 32 stages);
 //   * the A operand, the 256 x 64 f16 weights, is dequantized by 16 warps
-//     (two groups of 8, one per K-step parity, each filling its own stage)
-//     into the same swizzled layout, computed before the stage is free and
-//     stored once it is; the raw Q4_K super-blocks reach shared memory by
+//     (two groups of 8, one per K-step parity, each filling its own stages)
+//     into the same swizzled layout, computed before the stages are free and
+//     stored once they are; the raw Q4_K super-blocks reach shared memory by
 //     TMA, one 144-byte box per tile row per super-block column (four K
 //     steps), two columns in flight (a copy warp of its own);
 //   * one thread issues the 8 MMAs and commits them to the stage's "empty"
 //     barrier, which frees the stage for the producers; it waits on one
 //     barrier per step, the producers' plus a relay arrival once B landed.
-// Two operand stages are in flight.  Tiles of at most 128 operand rows (a
+// Four K = 32 operand stages are in flight.  Tiles of at most 128 operand rows (a
 // batch of up to 128 f16 or 64 exact activation rows) run the TS form
 // instead (GemmForm below): the weights go straight into tensor memory, four
 // stages in flight.  The epilogue (the 16 producer warps: per
@@ -54,11 +54,7 @@ constexpr uint32_t kGMmaM = 128;                        // MMA M = TMEM lanes
 constexpr uint32_t kGHalves = 2;                        // MMA row blocks per CTA (one accumulator each)
 constexpr uint32_t kGRows = kGMmaM * kGHalves;          // weight rows per CTA tile
 constexpr uint32_t kGTokens = 128;                      // max activation rows per tile (MMA N = 2 per row)
-constexpr uint32_t kGK = 64;                            // K per stage: 128 bytes of f16 per operand row
-constexpr uint32_t kGStages = 2;
-constexpr uint32_t kGASub = kGMmaM * kGK * 2;           // 16 KB: one 128-row A block
-constexpr uint32_t kGABytes = kGHalves * kGASub;        // 32 KB
-constexpr uint32_t kGBBytes = 2 * kGTokens * kGK * 2;   // 32 KB
+constexpr uint32_t kGK = 64;                            // K per producer step (one 32-byte qs group per row)
 constexpr uint32_t kGDqGroups = 2;                      // producer groups: group p takes the K steps = p (mod 2)
 constexpr uint32_t kGDqWarps = 8 * kGDqGroups;          // dequantizing warps (8 per group), also the epilogue
 constexpr uint32_t kGRawWarp = 2 + kGDqWarps;            // the raw-weight copy warp
@@ -69,7 +65,10 @@ constexpr uint32_t kGAccCols = 2 * kGTokens;            // fp32 columns of one a
 constexpr uint32_t kGTmemCols = kGHalves * kGAccCols;   // 512: all of tensor memory
 
 // The two forms of the kernel.  SS: both operands in shared memory, tiles of
-// up to 256 operand rows (MMA N <= 256), two stages.  TS (tiles of at most
+// up to 256 operand rows (MMA N <= 256), four stages of K = 32 in the 64-byte
+// swizzled layout (two 64-wide K steps in flight, but a stage's B copy is
+// issued half a step sooner than with two stages of K = 64: the B copy
+// from L2 took ~0.65 us against ~0.5 us of MMAs per K step).  TS (tiles of at most
 // 128 operand rows): the producers store the weights straight into tensor
 // memory (tcgen05.st) and the MMA reads A from there.  A single-thread
 // stream of M = 128 kind::f16 MMAs measured on B200 costs ~89 cycles per
@@ -82,25 +81,32 @@ constexpr uint32_t kGTmemCols = kGHalves * kGAccCols;   // 512: all of tensor me
 // shared memory holds four B stages and four raw super-block columns.
 template <bool kTA>
 struct GemmForm {
-  static constexpr uint32_t kStages = kTA ? 4 : kGStages;
-  static constexpr uint32_t kABytes = kTA ? 0 : kGABytes;                // smem A stage
-  static constexpr uint32_t kBBytes = kTA ? 128 * kGK * 2 : kGBBytes;   // smem B stage (largest box)
+  static constexpr uint32_t kStages = 4;
+  static constexpr uint32_t kStageK = kTA ? kGK : kGK / 2;              // K per operand stage
+  static constexpr uint32_t kRowBytes = kStageK * 2;                    // operand row: 128 (TS B) or 64 bytes
+  static constexpr uint32_t kSbo = 8 * kRowBytes;                       // bytes between 8-row groups
+  static constexpr uint32_t kLayout = kTA ? 2 : 4;                      // descriptor swizzle: 128 B / 64 B
+  static constexpr uint32_t kASub = kGMmaM * kRowBytes;                 // smem A block (SS)
+  static constexpr uint32_t kABytes = kTA ? 0 : kGHalves * kASub;       // smem A stage
+  static constexpr uint32_t kBBytes = (kTA ? 128 : 2 * kGTokens) * kRowBytes;  // smem B stage (largest box)
   static constexpr uint32_t kAccCols = kTA ? 128 : kGAccCols;          // tensor-memory columns per accumulator
   static constexpr uint32_t kACol = kGHalves * kAccCols;               // first A column (TS)
   static constexpr uint32_t kAStageCols = kGHalves * (kGK / 2);        // A columns per stage (TS)
   static constexpr uint32_t kRawStages = kTA ? 4 : kGRawStages;        // raw super-block columns in flight
+  static constexpr uint32_t kStepsPerBlock = 256 / kStageK;            // operand stages per super-block column
   static constexpr size_t kSmem = 1024 + (size_t)kStages * (kABytes + kBBytes) + (size_t)kRawStages * kGRawBytes;
   static_assert(!kTA || kACol + kStages * kAStageCols <= kGTmemCols, "TS tensor-memory layout");
-  static_assert(kStages % kGDqGroups == 0, "each stage is filled by one producer group");
+  static_assert(kStages % (2 * kGK / kStageK) == 0, "a 64-wide K step's stages are filled by one producer group");
 };
 constexpr uint32_t kGMaxTsRows = 128;  // operand rows per tile up to which the TS form runs
 
-// UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzled
-// layout: 128-byte rows, 8-row groups 1024 bytes apart (stride offset), the
-// leading offset unused (1), descriptor version 1, layout type 2 (128B).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+// UMMA shared-memory descriptor of a K-major tile in a swizzled layout:
+// rows of 128 (layout 2, 128-byte swizzle) or 64 bytes (layout 4, 64-byte
+// swizzle), 8-row groups `sbo` bytes apart (stride offset), the leading
+// offset unused (1), descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t sbo, uint32_t layout) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(sbo >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)layout << 61);
 }
 
 // Instruction descriptor, kind::f16: D fp32, A and B f16 and K-major, M = 128.
@@ -330,15 +336,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       uint32_t gk = 0;
       for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x) {
         const GemmTile t = gemm_tile(a, &amap, &bmap, i);
-        const uint32_t b_bytes = a.parts * t.tile_tokens * kGK * 2;  // one B box
-        for (uint32_t ks = 0; ks < t.N / kGK; ++ks, ++gk) {
+        const uint32_t b_bytes = a.parts * t.tile_tokens * F::kRowBytes;  // one B box
+        for (uint32_t ks = 0; ks < t.N / F::kStageK; ++ks, ++gk) {
           const uint32_t s = gk % F::kStages, use = gk / F::kStages;
           if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1u, spin)) {
             failed = true;
             break;
           }
           mbar_arrive_expect_tx(&full_b[s], b_bytes);
-          tma_tile_g2s(sB + s * F::kBBytes, t.bmap, ks * kGK, a.parts * t.tok0, &full_b[s]);
+          tma_tile_g2s(sB + s * F::kBBytes, t.bmap, ks * F::kStageK, a.parts * t.tok0, &full_b[s]);
         }
       }
       // every issued copy has landed before the CTA can exit
@@ -354,7 +360,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       // arrival.
       uint32_t gk = 0;
       for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x) {
-        const uint32_t ksteps = gemm_tile(a, &amap, &bmap, i).N / kGK;
+        const uint32_t ksteps = gemm_tile(a, &amap, &bmap, i).N / F::kStageK;
         for (uint32_t ks = 0; ks < ksteps; ++ks, ++gk) {
           const uint32_t s = gk % F::kStages;
           if (!mbar_wait(&full_b[s], (gk / F::kStages) & 1u, spin)) {
@@ -373,12 +379,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       // plus constants (descriptor address fields count 16-byte units): the
       // single issuing thread paces the pipeline at small N, and per-MMA
       // address arithmetic on its dependency chain cost ~9% at T = 64.
-      const uint64_t db = smem_desc_sw128(smem_u32(sB));
-      const uint64_t da = smem_desc_sw128(smem_u32(sA));
+      const uint64_t db = smem_desc(smem_u32(sB), F::kSbo, F::kLayout);
+      const uint64_t da = smem_desc(smem_u32(sA), F::kSbo, F::kLayout);
       uint32_t gk0 = 0, tcount = 0;
       for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x, ++tcount) {
         const GemmTile t = gemm_tile(a, &amap, &bmap, i);
-        const uint32_t idesc = idesc_f16(t.n_mma), ksteps = t.N / kGK;
+        const uint32_t idesc = idesc_f16(t.n_mma), ksteps = t.N / F::kStageK;  // operand stages of the tile
         // the epilogue has read the previous tile's accumulators
         if (tcount > 0) {
           if (!mbar_wait(&acc_empty, (tcount - 1) & 1u, spin)) {
@@ -398,7 +404,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
             tc_fence_after();
             const uint32_t first = ks0 + s == 0;
 #pragma unroll
-            for (uint32_t kk = 0; kk < kGK / 16; ++kk) {
+            for (uint32_t kk = 0; kk < F::kStageK / 16; ++kk) {
               const uint64_t bd = db + (s * F::kBBytes + 32 * kk) / 16;
               const uint32_t acc = kk != 0 || !first;
 #pragma unroll
@@ -407,7 +413,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
                   umma_f16_ts(tmem + hb * F::kAccCols,
                               tmem + F::kACol + s * F::kAStageCols + hb * (kGK / 2) + kk * 8, bd, idesc, acc);
                 else
-                  umma_f16(tmem + hb * F::kAccCols, da + (s * F::kABytes + hb * kGASub + 32 * kk) / 16, bd, idesc,
+                  umma_f16(tmem + hb * F::kAccCols, da + (s * F::kABytes + hb * F::kASub + 32 * kk) / 16, bd, idesc,
                            acc);
               }
             }
@@ -437,7 +443,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     // arrive as zeros; their accumulator rows are never stored.  Waits are
     // warp-uniform (a vote), as the tensor-memory accesses are warp-wide.
     const uint32_t e = warp - 2, grp = e >> 3, q = warp & 3u, blk = (e >> 2) & 1u;
-    const uint32_t rb = 32 * q + lane, r = blk * kGMmaM + rb, sw = rb & 7u;  // 128-byte swizzle: chunk ^ row%8
+    const uint32_t rb = 32 * q + lane, r = blk * kGMmaM + rb;
     uint32_t gk0 = 0, gsb0 = 0, tcount = 0;
     for (uint32_t i = blockIdx.x; i < n_tiles && !failed; i += gridDim.x, ++tcount) {
       const GemmTile t = gemm_tile(a, &amap, &bmap, i);
@@ -456,26 +462,43 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
           if (lane == 0) mbar_arrive(&raw_empty[rs]);
         }
         const RowChunks ch = dequant_group(g, j);
-        const uint32_t gk = gk0 + ks, s = gk % F::kStages, use = gk / F::kStages;
-        if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty_bar[s], (use - 1) & 1u, spin))) {
-          failed = true;
-          break;
-        }
         if constexpr (kTA) {
+          const uint32_t gk = gk0 + ks, s = gk % F::kStages, use = gk / F::kStages;
+          if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty_bar[s], (use - 1) & 1u, spin))) {
+            failed = true;
+            break;
+          }
           tc_fence_after();  // the MMAs that read this stage have completed
           tmem_st32(tmem + ((32u * q) << 16) + F::kACol + s * F::kAStageCols + blk * (kGK / 2), ch.c);
           tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full_a[s]);
         } else {
-          uint8_t* dst = sA + s * F::kABytes + blk * kGASub + rb * 128;
+          // the step's two K = 32 stages: low nibbles (chunks 0-3) and high
+          // (chunks 4-7), 64-byte rows, 16-byte chunk c at c ^ ((row / 2) % 4)
+          const uint32_t h = 2 * (gk0 + ks), s = h % F::kStages, use = h / F::kStages;
+          if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty_bar[s], (use - 1) & 1u, spin) &&
+                                                      mbar_wait(&empty_bar[s + 1], (use - 1) & 1u, spin))) {
+            failed = true;
+            break;
+          }
+          const uint32_t sw64 = (rb >> 1) & 3u;
 #pragma unroll
-          for (uint32_t c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw) << 4)) = ch.c[c];
+          for (uint32_t hh = 0; hh < 2; ++hh) {
+            uint8_t* dst = sA + (s + hh) * F::kABytes + blk * F::kASub + rb * F::kRowBytes;
+#pragma unroll
+            for (uint32_t c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + ((c ^ sw64) << 4)) = ch.c[4 * hh + c];
+          }
           fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&full_a[s]);
+            mbar_arrive(&full_a[s + 1]);
+          }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full_a[s]);
       }
       if (failed) break;
-      gk0 += ksteps;
+      gk0 += ksteps;  // 64-wide K steps
       gsb0 += ksteps >> 2;
       // epilogue: producer warp e reads accumulator blk (rows 128 blk ..) in
       // its tensor-memory lane quarter w % 4, the 32-column chunks of parity
@@ -656,6 +679,21 @@ cudaError_t launch_gemm_kernel(const CUtensorMap& bmap, const CUtensorMap& amap,
                                                   : launch_form<false>(grid, bmap, amap, ga, device, s);
 }
 
+// The B operand's tensor map for tiles of `box_rows` operand rows: K = 64
+// boxes in the 128-byte swizzle (TS form) or K = 32 in the 64-byte swizzle
+// (SS form), matching the form's shared-memory stages.
+CUresult encode_operand_map(EncodeTiledFn enc, CUtensorMap* map, const void* operand, uint32_t N, uint32_t rows,
+                            uint32_t box_rows) {
+  const bool ts = box_rows <= kGMaxTsRows;
+  const cuuint64_t dims[2] = {N, rows};
+  const cuuint64_t strides[1] = {2ull * N};
+  const cuuint32_t box[2] = {ts ? GemmForm<true>::kStageK : GemmForm<false>::kStageK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(operand), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, ts ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
 }  // namespace
 
 int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t M, uint32_t N, uint32_t T,
@@ -703,13 +741,7 @@ int run_gemm(q4k_ctx* ctx, const uint8_t* w, const float* x, float* y, uint32_t 
     // a batch that fits one TS tile runs as one
     if (tile == full && gemm_tile_tokens(parts, tc) * parts <= kGMaxTsRows) tile = gemm_tile_tokens(parts, tc);
     CUtensorMap bmap;
-    const cuuint64_t dims[2] = {N, (cuuint64_t)parts * tc};
-    const cuuint64_t strides[1] = {2ull * N};
-    const cuuint32_t box[2] = {kGK, parts * tile};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bbuf, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    if (encode_operand_map(enc, &bmap, bbuf, N, parts * tc, parts * tile) != CUDA_SUCCESS)
       return ctx_fail(ctx, Q4K_ERR_CUDA, "q4k_gemm activation tensor map");
     GemmArgs ga;
     ga.w = w;
@@ -760,13 +792,7 @@ cudaError_t gemm_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_
 cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, uint32_t T, uint32_t parts) {
   EncodeTiledFn enc = gemm_encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  const cuuint64_t dims[2] = {N, (cuuint64_t)parts * T};
-  const cuuint64_t strides[1] = {2ull * N};
-  const cuuint32_t box[2] = {kGK, parts * gemm_tile_tokens(parts, T)};
-  const cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(operand), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+  return encode_operand_map(enc, map, operand, N, parts * T, parts * gemm_tile_tokens(parts, T)) == CUDA_SUCCESS
              ? cudaSuccess
              : cudaErrorInvalidValue;
 }
