@@ -100,7 +100,10 @@ uint32_t gemm_tile_rows();
 size_t gemm_operand_bytes(uint32_t N, uint32_t T, uint32_t parts);
 cudaError_t gemm_weight_map(CUtensorMap* map, const void* w, uint32_t M, uint32_t N);
 cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, uint32_t T, uint32_t parts);
-cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, cudaStream_t s);
+// One CTA per (job, token); `max_n` = the widest job, `aligned` = every
+// pointer of every job 16-byte aligned (then each input is read once).
+cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, uint32_t max_n,
+                             bool aligned, int device, cudaStream_t s);
 cudaError_t launch_gemm_tasks(const GemmTask* tasks, const uint2* tiles, uint32_t n_tiles, uint32_t parts,
                               uint32_t tile_tokens, uint32_t sms, int device, uint32_t* status, uint32_t spin,
                               cudaStream_t s);

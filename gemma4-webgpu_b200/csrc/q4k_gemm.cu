@@ -646,7 +646,66 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const GemmJob* jobs, uin
   }
 }
 
+// The same with the token's row staged in shared memory (N floats), so the
+// inputs are read once: 16-byte loads of x, or of gate and up (gelu_mul
+// computed once and stored to act on the way), the row's max |value|, then
+// each 8-element chunk scaled and written as one 16-byte store per operand
+// row.  Every pointer of every job is 16-byte aligned (checked by the host).
+__global__ void __launch_bounds__(256) gemm_prep_row_kernel(const GemmJob* jobs, uint32_t T, uint32_t parts) {
+  extern __shared__ float4 s_row4[];
+  __shared__ float s_red[8];
+  const GemmJob J = jobs[blockIdx.x / T];
+  const uint32_t t = blockIdx.x % T, n4 = J.N / 4;
+  const size_t base4 = (size_t)t * n4;
+  float mx = 0.0f;
+  for (uint32_t k = threadIdx.x; k < n4; k += blockDim.x) {
+    float4 v;
+    if (J.mode) {
+      const float4 g = reinterpret_cast<const float4*>(J.gate)[base4 + k];
+      const float4 u = reinterpret_cast<const float4*>(J.up)[base4 + k];
+      v = make_float4(gelu_mul_value(g.x, u.x), gelu_mul_value(g.y, u.y), gelu_mul_value(g.z, u.z),
+                      gelu_mul_value(g.w, u.w));
+      if (J.act) reinterpret_cast<float4*>(J.act)[base4 + k] = v;
+    } else {
+      v = reinterpret_cast<const float4*>(J.x)[base4 + k];
+    }
+    s_row4[k] = v;
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = s_red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, s_red[i]);
+  int e = 0, sexp = 0;
+  if (mx > 0.0f && mx <= 3.402823466e38f) {
+    frexpf(mx, &e);
+    sexp = 15 - e;
+    sexp = sexp > 100 ? 100 : (sexp < -100 ? -100 : sexp);
+  }
+  const float sc = ldexpf(1.0f, sexp);
+  if (threadIdx.x == 0) J.inv_scale[t] = ldexpf(1.0f, -sexp);
+  const float* s_row = reinterpret_cast<const float*>(s_row4);
+  __half* const op = static_cast<__half*>(J.operand) + (size_t)(parts * t) * J.N;
+  for (uint32_t c = threadIdx.x; c < J.N / 8; c += blockDim.x) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (uint32_t q = 0; q < 4; ++q) {
+      // positions 2q, 2q+1 of the chunk in the A tiles' K order
+      const float v0 = s_row[8 * c + chunk_elem(2 * q)] * sc, v1 = s_row[8 * c + chunk_elem(2 * q + 1)] * sc;
+      const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+      h[q] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      const __half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+      l[q] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    reinterpret_cast<uint4*>(op)[c] = make_uint4(h[0], h[1], h[2], h[3]);
+    if (parts == 2) reinterpret_cast<uint4*>(op + J.N)[c] = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 using EncodeTiledFn = decltype(&cuTensorMapEncodeTiled);
+
+constexpr size_t kGemmPrepRowMax = 96 * 1024;  // widest row the single-read preparation stages in shared memory
 
 EncodeTiledFn gemm_encode_fn() {
   static EncodeTiledFn fn = []() -> EncodeTiledFn {
@@ -797,9 +856,18 @@ cudaError_t gemm_operand_map(CUtensorMap* map, const void* operand, uint32_t N, 
              : cudaErrorInvalidValue;
 }
 
-cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, cudaStream_t s) {
+cudaError_t launch_gemm_prep(const GemmJob* jobs, uint32_t n_jobs, uint32_t T, uint32_t parts, uint32_t max_n,
+                             bool aligned, int device, cudaStream_t s) {
   if (n_jobs == 0) return cudaSuccess;
-  gemm_prep_kernel<<<n_jobs * T, 256, 0, s>>>(jobs, T, parts);
+  const size_t row_bytes = 4ull * max_n;
+  if (aligned && row_bytes <= kGemmPrepRowMax) {
+    static std::atomic<uint8_t> attr_set[kAttrDevices];
+    const cudaError_t e = smem_attr_once(attr_set, device, gemm_prep_row_kernel, (int)kGemmPrepRowMax);
+    if (e != cudaSuccess) return e;
+    gemm_prep_row_kernel<<<n_jobs * T, 256, row_bytes, s>>>(jobs, T, parts);
+  } else {
+    gemm_prep_kernel<<<n_jobs * T, 256, 0, s>>>(jobs, T, parts);
+  }
   return cudaGetLastError();
 }
 

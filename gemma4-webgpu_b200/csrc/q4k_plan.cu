@@ -70,6 +70,8 @@ struct Stage {
   GemmTask* gtasks_dev = nullptr;
   uint2* tiles_dev = nullptr;
   uint32_t n_gjobs = 0, n_tiles = 0;
+  uint32_t gjob_max_n = 0;      // widest activation job of the stage
+  bool gjobs_aligned = false;   // every job pointer 16-byte aligned (single-read preparation)
 };
 
 // Commit splits each recorded stage into launch units of one weight format
@@ -526,6 +528,12 @@ static int commit_gemm(q4k_plan* p) {
       ocur += align_up(4ull * T, 256);
       e = gemm_operand_map(&maps[st.n_tasks + j], J.operand, k.N, T, parts);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit activation tensor map");
+      st.gjob_max_n = st.gjob_max_n > k.N ? st.gjob_max_n : k.N;
+      const uintptr_t bits = reinterpret_cast<uintptr_t>(J.x) | reinterpret_cast<uintptr_t>(J.gate) |
+                             reinterpret_cast<uintptr_t>(J.up) | reinterpret_cast<uintptr_t>(J.act) |
+                             reinterpret_cast<uintptr_t>(J.operand);
+      if (j == 0) st.gjobs_aligned = true;
+      st.gjobs_aligned = st.gjobs_aligned && (bits & 15u) == 0;
     }
     std::vector<GemmTask> tasks(st.n_tasks);
     std::vector<uint2> tiles;
@@ -571,7 +579,8 @@ int q4k_plan_run(q4k_plan* p, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p->gemm) {
     for (const Stage& st : p->stages) {
-      cudaError_t e = launch_gemm_prep(st.gjobs_dev, st.n_gjobs, p->batch, p->parts, s);
+      cudaError_t e = launch_gemm_prep(st.gjobs_dev, st.n_gjobs, p->batch, p->parts, st.gjob_max_n,
+                                       st.gjobs_aligned, ctx->device, s);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_run GEMM activation prep launch");
       e = launch_gemm_tasks(st.gtasks_dev, st.tiles_dev, st.n_tiles, p->parts, gemm_tile_tokens(p->parts, p->batch),
                             (uint32_t)ctx->sm_count, ctx->device, ctx->select.status, ctx->select.spin_limit, s);
