@@ -75,12 +75,15 @@ struct alignas(16) GemmTask {
   const CUtensorMap* bmap;  // its activation operand (gemm_operand_map), device memory
   float* y;                 // [T][M]
   const float* inv_scale;   // [T]: 1/scale of each activation row (the operand's)
-  uint32_t M, N, T;
+  uint32_t M, N, T;         // N: the K range of this task (k0 .. k0 + N)
   uint32_t tile_tokens;     // activation rows per tile (gemm_tile_tokens)
+  uint32_t k0;              // first K element of the range (a multiple of 256)
+  uint32_t accumulate;      // 1: add into y (zeroed by the stage's preparation), one of a K split
 };
 
 // One activation operand: mode 0 from x [T][N]; mode 1 gelu_mul(gate, up)
-// [T][N] (shaders/gelu_mul.wgsl), stored to act when act != null.
+// [T][N] (shaders/gelu_mul.wgsl), stored to act when act != null.  Mode 2
+// has no operand: it zeroes act [T][N], the output of a K-split matrix.
 struct alignas(16) GemmJob {
   const float* x;
   const float* gate;

@@ -243,6 +243,7 @@ struct GemmTile {
   float* y;
   const float* inv_scale;
   uint32_t M, N, T, tile_tokens, row0, tok0, n_mma;
+  uint32_t k0, acc;  // K range start; 1: add into y (K split)
 };
 
 __device__ __forceinline__ GemmTile gemm_tile(const GemmArgs& a, const CUtensorMap* amap, const CUtensorMap* bmap,
@@ -261,6 +262,8 @@ __device__ __forceinline__ GemmTile gemm_tile(const GemmArgs& a, const CUtensorM
     t.tile_tokens = tk.tile_tokens;
     t.row0 = (tl.y & 0xffffu) * kGRows;
     t.tok0 = (tl.y >> 16) * t.tile_tokens;
+    t.k0 = tk.k0;
+    t.acc = tk.accumulate;
   } else {
     const uint32_t row_tiles = (a.M + kGRows - 1) / kGRows;
     t.amap = amap;
@@ -273,6 +276,8 @@ __device__ __forceinline__ GemmTile gemm_tile(const GemmArgs& a, const CUtensorM
     t.tile_tokens = a.tile_tokens;
     t.row0 = (i % row_tiles) * kGRows;
     t.tok0 = (i / row_tiles) * a.tile_tokens;
+    t.k0 = 0;
+    t.acc = 0;
   }
   // MMA N: the tile's operand rows, a multiple of 16
   const uint32_t ntok = min(t.tile_tokens, t.T - t.tok0);
@@ -344,7 +349,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
             break;
           }
           mbar_arrive_expect_tx(&full_b[s], b_bytes);
-          tma_tile_g2s(sB + s * F::kBBytes, t.bmap, ks * F::kStageK, a.parts * t.tok0, &full_b[s]);
+          tma_tile_g2s(sB + s * F::kBBytes, t.bmap, t.k0 + ks * F::kStageK, a.parts * t.tok0, &full_b[s]);
         }
       }
       // every issued copy has landed before the CTA can exit
@@ -529,13 +534,20 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
 #pragma unroll
           for (uint32_t u = 0; u < 16; ++u) {
             const float sc = __shfl_sync(0xffffffffu, my_scale, u);
-            if (tl0 + u < ntok && erow < t.M) ycol[(size_t)u * t.M] = (v[2 * u] + v[2 * u + 1]) * sc;
+            if (tl0 + u < ntok && erow < t.M) {
+              const float r = (v[2 * u] + v[2 * u + 1]) * sc;
+              if (t.acc) atomicAdd(ycol + (size_t)u * t.M, r);
+              else ycol[(size_t)u * t.M] = r;
+            }
           }
         } else {
 #pragma unroll
           for (uint32_t u = 0; u < 32; ++u) {
             const float sc = __shfl_sync(0xffffffffu, my_scale, u);
-            if (tl0 + u < ntok && erow < t.M) ycol[(size_t)u * t.M] = v[u] * sc;
+            if (tl0 + u < ntok && erow < t.M) {
+              if (t.acc) atomicAdd(ycol + (size_t)u * t.M, v[u] * sc);
+              else ycol[(size_t)u * t.M] = v[u] * sc;
+            }
           }
         }
       }
@@ -559,7 +571,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
           break;
         }
         mbar_arrive_expect_tx(&raw_full[rs], kGRawBytes);
-        tma_tile_g2s(sRaw + rs * kGRawBytes, t.amap, sb * (kBlockBytes / 4), t.row0, &raw_full[rs]);
+        tma_tile_g2s(sRaw + rs * kGRawBytes, t.amap, (t.k0 / 256 + sb) * (kBlockBytes / 4), t.row0, &raw_full[rs]);
       }
     }
     // every issued copy has landed before the CTA can exit
@@ -615,8 +627,12 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const GemmJob* jobs, uin
   __shared__ float s_red[8];
   const GemmJob J = jobs[blockIdx.x / T];
   const uint32_t t = blockIdx.x % T, N = J.N;
+  if (J.mode == 2) {  // a K-split output row, to be accumulated into
+    for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) J.act[(size_t)t * N + k] = 0.0f;
+    return;
+  }
   const size_t base = (size_t)t * N;
-  auto value = [&](size_t i) { return J.mode ? gelu_mul_value(J.gate[i], J.up[i]) : J.x[i]; };
+  auto value = [&](size_t i) { return J.mode ? gelu_mul_value(J.gate[i], J.up[i]) : J.x[i]; };  // modes 0, 1
   float mx = 0.0f;
   for (uint32_t k = threadIdx.x; k < N; k += blockDim.x) {
     const float v = value(base + k);
@@ -657,6 +673,10 @@ __global__ void __launch_bounds__(256) gemm_prep_row_kernel(const GemmJob* jobs,
   const GemmJob J = jobs[blockIdx.x / T];
   const uint32_t t = blockIdx.x % T, n4 = J.N / 4;
   const size_t base4 = (size_t)t * n4;
+  if (J.mode == 2) {  // a K-split output row, to be accumulated into
+    for (uint32_t k = threadIdx.x; k < J.N; k += blockDim.x) J.act[(size_t)t * J.N + k] = 0.0f;
+    return;
+  }
   float mx = 0.0f;
   for (uint32_t k = threadIdx.x; k < n4; k += blockDim.x) {
     float4 v;

@@ -71,6 +71,8 @@ struct Stage {
   uint2* tiles_dev = nullptr;
   uint32_t n_gjobs = 0, n_tiles = 0;
   uint32_t gjob_max_n = 0;      // widest activation job of the stage
+  uint32_t gsplit = 1;          // K split of every matrix of the stage (1 or 2)
+  uint32_t n_gkeys = 0;         // activation jobs; the K-split zeroing jobs follow them
   bool gjobs_aligned = false;   // every job pointer 16-byte aligned (single-read preparation)
 };
 
@@ -481,8 +483,25 @@ static int commit_gemm(q4k_plan* p) {
       for (const Key& k : keys[s]) used |= (k.gelu == (int)g);
       if (!used) keys[s].push_back({st.gelus[g].act, st.gelus[g].n, (int)g});
     }
-    st.n_tasks = (uint32_t)st.gemvs.size();
-    st.n_gjobs = (uint32_t)keys[s].size();
+    // A stage of long-K matrices that fills less than whole rounds of the
+    // SMs (the downs at small T: 210 tiles of 96 K steps on 148 SMs) runs
+    // each matrix as two K halves accumulating into its zeroed output.  The
+    // output is then 0 + a + b in either order, which fp32 gives exactly.
+    {
+      bool can = !st.gemvs.empty();
+      uint32_t steps = 0;
+      for (const PlanGemv& g : st.gemvs) {
+        can = can && g.N % 512 == 0 && g.N >= 2048;
+        steps = steps > g.N / 64 ? steps : g.N / 64;
+      }
+      const uint32_t sms = (uint32_t)(ctx->sm_count > 0 ? ctx->sm_count : 1);
+      auto rounds = [&](uint32_t n) { return (n + sms - 1) / sms; };
+      st.gsplit = can && rounds(2 * st.n_tiles) * (steps / 2) < rounds(st.n_tiles) * steps ? 2 : 1;
+    }
+    st.n_tiles *= st.gsplit;
+    st.n_tasks = (uint32_t)st.gemvs.size() * st.gsplit;
+    st.n_gkeys = (uint32_t)keys[s].size();
+    st.n_gjobs = st.n_gkeys + (st.gsplit > 1 ? (uint32_t)st.gemvs.size() : 0u);
     desc += align_up(sizeof(GemmTask) * st.n_tasks, 256) + align_up(sizeof(GemmJob) * st.n_gjobs, 256) +
             align_up(sizeof(CUtensorMap) * (st.n_tasks + st.n_gjobs), 256) + align_up(sizeof(uint2) * st.n_tiles, 256);
     for (const Key& k : keys[s]) ops += align_up(gemm_operand_bytes(k.N, T, parts), 256) + align_up(4ull * T, 256);
@@ -508,7 +527,7 @@ static int commit_gemm(q4k_plan* p) {
     cur += align_up(sizeof(uint2) * st.n_tiles, 256);
     std::vector<CUtensorMap> maps(st.n_tasks + st.n_gjobs);
     std::vector<GemmJob> jobs(st.n_gjobs);
-    for (uint32_t j = 0; j < st.n_gjobs; ++j) {
+    for (uint32_t j = 0; j < st.n_gkeys; ++j) {
       const Key& k = keys[s][j];
       GemmJob& J = jobs[j];
       J = GemmJob{};
@@ -535,21 +554,32 @@ static int commit_gemm(q4k_plan* p) {
       if (j == 0) st.gjobs_aligned = true;
       st.gjobs_aligned = st.gjobs_aligned && (bits & 15u) == 0;
     }
+    // the K-split zeroing jobs: one per matrix output
+    for (uint32_t i = 0; st.gsplit > 1 && i < st.gemvs.size(); ++i) {
+      GemmJob& J = jobs[st.n_gkeys + i];
+      J = GemmJob{};
+      J.mode = 2;
+      J.act = st.gemvs[i].y;
+      J.N = st.gemvs[i].M;
+    }
     std::vector<GemmTask> tasks(st.n_tasks);
     std::vector<uint2> tiles;
     tiles.reserve(st.n_tiles);
     for (uint32_t i = 0; i < st.n_tasks; ++i) {
-      const PlanGemv& g = st.gemvs[i];
-      const uint32_t j = task_job[s][i];
+      const PlanGemv& g = st.gemvs[i / st.gsplit];
+      const uint32_t j = task_job[s][i / st.gsplit], h = i % st.gsplit;
       e = gemm_weight_map(&maps[i], g.w, g.M, g.N);
       if (e != cudaSuccess) return ctx_cuda(ctx, e, "q4k_plan_commit weight tensor map");
       GemmTask& t = tasks[i];
+      t = GemmTask{};
       t.amap = maps_dev + i;
       t.bmap = maps_dev + st.n_tasks + j;
       t.y = g.y;
       t.inv_scale = jobs[j].inv_scale;
       t.M = g.M;
-      t.N = g.N;
+      t.N = g.N / st.gsplit;
+      t.k0 = h * t.N;
+      t.accumulate = st.gsplit > 1;
       t.T = T;
       t.tile_tokens = tt;
       for (uint32_t r = 0; r < (g.M + tr - 1) / tr; ++r)
