@@ -185,3 +185,25 @@ def test_gemm_plan_one_launch_per_stage_matches_oracle(ctx, oracle, T, exact):
     ctx.check()
     for key, t in bs.out.items():
         assert torch.equal(t.view(torch.int32), first[key].view(torch.int32)), key
+
+
+
+def test_gemm_plan_wide_rows_take_the_two_pass_preparation(ctx, oracle):
+    """A GEMM plan whose activation rows are wider than the single-read
+    preparation stages in shared memory (N > 24576 floats) prepares them in
+    two passes over global memory instead; the result still matches the
+    oracle on the f16-rounded activations within the GEMV tolerance."""
+    from q4k import Plan
+
+    T, M, N = 64, 256, 97 * 256
+    w = synth.q4k_matrix(M, N, synth.seed_for(4, 97))
+    x = synth.activations(T, N, synth.seed_for(4, 98))
+    y = torch.zeros(T * M, dtype=torch.float32, device=DEV)
+    p = Plan(ctx, T)
+    p.gemv(0, to_dev(w), to_dev(x), y, M, N)
+    p.commit()
+    p.run()
+    torch.cuda.synchronize()
+    ctx.check()
+    check(oracle, y.cpu().numpy().reshape(T, M), w, f16_rounded(x), M, N)
+    p.close()
