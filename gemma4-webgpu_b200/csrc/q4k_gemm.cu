@@ -6,31 +6,32 @@
 // 168-210 + 425-473).
 //
 // Here the work is a dense contraction, so it runs on the 5th-generation
-// tensor cores: one CTA computes a 256-row x 128-activation-row tile of Y
-// (64 activation rows when 128-row tiles would leave SMs idle) as two
-// 128-row blocks, each with tcgen05.mma (M = 128, N = 2 x activation rows,
-// K = 16 per instruction) into its own fp32 accumulator in tensor memory
-// (2 x 256 columns); both blocks read the same B tile, so the activation
-// operand is fetched once per 256 weight rows.  Per 64-wide K step:
-//   * the B operand, x split exactly into f16 hi + lo parts (two operand rows
-//     per activation row, scaled per row by a power of two), arrives by TMA
-//     tensor copies in a swizzled K-major layout (two K = 32 stages);
+// tensor cores.  A tile of Y is 256 weight rows x up to 256 operand rows (one
+// operand row per activation row in the f16 form, two -- the exact f16 hi
+// and lo parts, scaled per row by a power of two -- in the exact form),
+// computed as two 128-row blocks, each with tcgen05.mma (M = 128, N = the
+// tile's operand rows, K = 16 per instruction) into its own fp32
+// accumulator in tensor memory; both blocks read the same B tile, so the
+// activation operand is fetched once per 256 weight rows.  The launch is
+// persistent: one CTA per SM walks its tiles, every role keeping its ring
+// counters from tile to tile.  Per 64-wide K step:
+//   * the B operand arrives by TMA tensor copies in a swizzled K-major
+//     layout;
 //   * the A operand, the 256 x 64 f16 weights, is dequantized by 16 warps
-//     (two groups of 8, one per K-step parity, each filling its own stages)
-//     into the same swizzled layout, computed before the stages are free and
-//     stored once they are; the raw Q4_K super-blocks reach shared memory by
-//     TMA, one 144-byte box per tile row per super-block column (four K
-//     steps), two columns in flight (a copy warp of its own);
-//   * one thread issues the 8 MMAs and commits them to the stage's "empty"
+//     (two groups of 8, one per K-step parity), computed before its stage is
+//     free and stored once it is; the raw Q4_K super-blocks reach shared
+//     memory by TMA, one 144-byte box per tile row per super-block column
+//     (four K steps), from a copy warp of its own;
+//   * one thread issues the MMAs and commits them to the stage's "empty"
 //     barrier, which frees the stage for the producers; it waits on one
 //     barrier per step, the producers' plus a relay arrival once B landed.
-// Four K = 32 operand stages are in flight.  Tiles of at most 128 operand rows (a
-// batch of up to 128 f16 or 64 exact activation rows) run the TS form
-// instead (GemmForm below): the weights go straight into tensor memory, four
-// stages in flight.  The epilogue (the 16 producer warps: per
-// accumulator one per 32-lane quarter of tensor memory and column half) reads
-// the accumulators, adds each activation
-// row's hi and lo columns, undoes the scale and stores Y.  f16 x f16
+// Two forms (GemmForm below): SS, A in shared memory, four K = 32 stages;
+// TS, for tiles of at most 128 operand rows (a batch of up to 128 f16 or 64
+// exact activation rows), A stored straight into tensor memory, four K = 64
+// stages.  The epilogue (the 16 producer warps: per accumulator one per
+// 32-lane quarter of tensor memory and column half) reads the accumulators,
+// adds each activation row's hi and lo columns, undoes the scale and stores
+// Y (or adds into it, for the two K halves of a split matrix).  f16 x f16
 // products are exact and the hi/lo split carries x to ~2^-22, so the result
 // is the f32 dot product of the reference's f16 weights with x, up to fp32
 // accumulation order.
